@@ -1,0 +1,345 @@
+// pointwise.cu -- persistent, warp-specialised tcgen05 (kind::i8) kernel for
+// the MFFT pointwise step; see pointwise.cuh for the job semantics.
+//
+// One CTA per SM.  Warp 0 streams K-major int8 tiles of Ahat and F into a
+// 4-stage shared-memory ring with TMA (128-byte swizzle, no multicast).  One
+// thread of warp 1 issues tcgen05.mma (M=128, N=block_n, K=32 per
+// instruction) into one of two 256-column int32 TMEM accumulators.  Warps 2-5
+// drain the other accumulator (tcgen05.ld) and store int32 rows to HBM while
+// the next tile accumulates.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstring>
+
+#include "ptx.cuh"
+#include "pointwise.cuh"
+#include "runtime.h"
+
+namespace mfftb {
+
+__device__ __forceinline__ void pw_tile_decode(const PwParams& p, long long tile, int& q, int& mt,
+                                               int& nt) {
+    long long per_job = (long long)p.tiles_m * p.tiles_n;
+    q = (int)(tile / per_job);
+    int r = (int)(tile % per_job);
+    int group = PW_GROUP_M * p.tiles_n;
+    int g = r / group;
+    int first_m = g * PW_GROUP_M;
+    int gm = p.tiles_m - first_m < PW_GROUP_M ? p.tiles_m - first_m : PW_GROUP_M;
+    int local = r % group;
+    mt = first_m + local % gm;
+    nt = local / gm;
+}
+
+__global__ void __launch_bounds__(PW_THREADS, 1)
+    pointwise_i8_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmF, const PwParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + PW_STAGES * PW_A_STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + PW_STAGES * PW_B_STAGE_BYTES);
+    // bars[0..S): full, [S..2S): empty, [2S..2S+2): tmem full, [2S+2..2S+4): tmem empty,
+    // [2S+4]: drain
+    const uint32_t bar_full = smem_u32(bars);
+    const uint32_t bar_empty = smem_u32(bars + PW_STAGES);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * PW_STAGES);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * PW_STAGES + 2);
+    const uint32_t bar_drain = smem_u32(bars + 2 * PW_STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PW_STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PW_STAGES; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar_tfull + 8 * a, 1);
+            mbar_init(bar_tempty + 8 * a, 128);
+        }
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmF);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), PW_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const unsigned long long tmo = p.timeout_ns;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------ TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[PW_STAGES];
+        for (int s = 0; s < PW_STAGES; ++s) issued_parity[s] = -1;
+        const uint32_t tx_bytes = PW_A_STAGE_BYTES + p.block_n * PW_BK;
+        for (long long tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            for (int s = s0; s < s1; ++s) {
+                int pa, pf;
+                pw_segment_planes(p.jobs, j, t, w, s, pa, pf);
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                                           global_timer_ns() + tmo))
+                        goto producer_done;
+                    mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                    tma_load_3d(smem_u32(sA + stage * PW_A_STAGE_BYTES), &tmA, bar_full + 8 * stage,
+                                kb * PW_BK, mt * PW_BM, pa);
+                    tma_load_3d(smem_u32(sB + stage * PW_B_STAGE_BYTES), &tmF, bar_full + 8 * stage,
+                                kb * PW_BK, nt * p.block_n, pf);
+                    issued_parity[stage] = (int)phase;
+                    if (++stage == PW_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    producer_done:
+        // Every TMA load this thread issued must have landed before the CTA
+        // may exit (its shared memory is the destination).
+        for (int s = 0; s < PW_STAGES; ++s)
+            if (issued_parity[s] >= 0)
+                if (!mbar_wait_deadline(bar_full + 8 * s, (uint32_t)issued_parity[s],
+                                        global_timer_ns() + tmo))
+                    *abort_flag = 1;
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------ MMA issuer
+        const uint32_t idesc = idesc_i8(PW_BM, p.block_n);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            const int nsteps = (s1 - s0) * p.kblocks;
+            if (!mbar_wait_bounded(bar_tempty + 8 * acc, acc_phase ^ 1, abort_flag,
+                                   global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+            for (int it = 0; it < nsteps; ++it) {
+                if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                       global_timer_ns() + tmo))
+                    goto mma_done;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + stage * PW_A_STAGE_BYTES);
+                const uint32_t b0 = smem_u32(sB + stage * PW_B_STAGE_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < PW_BK / 32; ++kk) {
+                    mma_i8(d_tmem, sdesc_kmajor_sw128(a0 + kk * 32), sdesc_kmajor_sw128(b0 + kk * 32),
+                           idesc, (it | kk) != 0 ? 1u : 0u);
+                }
+                mma_commit(bar_empty + 8 * stage);
+                if (++stage == PW_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit(bar_tfull + 8 * acc);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    mma_done:
+        // all MMAs issued by this thread complete before TMEM is released
+        mma_commit(bar_drain);
+        if (!mbar_wait_deadline(bar_drain, 0, global_timer_ns() + tmo)) *abort_flag = 1;
+    } else if (warp >= 2) {
+        // ------------------------------------------------------ epilogue
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            if (!mbar_wait_bounded(bar_tfull + 8 * acc, acc_phase, abort_flag,
+                                   global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const bool empty_job = (s1 <= s0);
+            const int row = mt * PW_BM + quarter * 32 + lane;
+            const int col0 = nt * p.block_n;
+            int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
+            const int colmax = p.cols - col0;
+            for (int c = 0; c < p.block_n / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                       (uint32_t)(acc * 256 + c * 32),
+                                   v);
+                tmem_ld_wait();
+                if (row < p.rows) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        const int col = c * 32 + e;
+                        if (col < colmax) {
+                            int4 o;
+                            o.x = empty_job ? 0 : (int)v[e];
+                            o.y = empty_job ? 0 : (int)v[e + 1];
+                            o.z = empty_job ? 0 : (int)v[e + 2];
+                            o.w = empty_job ? 0 : (int)v[e + 3];
+                            *reinterpret_cast<int4*>(orow + col) = o;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(bar_tempty + 8 * acc);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicCAS(p.err, 0, MFFTB_ERR_TIMEOUT);
+    if (warp == 1) tmem_dealloc(tmem_base, PW_TMEM_COLS);
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) !=
+                cudaSuccess ||
+            qr != cudaDriverEntryPointSuccess)
+            return nullptr;
+        fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+// 3-D int8 tensor [planes][rows][kdim] with row stride ld bytes and plane
+// stride plane_bytes; box = box_rows x 128 bytes of one plane, 128B swizzle.
+static int make_map(CUtensorMap* m, const void* base, int kdim, int rows, int planes, long long ld,
+                    long long plane_bytes, int box_rows) {
+    auto enc = get_encode_fn();
+    if (!enc) return MFFTB_ERR_CUDA;
+    cuuint64_t dims[3] = {(cuuint64_t)kdim, (cuuint64_t)rows, (cuuint64_t)planes};
+    cuuint64_t strides[2] = {(cuuint64_t)ld, (cuuint64_t)plane_bytes};
+    cuuint32_t box[3] = {(cuuint32_t)PW_BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
+    if (L.kdim <= 0 || L.rows <= 0 || L.cols <= 0) return MFFTB_ERR_ARG;
+    if ((L.lda % 16) || (L.ldf % 16) || (L.ldo % 4) || (L.a_plane_bytes % 16) ||
+        (L.f_plane_bytes % 16) || (L.cols % 16))
+        return MFFTB_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(L.A) % 16 || reinterpret_cast<uintptr_t>(L.F) % 16 ||
+        reinterpret_cast<uintptr_t>(L.out) % 16)
+        return MFFTB_ERR_ARG;
+    PwParams p;
+    p.jobs = L.jobs;
+    p.rows = L.rows;
+    p.cols = L.cols;
+    p.kdim = L.kdim;
+    p.kblocks = (L.kdim + PW_BK - 1) / PW_BK;
+    p.block_n = L.block_n;
+    if (p.block_n != 64 && p.block_n != 128 && p.block_n != 256) return MFFTB_ERR_ARG;
+    p.tiles_m = (L.rows + PW_BM - 1) / PW_BM;
+    p.tiles_n = (L.cols + p.block_n - 1) / p.block_n;
+    p.num_tiles = (long long)p.tiles_m * p.tiles_n * L.jobs.njobs;
+    p.out = L.out;
+    p.out_plane = L.out_plane;
+    p.ldo = L.ldo;
+    p.err = L.err;
+    p.timeout_ns = L.timeout_ns;
+
+    CUtensorMap tmA, tmF;
+    int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);
+    if (rc) return rc;
+    rc = make_map(&tmF, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, p.block_n);
+    if (rc) return rc;
+
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(pointwise_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PW_SMEM_BYTES) != cudaSuccess)
+            return MFFTB_ERR_CUDA;
+        attr_set = true;
+    }
+    long long grid = L.num_sms;
+    if (grid > p.num_tiles) grid = p.num_tiles;
+    if (grid <= 0) return MFFTB_OK;
+    pointwise_i8_kernel<<<(unsigned)grid, PW_THREADS, PW_SMEM_BYTES, stream>>>(tmA, tmF, p);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+}  // namespace mfftb
+
+// ---------------------------------------------------------------- checker
+// Plain CUDA-core evaluation of the same job table, one thread per output
+// element with an int64 accumulator.  Used only by the unit tests of the
+// tcgen05 kernel (never on the product path).
+namespace mfftb {
+
+__global__ void pointwise_simt_check_kernel(const int8_t* A, long long lda, long long a_plane,
+                                            const int8_t* F, long long ldf, long long f_plane,
+                                            int rows, int cols, int kdim, PwJobs J, int32_t* out,
+                                            long long out_plane, int ldo, int* mismatch,
+                                            long long* first_bad) {
+    long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    long long per_job = (long long)rows * cols;
+    if (idx >= per_job * J.njobs) return;
+    int q = (int)(idx / per_job);
+    int r = (int)((idx % per_job) / cols);
+    int c = (int)(idx % cols);
+    int j, t, w, ch, s0, s1;
+    pw_job_decode(J, q, j, t, w, ch);
+    pw_chunk_range(J, w, ch, s0, s1);
+    long long acc = 0;
+    for (int s = s0; s < s1; ++s) {
+        int pa, pf;
+        pw_segment_planes(J, j, t, w, s, pa, pf);
+        const int8_t* a = A + pa * a_plane + r * lda;
+        const int8_t* f = F + pf * f_plane + c * ldf;
+        for (int k = 0; k < kdim; ++k) acc += (long long)a[k] * (long long)f[k];
+    }
+    int32_t got = out[q * out_plane + (long long)r * ldo + c];
+    if ((long long)got != acc) {
+        if (atomicAdd(mismatch, 1) == 0) *first_bad = idx;
+    }
+}
+
+int pointwise_check_launch(const PwLaunch& L, int* d_mismatch, long long* d_first_bad,
+                           cudaStream_t stream) {
+    long long total = (long long)L.rows * L.cols * L.jobs.njobs;
+    int threads = 256;
+    long long blocks = (total + threads - 1) / threads;
+    pointwise_simt_check_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+        L.A, L.lda, L.a_plane_bytes, L.F, L.ldf, L.f_plane_bytes, L.rows, L.cols, L.kdim, L.jobs,
+        L.out, L.out_plane, L.ldo, d_mismatch, d_first_bad);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+}  // namespace mfftb

@@ -1,0 +1,102 @@
+// pointwise.cuh -- the MFFT pointwise step as one persistent tcgen05 kernel.
+//
+// Reference semantics (src/mfft.c:383-396, leaf src/kernel.c:160-191): for
+// every evaluation point j and output ring coefficient t,
+//
+//     Chat[j][t] = sum_{c1} sign(c1,t) * Ahat[j][c1] * Bhat[j][(t-c1) mod K]
+//
+// with sign -1 where c1 > t (the negacyclic wrap of Z[y]/(y^K+1)).  Here the
+// K plane products of one (j,t) are a single GEMM whose contraction is the
+// K operand planes laid end to end (length K*n).  The B operand of (j,t) is a
+// window of the "F" stack the forward transform writes for B:
+//
+//     F[r] = +Bhat[K-1-r]   for r <  K
+//     F[r] = -Bhat[2K-1-r]  for r >= K            (r = 0 .. 2K-2)
+//
+// so the B plane paired with Ahat[j][c1] is F[K-1-t+c1]: no sign handling
+// inside the kernel.  Transformed values wider than int8 are split into dA/dB
+// signed 7-bit digits; a job then also carries a digit-weight class
+// w = da + db, and its contraction runs over every (da, db) pair of that
+// class.  Long contractions are split into nchunk chunks so that the int32
+// TMEM accumulator provably cannot overflow (bounds are checked on the host
+// when the plan is built).
+#pragma once
+#include <cstdint>
+
+namespace mfftb {
+
+constexpr int PW_BM = 128;          // rows of a tile (MMA M)
+constexpr int PW_BK = 128;          // contraction bytes per pipeline stage
+constexpr int PW_STAGES = 4;        // smem pipeline depth
+constexpr int PW_MAX_BN = 256;      // widest tile (MMA N)
+constexpr int PW_THREADS = 192;     // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int PW_TMEM_COLS = 512;   // two accumulator buffers of up to 256 columns
+constexpr int PW_GROUP_M = 16;      // tile raster: 16 row-tiles per group for L2 reuse
+
+constexpr int PW_A_STAGE_BYTES = PW_BM * PW_BK;
+constexpr int PW_B_STAGE_BYTES = PW_MAX_BN * PW_BK;
+constexpr int PW_SMEM_BYTES =
+    1024 /*alignment slack*/ + PW_STAGES * (PW_A_STAGE_BYTES + PW_B_STAGE_BYTES) + 256;
+
+struct PwJobs {
+    int K;        // ring dimension
+    int dA, dB;   // int8 digits per transformed A / B value
+    int nW;       // digit-weight classes = dA + dB - 1
+    int nchunk;   // contraction chunks per (j, t, w)
+    int njobs;    // NB * K * nW * nchunk
+};
+
+struct PwParams {
+    PwJobs jobs;
+    int rows;          // valid rows of A (and of the output planes)
+    int cols;          // valid columns of the output planes (= rows of B^T)
+    int kdim;          // valid contraction length of one plane pair
+    int kblocks;       // ceil(kdim / PW_BK)
+    int block_n;       // MMA N: 64, 128 or 256
+    int tiles_m, tiles_n;
+    long long num_tiles;
+    int32_t* out;      // [job][rows][ldo] int32
+    long long out_plane;  // elements between job planes
+    int ldo;           // output row stride (elements)
+    int* err;          // device status word (0 = ok)
+    unsigned long long timeout_ns;
+};
+
+// Segment s of job q: which A plane and which F plane feed it.  Shared by
+// the kernel and the host-side checker so both read the same job table.
+__host__ __device__ inline void pw_job_decode(const PwJobs& J, int q, int& j, int& t, int& w,
+                                              int& ch) {
+    ch = q % J.nchunk;
+    int r = q / J.nchunk;
+    w = r % J.nW;
+    r /= J.nW;
+    t = r % J.K;
+    j = r / J.K;
+}
+
+__host__ __device__ inline int pw_class_first_da(const PwJobs& J, int w) {
+    int lo = w - (J.dB - 1);
+    return lo > 0 ? lo : 0;
+}
+__host__ __device__ inline int pw_class_pairs(const PwJobs& J, int w) {
+    int lo = pw_class_first_da(J, w);
+    int hi = w < J.dA - 1 ? w : J.dA - 1;
+    return hi - lo + 1;
+}
+// segments [s0, s1) of job q's class that chunk ch covers; the split is
+// balanced so no chunk is empty while nchunk <= K (checked by the planner)
+__host__ __device__ inline void pw_chunk_range(const PwJobs& J, int w, int ch, int& s0, int& s1) {
+    int total = pw_class_pairs(J, w) * J.K;
+    s0 = (int)((long long)ch * total / J.nchunk);
+    s1 = (int)((long long)(ch + 1) * total / J.nchunk);
+}
+__host__ __device__ inline void pw_segment_planes(const PwJobs& J, int j, int t, int w, int s,
+                                                  int& planeA, int& planeF) {
+    int pair = s / J.K, c1 = s % J.K;
+    int da = pw_class_first_da(J, w) + pair;
+    int db = w - da;
+    planeA = (j * J.dA + da) * J.K + c1;
+    planeF = (j * J.dB + db) * (2 * J.K - 1) + (J.K - 1 - t + c1);
+}
+
+}  // namespace mfftb
