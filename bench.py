@@ -1,0 +1,456 @@
+#!/usr/bin/env python3
+"""bench.py -- seconds per exact n x n W-bit integer matmul on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+    python bench.py --impl reference ...                      (reference CPU arm)
+
+Metric: "s per exact n x n W-bit matmul; effective int8 TOPS
+vs tcgen05 int8 peak".  One step = one exact product of the workload's two
+matrices (inputs resident in HBM, device-timed with CUDA events on the
+launching stream, max over ranks).  The default workload is BASELINE
+configs[4] (n=16384, W=64 signed, the north star's target configuration); the
+others are selectable with --workload c1..c5 (configs[0..4]).
+
+Also reported on the same JSON line: the live roofline of the dominant kernel
+(the tcgen05 pointwise contraction), an end-to-end number through the C ABI
+with host buffers (H2D + compute + D2H every step), the reference CPU
+baseline timed on a bounded sample, SM clocks sampled during the timed
+region and the number of our kernel launches.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEED_A, SEED_B = 12345, 12345 ^ 0xABCDEF
+RL_OF = lambda L: 2 * L + 1  # noqa: E731
+
+WORKLOADS = {
+    "c1": dict(n=64, kind="u16", L=512, signed=False,
+               desc="configs[0]: n=64, W=8192 unsigned (bigmat_rand)"),
+    "c2": dict(n=1024, kind="u16", L=16, signed=True,
+               desc="configs[1]: n=1024, W=256 signed two's complement"),
+    "c3": dict(n=4096, kind="u16", L=64, signed=False,
+               desc="configs[2]: n=4096, W=1024 unsigned (bigmat_rand)"),
+    "c4": dict(n=8192, kind="f32", force_bits=512,
+               desc="configs[3]: n=8192 fp32 N(0,1)*2^k on the 512-bit grid"),
+    "c5": dict(n=16384, kind="i64", signed=True,
+               desc="configs[4]: n=16384, W=64 signed int64"),
+}
+# bounded CPU samples of the same workload for the reference arm / baseline:
+# (sample n, what is timed).  Full-size reference runs take hours (c3-c5).
+CPU_SAMPLE_N = {"c1": 64, "c2": 256, "c3": 128, "c4": 256, "c5": 512}
+
+METRIC = "s per exact n x n W-bit matmul; effective int8 TOPS vs tcgen05 int8 peak"
+
+
+# ---------------------------------------------------------------------------- helpers
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_count():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------- reference CPU work
+def _ref_sample(workload, n_s, reps):
+    """Run the reference's own CPU hot path (oracle/_ref, compiled from the
+    reference sources) once on a sample of the workload; returns seconds of
+    the reference's timed region (the product; encode/decode excluded as in
+    src/mlgemm.c:1103-1106)."""
+    import numpy as np
+    from oracle.oracle import Oracle, RefLib
+    r, o = RefLib(), Oracle()
+    w = WORKLOADS[workload]
+    best = 1e30
+    if w["kind"] in ("u16", "i64"):
+        L = w.get("L", 4)
+        if w["kind"] == "i64":
+            A = o.int64_to_planes(o.int64_entries(n_s, SEED_A), n_s)
+            B = o.int64_to_planes(o.int64_entries(n_s, SEED_B), n_s)
+        elif w["signed"]:
+            A, B = o.signed_planes(n_s, L, SEED_A), o.signed_planes(n_s, L, SEED_B)
+        else:
+            A, B = r.bigmat_rand(n_s, L, SEED_A), r.bigmat_rand(n_s, L, SEED_B)
+        signed = w["kind"] == "i64" or w["signed"]
+        if signed:
+            A32, B32 = o.signlimb(A, n_s, L), o.signlimb(B, n_s, L)
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            if signed:  # conv_mfft + normalize_planes (the reference's signed route)
+                cw = r.conv_mfft(A32, B32, n_s, L)
+                r.normalize_planes(cw, 2 * L - 1, n_s, RL_OF(L))
+            else:
+                r.mm_mfft(A, B, n_s, L)
+            best = min(best, time.perf_counter() - t0)
+    else:
+        A, B = o.normal_f32(n_s, SEED_A)
+        import ctypes as C
+        from oracle.oracle import RefFpx
+        c = RefFpx()
+        r.lib.fpx_init(C.byref(c), A, B, n_s, w["force_bits"])
+        r.lib.fpx_encode(C.byref(c), A, B)
+        nn = n_s * n_s
+        A32 = np.ctypeslib.as_array(c.A32, shape=(c.L * nn,))
+        B32 = np.ctypeslib.as_array(c.B32, shape=(c.L * nn,))
+        cw = np.ctypeslib.as_array(c.Cw, shape=((2 * c.L - 1) * nn,))
+        plan = r.plan(c.L)
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            r.lib.conv_mfft(cw, A32, B32, n_s, c.L, C.byref(plan), 2)
+            best = min(best, time.perf_counter() - t0)
+        r.lib.fpx_free(C.byref(c))
+    return best
+
+
+def _ref_worker(args):
+    workload, n_s = args
+    return _ref_sample(workload, n_s, 1)
+
+
+def reference_line(args):
+    """--impl reference: the reference's CPU path on all host cores; every
+    step is one round of T concurrent bounded samples (one per core)."""
+    import multiprocessing as mp
+    w = WORKLOADS[args.workload]
+    n_s = CPU_SAMPLE_N[args.workload]
+    scale = (w["n"] / n_s) ** 3
+    T = cpu_count()
+    ctx = mp.get_context("spawn")
+    times = []
+    with ctx.Pool(T) as pool:
+        for step in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            pool.map(_ref_worker, [(args.workload, n_s)] * T)
+            dt = time.perf_counter() - t0
+            if step >= args.warmup:
+                times.append(dt)
+    per_round = statistics.mean(times)
+    value = per_round * scale / T
+    sample = (f"reference conv path (oracle/_ref, packed leaf) at n={n_s}, {T} concurrent "
+              f"processes per step, scaled by (n/{n_s})^3 = {scale:.0f}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": per_round * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
+                       "sample_n": n_s},
+            "cpu_baseline": {"value": value, "unit": "s", "cores": T, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- B200 arm
+class Workload:
+    """Device-resident inputs and one exact product per step."""
+
+    def __init__(self, name, ctx, torch, rank, world, device):
+        from mfft_bench_b200 import dist as D
+        self.name, self.w = name, WORKLOADS[name]
+        self.ctx, self.torch, self.rank, self.world = ctx, torch, rank, world
+        w = self.w
+        n = self.n = w["n"]
+        self.ranges = D.all_ranges(n, world)
+        self.r0, self.r1 = self.ranges[rank]
+        self.rows = self.r1 - self.r0
+        dev = device
+        if w["kind"] == "i64":
+            self.RL = 9
+            full_A = torch.empty(n * n, dtype=torch.int64, device=dev)
+            ctx.gen_int64(full_A, SEED_A)
+            self.B_local = torch.empty(self.rows * n, dtype=torch.int64, device=dev)
+            full_B = torch.empty(n * n, dtype=torch.int64, device=dev)
+            ctx.gen_int64(full_B, SEED_B)
+            self.bytes_in = 8
+        elif w["kind"] == "u16":
+            L = w["L"]
+            self.RL = RL_OF(L)
+            full_A = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
+            full_B = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
+            ctx.gen_bigmat(full_A, n, L, SEED_A)
+            ctx.gen_bigmat(full_B, n, L, SEED_B)
+            self.bytes_in = 2 * L
+        else:
+            from mfft_bench_b200 import gen_normal_f32
+            self.RL = 1
+            A, B = gen_normal_f32(n, SEED_A)
+            full_A = torch.from_numpy(A).to(dev)
+            full_B = torch.from_numpy(B).to(dev)
+            self.bytes_in = 4
+        ctx.sync()
+        self.A, self.B = full_A, full_B
+        # this rank's share of B (rows), gathered every step in sharded runs
+        if world > 1 and w["kind"] != "u16":
+            self.B_local = full_B.view(n, -1)[self.r0:self.r1].contiguous().view(-1)
+        self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=torch.float32
+                               if w["kind"] == "f32" else torch.uint16, device=dev)
+        self.full_out = None
+        if world > 1 and rank == 0:
+            self.full_out = torch.empty(self.RL * n * n, dtype=self.out.dtype, device=dev)
+
+    def step(self):
+        """One product; sharded across ranks when world > 1."""
+        from mfft_bench_b200 import dist as D
+        w, ctx, n = self.w, self.ctx, self.n
+        if self.world > 1 and w["kind"] != "u16":
+            D.allgather_rows(self.B_local, self.B, n, self.ranges)
+        rows = (self.r0, self.r1)
+        if w["kind"] == "i64":
+            ctx.mm_i64(self.A, self.B, n, RL=self.RL, out=self.out, rows=rows)
+        elif w["kind"] == "u16":
+            ctx.mm_u16(self.A, self.B, n, w["L"], signed=w["signed"], RL=self.RL, out=self.out,
+                       rows=rows)
+        else:
+            ctx.fp32(self.A, self.B, n, w["force_bits"], out=self.out, rows=rows)
+        if self.world > 1:
+            D.gather_planes_to_root(self.out, self.full_out, n, self.RL, self.ranges)
+
+
+def e2e_measure(ctx, wl, steps, torch):
+    """The same product through the host-pointer C ABI: pinned host inputs,
+    H2D + compute + D2H inside the timed region every step."""
+    w, n = wl.w, wl.n
+    hA = wl.A.cpu().pin_memory()
+    hB = wl.B.cpu().pin_memory()
+    hout = torch.empty(wl.RL * n * n, dtype=wl.out.dtype).pin_memory()
+    import numpy as np  # noqa: F401
+
+    def run():
+        if w["kind"] == "i64":
+            ctx.mm_i64(hA.numpy(), hB.numpy(), n, RL=wl.RL, out=hout.numpy())
+        elif w["kind"] == "u16":
+            ctx.mm_u16(hA.view(torch.int16).numpy().view("uint16"),
+                       hB.view(torch.int16).numpy().view("uint16"), n, w["L"],
+                       signed=w["signed"], RL=wl.RL, out=hout.view(torch.int16).numpy().view("uint16"))
+        else:
+            ctx.fp32(hA.numpy(), hB.numpy(), n, w["force_bits"], out=hout.numpy())
+
+    run()
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        run()
+        ts.append(time.perf_counter() - t0)
+    h2d = 2 * n * n * wl.bytes_in
+    d2h = wl.RL * n * n * (4 if w["kind"] == "f32" else 2)
+    return {"value": statistics.mean(ts), "unit": "s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = env_int("RANK", 0)
+    world = env_int("WORLD_SIZE", 1)
+    local_rank = env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        if rank == 0:
+            reference_line(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import mfft_bench_b200 as m
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    stream = torch.cuda.current_stream()
+    ctx = m.Context(local_rank, stream=stream)
+    wl = Workload(args.workload, ctx, torch, rank, world, device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        wl.step()
+    ctx.sync()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    ctx.set_profile(2)  # per-kernel events, recorded without host syncs
+    launches_per_step = None
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        wl.step()
+        if launches_per_step is None:
+            launches_per_step = ctx.launches()
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ctx.sync()
+    ms = t_start.elapsed_time(t_end) / args.steps
+    ph = ctx.phase_ms()
+    ctx.set_profile(0)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    n = wl.n
+    w = WORKLOADS[args.workload]
+    pi = ctx.last_plan()
+    peaks, peak_kind = load_peaks()
+    # int8 tcgen05 peak: twice the measured bf16 rate (kind::i8 issues 2x the
+    # MACs per cycle of kind::f16); sustained figure for a kernel inside a
+    # long step
+    peak_int8 = 2.0 * float(peaks.get("bf16_tflops_sustained", 1400.0))
+    line = {"metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic (seeded splitmix64, reference generators)",
+            "config": {"workload": args.workload, "desc": w["desc"], "n": n,
+                       "parallelism": f"row-blocks x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (no flush needed)"},
+            "gpu_launches": (launches_per_step or 0) * args.steps,
+            "clocks": clk}
+    if True:
+        macs = pi.get("int8_macs")
+        pw_ms = ph["pointwise"] / args.steps
+        if macs:
+            macs_rank = macs * (wl.rows / n)
+            achieved = 2 * macs_rank / (pw_ms * 1e-3) / 1e12
+            line["roofline"] = {
+                "bound": "tensor", "kernel": "pointwise_i8_kernel (tcgen05 kind::i8)",
+                "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
+                "frac": achieved / peak_int8, "traffic": None,
+                "peak_basis": f"2 x bf16_tflops_sustained ({peak_kind} MEASURED_PEAKS.json)",
+                "ops_per_step": 2 * macs_rank, "pointwise_ms_per_step": pw_ms}
+            line["int8_tops_issued"] = 2 * macs / (ms * 1e-3) / 1e12
+            line["schoolbook_equiv_tops"] = 2 * pi["schoolbook_macs"] / (ms * 1e-3) / 1e12
+            line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs")}
+        line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
+        share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
+        line["pointwise_share"] = share
+    traffic_path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if "roofline" in line and os.path.exists(traffic_path):
+        with open(traffic_path) as f:
+            tr = json.load(f).get(args.workload)
+        if tr:
+            line["roofline"]["traffic"] = tr["bytes_per_launch"]
+            line["roofline"]["traffic_note"] = tr.get("note")
+
+    if not args.no_e2e:
+        if world == 1:
+            line["e2e"] = e2e_measure(ctx, wl, min(3, args.steps), torch)
+        else:
+            line["e2e"] = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            n_s = CPU_SAMPLE_N[args.workload]
+            t = _ref_sample(args.workload, n_s, 2)
+            scale = (n / n_s) ** 3
+            line["cpu_baseline"] = {
+                "value": t * scale, "unit": "s", "cores": 1, "kind": "reference",
+                "sample": (f"reference conv path (oracle/_ref, packed leaf, single thread as in "
+                           f"the reference) at n={n_s}: {t:.3f} s, scaled by (n/{n_s})^3 = "
+                           f"{scale:.0f}")}
+        except Exception as e:  # the baseline is reported, never required
+            line["cpu_baseline"] = {"value": None, "unit": "s", "cores": 0, "kind": "reference",
+                                    "sample": f"unavailable: {e}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

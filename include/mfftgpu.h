@@ -1,0 +1,151 @@
+/* mfftgpu.h -- native C ABI of libmfftb200, the B200 (sm_100a) implementation
+ * of hadilq/mfft-bench's exact-integer MFFT matmul path.
+ *
+ * Every entry point returns an int status (MFFTGPU_OK = 0) and never exits
+ * the process.  A context owns one CUDA device, one stream, a grow-only
+ * device workspace and a device status word.  "_dev" entry points take
+ * device pointers and are asynchronous on the context stream (call
+ * mfftgpu_sync for the status of the device-side checks); the other
+ * entry points take host pointers, copy inputs in, compute, copy results
+ * out and synchronise.
+ *
+ * Layouts follow the reference (src/mfftbench.h:74-82): a matrix of
+ * multi-limb integers is plane-major, p[u*n*n + i*n + j] = limb u of entry
+ * (i, j), limbs of 16 bits, least significant first.  Products come back as
+ * RL limbs of two's complement.  A row range [row_begin, row_end) computes
+ * only those rows of C (row-block sharding across GPUs); out then holds
+ * (row_end - row_begin) rows per plane.
+ *
+ * The reference's own API (mm_mfft, conv_mfft, fpx_*) is provided on top of
+ * this by include/mfftbench_b200.h.
+ */
+#ifndef MFFTGPU_H
+#define MFFTGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    MFFTGPU_OK = 0,
+    MFFTGPU_ERR_ARG = 1,
+    MFFTGPU_ERR_NOMEM = 2,
+    MFFTGPU_ERR_CUDA = 3,
+    MFFTGPU_ERR_TIMEOUT = 4,
+    MFFTGPU_ERR_RANGE = 5,
+    MFFTGPU_ERR_NODEVICE = 6,
+    MFFTGPU_ERR_PLAN = 7,
+    MFFTGPU_ERR_UNSUPPORTED = 8,
+};
+
+typedef struct mfftgpu_ctx mfftgpu_ctx;
+
+/* Plan summary (see mfft_bench_b200/csrc/plan.h). */
+typedef struct {
+    int n, n_int, mode, b, LbA, LbB, S, NB, K, g, ncA, ncB, dA, dB, nW, nchunk, njobs,
+        positions;
+    long long acc_bound;
+    double inv_bound_log2;
+    double int8_macs;        /* issued int8 MACs for the whole n x n product */
+    double schoolbook_macs;  /* n^3 * LbA * LbB: the limb-plane schoolbook equivalent */
+} mfftgpu_plan_info;
+
+/* --- context --------------------------------------------------------------
+ * Replaces the reference's implicit process-global state (g_mfft_prof,
+ * src/mfft.c:43-44; scratch malloc'd per call, src/mfft.c:310-316). */
+int mfftgpu_create(mfftgpu_ctx **ctx, int device);
+int mfftgpu_destroy(mfftgpu_ctx *ctx);
+int mfftgpu_set_stream(mfftgpu_ctx *ctx, void *cuda_stream);
+int mfftgpu_set_workspace_limit(mfftgpu_ctx *ctx, size_t bytes);
+int mfftgpu_set_timeout_ns(mfftgpu_ctx *ctx, unsigned long long ns);
+int mfftgpu_sync(mfftgpu_ctx *ctx);
+const char *mfftgpu_last_error(mfftgpu_ctx *ctx);
+const char *mfftgpu_status_string(int status);
+int mfftgpu_device_count(void);
+
+/* Plan the product (mode 0: value re-radix, 1: limb mode as used by
+ * conv_mfft).  wA/wB: magnitude bits (mode 0) or limb counts (mode 1). */
+int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info *out);
+/* The plan of the last product run on this context (the fp32 plan depends on
+ * the exponent window of the data). */
+int mfftgpu_last_plan(mfftgpu_ctx *ctx, mfftgpu_plan_info *out);
+
+/* Per-kernel device timing (mirrors the reference's --profile split,
+ * src/mfft.c:43-73).  mode 0: off; 1: the last product; 2: accumulate over
+ * every product since this call.  Events are recorded on the context stream
+ * without host synchronisation, so profiling does not perturb a timed loop.
+ * mfftgpu_last_phase_ms waits for the events and returns milliseconds:
+ * [pack, forward, pointwise, inverse+carry, first-to-last event]. */
+int mfftgpu_set_profile(mfftgpu_ctx *ctx, int mode);
+int mfftgpu_last_phase_ms(mfftgpu_ctx *ctx, float out[5]);
+/* Number of kernel launches of the last product. */
+int mfftgpu_last_launches(mfftgpu_ctx *ctx);
+
+/* --- exact integer products ------------------------------------------------
+ * Replaces mm_mfft (src/mfft.c:424-438, src/mfftbench.h:156-157).  A, B: L
+ * uint16 limb planes each; is_signed = 1 reads them as two's complement
+ * 16L-bit integers (the reference's signed convention via conv_mfft +
+ * normalize_planes).  out: RL limb planes of the rows asked for. */
+int mfftgpu_mm_u16_dev(mfftgpu_ctx *ctx, const uint16_t *A, const uint16_t *B, int n, int L,
+                       int is_signed, uint16_t *out, int RL, int row_begin, int row_end);
+int mfftgpu_mm_u16(mfftgpu_ctx *ctx, const uint16_t *A, const uint16_t *B, int n, int L,
+                   int is_signed, uint16_t *out, int RL);
+
+/* W <= 64-bit signed entries, row-major int64 (A[i*n + j]). */
+int mfftgpu_mm_i64_dev(mfftgpu_ctx *ctx, const int64_t *A, const int64_t *B, int n,
+                       uint16_t *out, int RL, int row_begin, int row_end);
+int mfftgpu_mm_i64(mfftgpu_ctx *ctx, const int64_t *A, const int64_t *B, int n, uint16_t *out,
+                   int RL);
+
+/* Replaces conv_mfft (src/mfft.c:302-422): int32 limb planes with
+ * |limb| <= 65535 (the signed-limb convention of src/fpfixed.c:187-192);
+ * writes the 2L-1 unnormalised int64 convolution planes
+ * Cw[w] = sum_{u+v=w} A_u B_v, bit-identical to the reference. */
+int mfftgpu_conv_i32_dev(mfftgpu_ctx *ctx, const int32_t *A32, const int32_t *B32, int n, int L,
+                         int64_t *Cw);
+int mfftgpu_conv_i32(mfftgpu_ctx *ctx, const int32_t *A32, const int32_t *B32, int n, int L,
+                     int64_t *Cw);
+
+/* --- fp32 fixed-point embedding --------------------------------------------
+ * fpx_init + fpx_encode + conv + fpx_decode_f32 (src/fpfixed.c:96-285) fused
+ * on the device: C = A * B computed exactly on the grid (force_bits > 0:
+ * SA = SB = force_bits/2; 0: adaptive grid from the data) and rounded once to
+ * fp32.  Row-major fp32 n x n. */
+int mfftgpu_fp32_dev(mfftgpu_ctx *ctx, const float *A, const float *B, int n, int force_bits,
+                     float *C, int row_begin, int row_end);
+int mfftgpu_fp32(mfftgpu_ctx *ctx, const float *A, const float *B, int n, int force_bits,
+                 float *C);
+
+/* --- device-side input generators (bench workloads) ------------------------
+ * bigmat_rand (src/bigmat.c:20-35) evaluated in parallel: draw i of the
+ * splitmix64 stream from `seed` is a pure function of (seed, i). */
+int mfftgpu_gen_bigmat_dev(mfftgpu_ctx *ctx, uint16_t *m, int n, int L, uint64_t seed);
+int mfftgpu_gen_int64_dev(mfftgpu_ctx *ctx, int64_t *x, size_t count, uint64_t seed);
+/* fp32 workload on the host: N(0,1) * 2^k, k uniform in [-8, 8]; one
+ * splitmix64 stream, A's entries first, 3 draws per entry (Box-Muller u1, u2,
+ * then k).  The reference's ML track only generates U(-1,1)
+ * (src/mlgemm.c:657-680). */
+void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
+
+/* Self-test of the tcgen05 pointwise kernel: random int8 Ahat/F planes for
+ * the given job shape, the kernel's int32 job planes compared element by
+ * element with a CUDA-core evaluation of the same job table.  *mismatches
+ * receives the number of differing elements. */
+int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
+                               int dA, int dB, int nchunk, int block_n, long long *mismatches);
+
+/* Self-test of the bounded device waits: launches the pointwise kernel with
+ * a producer that never loads, so its consumers must give up after
+ * timeout_ns.  Returns MFFTGPU_ERR_TIMEOUT when the timeout path works; the
+ * context stays usable afterwards. */
+int mfftgpu_selftest_timeout(mfftgpu_ctx *ctx, unsigned long long timeout_ns);
+
+/* host self-test of the device fp32 rounding rule (no GPU needed) */
+float mfftgpu_decode_words_f32(uint32_t *words, int nwords, int bit_off, int S);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,13 @@
+"""mfft_bench_b200 -- B200 (sm_100a) implementation of hadilq/mfft-bench's
+exact-integer MFFT matmul hot path (mm_mfft / conv_mfft + the fp32 fpfixed
+embedding), behind the reference's own C API.
+
+The compute path is libmfftb200.so (hand-written CUDA for sm_100a:
+limb-split pack, forward/inverse MFFT transforms, tcgen05 int8 pointwise
+contraction, fused fold/carry/round).  Python only binds it.
+"""
+from .api import (KERNEL_PACKED, KERNEL_SM100, PLAN_LIMB, PLAN_VALUE, Context, Fpx,  # noqa: F401
+                  MfftError, bigmat_rand, conv_mfft, decode_words_f32, device_count,
+                  fpx_gemm_f32, gen_normal_f32, mfft_plan_init, mm_mfft, mm_mfft_signed, normalize_planes,
+                  plan_info)
+from ._lib import LIB_PATH  # noqa: F401

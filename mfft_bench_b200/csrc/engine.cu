@@ -1,0 +1,831 @@
+// engine.cu -- host orchestration of the B200 MFFT path and the native C ABI
+// (include/mfftgpu.h).
+//
+// One product = pack(B, transposed) -> forward(F stack) once, then for each
+// row block of A: pack(A) -> forward(Ahat) -> tcgen05 pointwise -> inverse +
+// fold + carry straight into the caller's output rows.  Row blocks bound the
+// device workspace (the reference mallocs NB*K full planes per call,
+// src/mfft.c:310-316; here only F is kept whole) and are also the unit of
+// multi-GPU sharding: a rank computes rows [row_begin, row_end).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "../../include/mfftgpu.h"
+#include "kernels.h"
+#include "plan.h"
+#include "runtime.h"
+
+using namespace mfftb;
+
+struct mfftgpu_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    int* d_err = nullptr;    // device status word
+    int* d_scan = nullptr;   // fp32 exponent scan results
+    char* ws = nullptr;      // grow-only workspace
+    size_t ws_bytes = 0;
+    size_t ws_limit = 0;
+    char* io = nullptr;      // grow-only staging for the host-pointer entry points
+    size_t io_bytes = 0;
+    unsigned long long timeout_ns = 4000000000ull;
+    int profile = 0;  // 0 off, 1 last product, 2 accumulate across products
+    // profiling: start/end events per launch, recorded without host syncs;
+    // times are read back lazily by mfftgpu_last_phase_ms
+    static constexpr int kMaxEv = 512;
+    cudaEvent_t ev[kMaxEv] = {};
+    int ev_phase[kMaxEv / 2] = {};
+    int ev_used = 0;
+    float phase_ms[5] = {};
+    bool phase_valid = true;
+    int launches = 0;
+    Plan last_plan{};
+    bool have_plan = false;
+    char msg[512] = {};
+};
+
+namespace {
+
+int set_err(mfftgpu_ctx* c, int code, const char* fmt, ...) {
+    if (c) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(c->msg, sizeof c->msg, fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+#define CUDA_OK(call)                                                                  \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess)                                                         \
+            return set_err(C, MFFTB_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+int ensure(mfftgpu_ctx* C, char** buf, size_t* have, size_t need) {
+    if (need <= *have) return MFFTB_OK;
+    if (*buf) {
+        cudaStreamSynchronize(C->stream);
+        cudaFree(*buf);
+        *buf = nullptr;
+        *have = 0;
+    }
+    size_t sz = (need + (1u << 20) - 1) & ~(size_t)((1u << 20) - 1);
+    if (cudaMalloc(buf, sz) != cudaSuccess) {
+        cudaGetLastError();
+        return set_err(C, MFFTB_ERR_NOMEM, "cudaMalloc(%zu bytes) failed", sz);
+    }
+    *have = sz;
+    return MFFTB_OK;
+}
+
+struct Operand {
+    int fmt;
+    const void* p;
+    int n, L16, W, is_signed;
+    int S_grid, lo_bit, trunc_rel;
+};
+
+struct OutSpec {
+    int kind;   // INV_*
+    void* p;
+    long long plane;
+    int ld;
+    int RL;
+    int bit_off, S_scale;
+    int esize;  // bytes per output element
+};
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int inv_elems(const Plan& P) {
+    int nk = P.NB * P.K;
+    int e = 32;
+    while (e > 1 && (nk * e > 16 * 256 || (size_t)nk * e * 8 > 200 * 1024)) e >>= 1;
+    return e;
+}
+
+int log2i(int x) {
+    int r = 0;
+    while ((1 << r) < x) ++r;
+    return r;
+}
+
+int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& B,
+                int row_begin, int row_end, const OutSpec& O) {
+    const int n_int = P.n_int;
+    const int dbytes = plan_digit_bytes(P);
+    const long long nn_int = (long long)n_int * n_int;
+    const int rows = row_end - row_begin;
+    if (rows <= 0) return MFFTB_OK;
+    const int fpl = P.NB * P.dB * (2 * P.K - 1);
+    const int apl = P.NB * P.dA * P.K;
+    const size_t szDB = align256((size_t)P.LbB * nn_int * dbytes);
+    const size_t szF = align256((size_t)fpl * nn_int);
+    const size_t per_row = (size_t)n_int * ((size_t)P.LbA * dbytes + apl + 4 * (size_t)P.njobs);
+    size_t limit = C->ws_limit;
+    const int rows_pad = (rows + 15) / 16 * 16;
+    long long R;
+    if (limit > szDB + szF + per_row * 128)
+        R = (long long)((limit - szDB - szF) / per_row) / 128 * 128;
+    else
+        R = 128;
+    if (R > rows_pad) R = rows_pad;
+    if (R < 16) R = 16;
+    const size_t szDA = align256((size_t)P.LbA * R * n_int * dbytes);
+    const size_t szAh = align256((size_t)apl * R * n_int);
+    const size_t szAcc = align256((size_t)P.njobs * R * n_int * 4);
+    int rc = ensure(C, &C->ws, &C->ws_bytes, szDB + szF + szDA + szAh + szAcc);
+    if (rc) return rc;
+    char* DB = C->ws;
+    int8_t* F = reinterpret_cast<int8_t*>(DB + szDB);
+    char* DA = DB + szDB + szF;
+    int8_t* Ah = reinterpret_cast<int8_t*>(DA + szDA);
+    int32_t* acc = reinterpret_cast<int32_t*>(DA + szDA + szAh);
+    cudaStream_t st = C->stream;
+    C->launches = 0;
+    C->last_plan = P;
+    C->have_plan = true;
+    CUDA_OK(cudaMemsetAsync(C->d_err, 0, sizeof(int), st));
+    if (C->profile != 2) C->ev_used = 0;
+    C->phase_valid = false;
+    // phase ids: 0 pack, 1 forward, 2 pointwise, 3 inverse
+    int cur_phase = 0;
+    auto tick = [&](int phase) {
+        cur_phase = phase;
+        if (C->profile && C->ev_used + 2 <= mfftgpu_ctx::kMaxEv)
+            cudaEventRecord(C->ev[C->ev_used], st);
+    };
+    auto tock = [&]() {
+        if (C->profile && C->ev_used + 2 <= mfftgpu_ctx::kMaxEv) {
+            cudaEventRecord(C->ev[C->ev_used + 1], st);
+            C->ev_phase[C->ev_used / 2] = cur_phase;
+            C->ev_used += 2;
+        }
+    };
+
+    // ---- B: digits (transposed) and the F stack, once per product
+    PackArgs pb{};
+    pb.fmt = B.fmt;
+    pb.src = B.p;
+    pb.n = B.n;
+    pb.row0 = 0;
+    pb.L16 = B.L16;
+    pb.W = B.W;
+    pb.is_signed = B.is_signed;
+    pb.S_grid = B.S_grid;
+    pb.lo_bit = B.lo_bit;
+    pb.trunc_rel = B.trunc_rel;
+    pb.b = P.b;
+    pb.Lb = P.LbB;
+    pb.dst = DB;
+    pb.rows = n_int;
+    pb.ld = n_int;
+    pb.plane = nn_int;
+    pb.transpose = 1;
+    pb.err = C->d_err;
+    tick(0);
+    if ((rc = pack_launch(pb, st))) return set_err(C, rc, "pack(B) launch failed");
+    ++C->launches;
+    tock();
+    FwdArgs fb{};
+    fb.D = DB;
+    fb.dbytes = dbytes;
+    fb.dplane = nn_int;
+    fb.Lb = P.LbB;
+    fb.nelem = nn_int;
+    fb.S = P.S;
+    fb.NB = P.NB;
+    fb.K = P.K;
+    fb.g = P.g;
+    fb.nc = P.ncB;
+    fb.d = P.dB;
+    fb.lgS = log2i(P.S);
+    fb.lgK = log2i(P.K);
+    fb.f_stack = 1;
+    fb.out = F;
+    fb.oplane = nn_int;
+    fb.err = C->d_err;
+    tick(1);
+    if ((rc = forward_launch(fb, st))) return set_err(C, rc, "forward(B) launch failed");
+    ++C->launches;
+    tock();
+
+    // ---- A row blocks
+    for (int r = 0; r < rows; r += (int)R) {
+        const int rb = (int)std::min<long long>(R, rows - r);
+        PackArgs pa = pb;
+        pa.fmt = A.fmt;
+        pa.src = A.p;
+        pa.n = A.n;
+        pa.row0 = row_begin + r;
+        pa.L16 = A.L16;
+        pa.W = A.W;
+        pa.is_signed = A.is_signed;
+        pa.S_grid = A.S_grid;
+        pa.lo_bit = A.lo_bit;
+        pa.trunc_rel = A.trunc_rel;
+        pa.Lb = P.LbA;
+        pa.dst = DA;
+        pa.rows = rb;
+        pa.plane = R * n_int;
+        pa.transpose = 0;
+        tick(0);
+        if ((rc = pack_launch(pa, st))) return set_err(C, rc, "pack(A) launch failed");
+        ++C->launches;
+        tock();
+        FwdArgs fa = fb;
+        fa.D = DA;
+        fa.dplane = R * n_int;
+        fa.Lb = P.LbA;
+        fa.nelem = (long long)rb * n_int;
+        fa.nc = P.ncA;
+        fa.d = P.dA;
+        fa.f_stack = 0;
+        fa.out = Ah;
+        fa.oplane = R * n_int;
+        tick(1);
+        if ((rc = forward_launch(fa, st))) return set_err(C, rc, "forward(A) launch failed");
+        ++C->launches;
+        tock();
+
+        PwLaunch L{};
+        L.A = Ah;
+        L.lda = n_int;
+        L.a_plane_bytes = R * n_int;
+        L.a_planes = apl;
+        L.F = F;
+        L.ldf = n_int;
+        L.f_plane_bytes = nn_int;
+        L.f_planes = fpl;
+        L.rows = rb;
+        L.cols = n_int;
+        L.kdim = n_int;
+        L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs};
+        L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
+        L.out = acc;
+        L.out_plane = R * n_int;
+        L.ldo = n_int;
+        L.err = C->d_err;
+        L.timeout_ns = C->timeout_ns;
+        L.num_sms = C->num_sms;
+        tick(2);
+        if ((rc = pointwise_launch(L, st))) return set_err(C, rc, "pointwise launch failed");
+        ++C->launches;
+        tock();
+
+        InvArgs ia{};
+        ia.acc = acc;
+        ia.acc_plane = R * n_int;
+        ia.lda = n_int;
+        ia.rows = rb;
+        ia.cols = P.n;
+        ia.S = P.S;
+        ia.NB = P.NB;
+        ia.K = P.K;
+        ia.g = P.g;
+        ia.nW = P.nW;
+        ia.nchunk = P.nchunk;
+        ia.log2NB = log2i(P.NB);
+        ia.lgS = log2i(P.S);
+        ia.lgK = log2i(P.K);
+        ia.b = P.b;
+        ia.positions = P.positions;
+        ia.out_kind = O.kind;
+        ia.out = static_cast<char*>(O.p) + (size_t)r * O.ld * O.esize;
+        ia.out_plane = O.plane;
+        ia.ldo = O.ld;
+        ia.RL = O.RL;
+        ia.bit_off = O.bit_off;
+        ia.S_scale = O.S_scale;
+        ia.elems = inv_elems(P);
+        ia.lgE = log2i(ia.elems);
+        ia.err = C->d_err;
+        tick(3);
+        if ((rc = inverse_launch(ia, st))) return set_err(C, rc, "inverse launch failed (%d)", rc);
+        ++C->launches;
+        tock();
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_err(C, MFFTB_ERR_CUDA, "%s", cudaGetErrorString(e));
+    return MFFTB_OK;
+}
+
+int check_rows(int n, int row_begin, int row_end) {
+    return (row_begin < 0 || row_end > n || row_begin > row_end) ? MFFTB_ERR_ARG : MFFTB_OK;
+}
+
+int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P) {
+    int rc = plan_search(n, mode, wA, wB, 0, 0, P);
+    if (rc)
+        return set_err(C, MFFTB_ERR_PLAN, "no exact int8 plan for n=%d mode=%d widths %d/%d", n,
+                       mode, wA, wB);
+    return MFFTB_OK;
+}
+
+__global__ void gen_u16_kernel(uint16_t* m, long long count, uint64_t seed) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count;
+         i += (long long)gridDim.x * blockDim.x) {
+        uint64_t z = seed + (uint64_t)(i + 1) * 0x9E3779B97F4A7C15ULL;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+        m[i] = (uint16_t)((z ^ (z >> 31)) & 0xFFFFu);
+    }
+}
+
+__global__ void gen_i64_kernel(int64_t* x, long long count, uint64_t seed) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count;
+         i += (long long)gridDim.x * blockDim.x) {
+        uint64_t z = seed + (uint64_t)(i + 1) * 0x9E3779B97F4A7C15ULL;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+        x[i] = (int64_t)(z ^ (z >> 31));
+    }
+}
+
+int next_pow2i(int x) {
+    int r = 1;
+    while (r < x) r <<= 1;
+    return r;
+}
+
+}  // namespace
+
+// =====================================================================================
+extern "C" {
+
+const char* mfftgpu_status_string(int s) {
+    switch (s) {
+        case MFFTGPU_OK: return "ok";
+        case MFFTGPU_ERR_ARG: return "invalid argument";
+        case MFFTGPU_ERR_NOMEM: return "out of device memory";
+        case MFFTGPU_ERR_CUDA: return "CUDA error";
+        case MFFTGPU_ERR_TIMEOUT: return "device-side wait timed out";
+        case MFFTGPU_ERR_RANGE: return "input limb out of range";
+        case MFFTGPU_ERR_NODEVICE: return "no usable sm_100 device";
+        case MFFTGPU_ERR_PLAN: return "no exact plan";
+        case MFFTGPU_ERR_UNSUPPORTED: return "unsupported";
+        default: return "unknown status";
+    }
+}
+
+int mfftgpu_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int mfftgpu_create(mfftgpu_ctx** out, int device) {
+    if (!out) return MFFTB_ERR_ARG;
+    *out = nullptr;
+    int ndev = mfftgpu_device_count();
+    if (device < 0 || device >= ndev) return MFFTB_ERR_NODEVICE;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return MFFTB_ERR_CUDA;
+    if (prop.major != 10 || prop.minor != 0) return MFFTB_ERR_NODEVICE;
+    mfftgpu_ctx* C = new (std::nothrow) mfftgpu_ctx();
+    if (!C) return MFFTB_ERR_NOMEM;
+    C->device = device;
+    C->num_sms = prop.multiProcessorCount;
+    if (cudaSetDevice(device) != cudaSuccess) {
+        delete C;
+        return MFFTB_ERR_CUDA;
+    }
+    if (cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&C->d_err, 64) != cudaSuccess) {
+        delete C;
+        return MFFTB_ERR_CUDA;
+    }
+    C->own_stream = true;
+    C->d_scan = C->d_err + 4;
+    for (auto& e : C->ev) {
+        if (cudaEventCreate(&e) != cudaSuccess) {
+            e = nullptr;
+            C->profile = 0;
+        }
+    }
+    size_t fr = 0, tot = 0;
+    cudaMemGetInfo(&fr, &tot);
+    C->ws_limit = (size_t)(0.55 * (double)fr);
+    if (const char* s = getenv("MFFTGPU_WS_GB")) C->ws_limit = (size_t)(atof(s) * 1073741824.0);
+    cudaMemset(C->d_err, 0, 64);
+    *out = C;
+    return MFFTB_OK;
+}
+
+int mfftgpu_destroy(mfftgpu_ctx* C) {
+    if (!C) return MFFTB_OK;
+    cudaSetDevice(C->device);
+    if (C->stream) cudaStreamSynchronize(C->stream);
+    cudaFree(C->ws);
+    cudaFree(C->io);
+    cudaFree(C->d_err);
+    for (auto& e : C->ev)
+        if (e) cudaEventDestroy(e);
+    if (C->own_stream && C->stream) cudaStreamDestroy(C->stream);
+    delete C;
+    return MFFTB_OK;
+}
+
+int mfftgpu_set_stream(mfftgpu_ctx* C, void* s) {
+    if (!C) return MFFTB_ERR_ARG;
+    if (C->own_stream && C->stream) cudaStreamDestroy(C->stream);
+    C->stream = static_cast<cudaStream_t>(s);
+    C->own_stream = false;
+    return MFFTB_OK;
+}
+
+int mfftgpu_set_workspace_limit(mfftgpu_ctx* C, size_t bytes) {
+    if (!C) return MFFTB_ERR_ARG;
+    C->ws_limit = bytes;
+    return MFFTB_OK;
+}
+
+int mfftgpu_set_timeout_ns(mfftgpu_ctx* C, unsigned long long ns) {
+    if (!C || ns == 0) return MFFTB_ERR_ARG;
+    C->timeout_ns = ns;
+    return MFFTB_OK;
+}
+
+int mfftgpu_set_profile(mfftgpu_ctx* C, int mode) {
+    if (!C || mode < 0 || mode > 2) return MFFTB_ERR_ARG;
+    C->profile = mode;
+    C->ev_used = 0;
+    C->phase_valid = false;
+    return MFFTB_OK;
+}
+
+int mfftgpu_last_phase_ms(mfftgpu_ctx* C, float out[5]) {
+    if (!C || !out) return MFFTB_ERR_ARG;
+    if (!C->phase_valid) {
+        for (float& v : C->phase_ms) v = 0.0f;
+        if (C->ev_used >= 2) {
+            cudaSetDevice(C->device);
+            CUDA_OK(cudaEventSynchronize(C->ev[C->ev_used - 1]));
+            for (int k = 0; k < C->ev_used; k += 2) {
+                float ms = 0;
+                CUDA_OK(cudaEventElapsedTime(&ms, C->ev[k], C->ev[k + 1]));
+                C->phase_ms[C->ev_phase[k / 2]] += ms;
+            }
+            float tot = 0;
+            CUDA_OK(cudaEventElapsedTime(&tot, C->ev[0], C->ev[C->ev_used - 1]));
+            C->phase_ms[4] = tot;
+        }
+        C->phase_valid = true;
+    }
+    memcpy(out, C->phase_ms, sizeof C->phase_ms);
+    return MFFTB_OK;
+}
+
+int mfftgpu_last_launches(mfftgpu_ctx* C) { return C ? C->launches : 0; }
+
+const char* mfftgpu_last_error(mfftgpu_ctx* C) { return C ? C->msg : "no context"; }
+
+int mfftgpu_sync(mfftgpu_ctx* C) {
+    if (!C) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    CUDA_OK(cudaStreamSynchronize(C->stream));
+    int h = 0;
+    CUDA_OK(cudaMemcpy(&h, C->d_err, sizeof h, cudaMemcpyDeviceToHost));
+    if (h) return set_err(C, h, "device reported: %s", mfftgpu_status_string(h));
+    return MFFTB_OK;
+}
+
+static void fill_info(const Plan& P, mfftgpu_plan_info* o);
+
+int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o) {
+    if (!o) return MFFTB_ERR_ARG;
+    Plan P;
+    if (plan_search(n, mode, wA, wB, 0, 0, &P)) return MFFTB_ERR_PLAN;
+    fill_info(P, o);
+    return MFFTB_OK;
+}
+
+int mfftgpu_last_plan(mfftgpu_ctx* C, mfftgpu_plan_info* o) {
+    if (!C || !o || !C->have_plan) return MFFTB_ERR_ARG;
+    fill_info(C->last_plan, o);
+    return MFFTB_OK;
+}
+
+static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
+    const int n = P.n;
+    o->n = P.n;
+    o->n_int = P.n_int;
+    o->mode = P.mode;
+    o->b = P.b;
+    o->LbA = P.LbA;
+    o->LbB = P.LbB;
+    o->S = P.S;
+    o->NB = P.NB;
+    o->K = P.K;
+    o->g = P.g;
+    o->ncA = P.ncA;
+    o->ncB = P.ncB;
+    o->dA = P.dA;
+    o->dB = P.dB;
+    o->nW = P.nW;
+    o->nchunk = P.nchunk;
+    o->njobs = P.njobs;
+    o->positions = P.positions;
+    o->acc_bound = P.acc_bound;
+    o->inv_bound_log2 = P.inv_bound_log2;
+    o->int8_macs = P.macs_per_elem * (double)P.n_int * P.n_int;
+    o->schoolbook_macs = (double)n * n * (double)n * P.LbA * P.LbB;
+}
+
+// --------------------------------------------------------------------- integers
+int mfftgpu_mm_u16_dev(mfftgpu_ctx* C, const uint16_t* A, const uint16_t* B, int n, int L,
+                       int is_signed, uint16_t* out, int RL, int row_begin, int row_end) {
+    if (!C || !A || !B || !out || n <= 0 || L <= 0 || RL <= 0) return MFFTB_ERR_ARG;
+    if (check_rows(n, row_begin, row_end)) return set_err(C, MFFTB_ERR_ARG, "bad row range");
+    cudaSetDevice(C->device);
+    Plan P;
+    int rc = plan_or_err(C, n, PLAN_VALUE, 16 * L, 16 * L, &P);
+    if (rc) return rc;
+    Operand a{PACK_U16PL, A, n, L, 16 * L, is_signed ? 1 : 0, 0, 0, 0};
+    Operand b = a;
+    b.p = B;
+    OutSpec o{INV_U16, out, (long long)(row_end - row_begin) * n, n, RL, 0, 0, 2};
+    return run_product(C, P, a, b, row_begin, row_end, o);
+}
+
+int mfftgpu_mm_i64_dev(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n, uint16_t* out,
+                       int RL, int row_begin, int row_end) {
+    if (!C || !A || !B || !out || n <= 0 || RL <= 0) return MFFTB_ERR_ARG;
+    if (check_rows(n, row_begin, row_end)) return set_err(C, MFFTB_ERR_ARG, "bad row range");
+    cudaSetDevice(C->device);
+    Plan P;
+    int rc = plan_or_err(C, n, PLAN_VALUE, 64, 64, &P);
+    if (rc) return rc;
+    Operand a{PACK_I64, A, n, 4, 64, 1, 0, 0, 0};
+    Operand b = a;
+    b.p = B;
+    OutSpec o{INV_U16, out, (long long)(row_end - row_begin) * n, n, RL, 0, 0, 2};
+    return run_product(C, P, a, b, row_begin, row_end, o);
+}
+
+int mfftgpu_conv_i32_dev(mfftgpu_ctx* C, const int32_t* A32, const int32_t* B32, int n, int L,
+                         int64_t* Cw) {
+    if (!C || !A32 || !B32 || !Cw || n <= 0 || L <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    Plan P;
+    int rc = plan_or_err(C, n, PLAN_LIMB, L, L, &P);
+    if (rc) return rc;
+    Operand a{PACK_I32LIMB, A32, n, L, 0, 1, 0, 0, 0};
+    Operand b = a;
+    b.p = B32;
+    OutSpec o{INV_I64, Cw, (long long)n * n, n, 2 * L - 1, 0, 0, 8};
+    return run_product(C, P, a, b, 0, n, o);
+}
+
+// --------------------------------------------------------------------- fp32
+int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int force_bits,
+                     float* Cout, int row_begin, int row_end) {
+    if (!C || !A || !B || !Cout || n <= 0 || force_bits < 0) return MFFTB_ERR_ARG;
+    if (check_rows(n, row_begin, row_end)) return set_err(C, MFFTB_ERR_ARG, "bad row range");
+    cudaSetDevice(C->device);
+    cudaStream_t st = C->stream;
+    const long long nn = (long long)n * n;
+    int rc;
+    if ((rc = scan_f32_launch(A, nn, C->d_scan, st))) return set_err(C, rc, "scan(A) failed");
+    if ((rc = scan_f32_launch(B, nn, C->d_scan + 3, st))) return set_err(C, rc, "scan(B) failed");
+    int h[6];
+    CUDA_OK(cudaMemcpyAsync(h, C->d_scan, sizeof h, cudaMemcpyDeviceToHost, st));
+    CUDA_OK(cudaStreamSynchronize(st));
+    const int loA = h[2] ? h[0] : 0, hiA = h[2] ? h[1] : 0, anyA = h[2];
+    const int loB = h[5] ? h[3] : 0, hiB = h[5] ? h[4] : 0, anyB = h[5];
+    // grid sizing of fpx_size (src/fpfixed.c:59-78) with sig = 24, wr = 3
+    int SA, SB, L;
+    const int spreadA = anyA ? hiA - loA : 0, spreadB = anyB ? hiB - loB : 0;
+    if (force_bits > 0) {
+        SA = SB = force_bits / 2;
+        L = next_pow2i(force_bits / 16);
+    } else {
+        SA = -loA;
+        SB = -loB;
+        int bits = std::max(24 + spreadA + 1, 24 + spreadB + 1);
+        int spread = std::max(spreadA, spreadB);
+        int need = (bits + 15) / 16, need2 = spread / 16 + 3;
+        L = next_pow2i(std::max(need, need2));
+        if (L < 2) L = 2;
+    }
+    // fpx_alloc's int64 headroom guard (src/fpfixed.c:84-88)
+    if ((double)n * L * 65535.0 * 65535.0 > 4.0e18)
+        return set_err(C, MFFTB_ERR_RANGE, "fpx: n=%d L=%d would overflow int64 accumulators", n, L);
+    // live bit windows on the grid
+    auto window = [&](int any, int lo, int hi, int S, int& lo_bit, int& width) {
+        lo_bit = 0;
+        width = 1;
+        if (!any) return;
+        int l = std::max(0, lo + S), t = std::min(16 * L, hi + S + 24);
+        if (t <= l) return;
+        lo_bit = l;
+        width = t - l;
+    };
+    int loBitA, wA, loBitB, wB;
+    window(anyA, loA, hiA, SA, loBitA, wA);
+    window(anyB, loB, hiB, SB, loBitB, wB);
+    Plan P;
+    if ((rc = plan_or_err(C, n, PLAN_VALUE, wA, wB, &P))) return rc;
+    Operand a{PACK_F32, A, n, 0, wA, 1, SA, loBitA, 16 * L - loBitA};
+    Operand b{PACK_F32, B, n, 0, wB, 1, SB, loBitB, 16 * L - loBitB};
+    OutSpec o{INV_F32, Cout, 0, n, 0, loBitA + loBitB, SA + SB, 4};
+    return run_product(C, P, a, b, row_begin, row_end, o);
+}
+
+// --------------------------------------------------------------------- host-pointer variants
+static int stage(mfftgpu_ctx* C, size_t inA, size_t inB, size_t outb, char** dA, char** dB,
+                 char** dO) {
+    size_t a = align256(inA), b = align256(inB), o = align256(outb);
+    int rc = ensure(C, &C->io, &C->io_bytes, a + b + o);
+    if (rc) return rc;
+    *dA = C->io;
+    *dB = C->io + a;
+    *dO = C->io + a + b;
+    return MFFTB_OK;
+}
+
+int mfftgpu_mm_u16(mfftgpu_ctx* C, const uint16_t* A, const uint16_t* B, int n, int L,
+                   int is_signed, uint16_t* out, int RL) {
+    if (!C || !A || !B || !out || n <= 0 || L <= 0 || RL <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const size_t in = (size_t)L * n * n * 2, ob = (size_t)RL * n * n * 2;
+    char *dA, *dB, *dO;
+    int rc = stage(C, in, in, ob, &dA, &dB, &dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
+    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
+    rc = mfftgpu_mm_u16_dev(C, (uint16_t*)dA, (uint16_t*)dB, n, L, is_signed, (uint16_t*)dO, RL, 0, n);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(out, dO, ob, cudaMemcpyDeviceToHost, C->stream));
+    return mfftgpu_sync(C);
+}
+
+int mfftgpu_mm_i64(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n, uint16_t* out,
+                   int RL) {
+    if (!C || !A || !B || !out || n <= 0 || RL <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const size_t in = (size_t)n * n * 8, ob = (size_t)RL * n * n * 2;
+    char *dA, *dB, *dO;
+    int rc = stage(C, in, in, ob, &dA, &dB, &dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
+    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
+    rc = mfftgpu_mm_i64_dev(C, (int64_t*)dA, (int64_t*)dB, n, (uint16_t*)dO, RL, 0, n);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(out, dO, ob, cudaMemcpyDeviceToHost, C->stream));
+    return mfftgpu_sync(C);
+}
+
+int mfftgpu_conv_i32(mfftgpu_ctx* C, const int32_t* A32, const int32_t* B32, int n, int L,
+                     int64_t* Cw) {
+    if (!C || !A32 || !B32 || !Cw || n <= 0 || L <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const size_t in = (size_t)L * n * n * 4, ob = (size_t)(2 * L - 1) * n * n * 8;
+    char *dA, *dB, *dO;
+    int rc = stage(C, in, in, ob, &dA, &dB, &dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(dA, A32, in, cudaMemcpyHostToDevice, C->stream));
+    CUDA_OK(cudaMemcpyAsync(dB, B32, in, cudaMemcpyHostToDevice, C->stream));
+    rc = mfftgpu_conv_i32_dev(C, (int32_t*)dA, (int32_t*)dB, n, L, (int64_t*)dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(Cw, dO, ob, cudaMemcpyDeviceToHost, C->stream));
+    return mfftgpu_sync(C);
+}
+
+int mfftgpu_fp32(mfftgpu_ctx* C, const float* A, const float* B, int n, int force_bits,
+                 float* Cout) {
+    if (!C || !A || !B || !Cout || n <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const size_t in = (size_t)n * n * 4;
+    char *dA, *dB, *dO;
+    int rc = stage(C, in, in, in, &dA, &dB, &dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
+    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
+    rc = mfftgpu_fp32_dev(C, (float*)dA, (float*)dB, n, force_bits, (float*)dO, 0, n);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(Cout, dO, in, cudaMemcpyDeviceToHost, C->stream));
+    return mfftgpu_sync(C);
+}
+
+// --------------------------------------------------------------------- generators
+int mfftgpu_gen_bigmat_dev(mfftgpu_ctx* C, uint16_t* m, int n, int L, uint64_t seed) {
+    if (!C || !m || n <= 0 || L <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    gen_u16_kernel<<<C->num_sms * 8, 256, 0, C->stream>>>(m, (long long)n * n * L, seed);
+    CUDA_OK(cudaGetLastError());
+    return MFFTB_OK;
+}
+
+int mfftgpu_gen_int64_dev(mfftgpu_ctx* C, int64_t* x, size_t count, uint64_t seed) {
+    if (!C || !x) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    gen_i64_kernel<<<C->num_sms * 8, 256, 0, C->stream>>>(x, (long long)count, seed);
+    CUDA_OK(cudaGetLastError());
+    return MFFTB_OK;
+}
+
+int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int NB, int K,
+                               int dA, int dB, int nchunk, int block_n, long long* mismatches) {
+    if (!C || !mismatches || rows <= 0 || cols <= 0 || kdim <= 0 || cols % 16 || NB < 1 ||
+        K < 1 || dA < 1 || dB < 1 || nchunk < 1 || nchunk > K)
+        return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const int ld = (kdim + 15) / 16 * 16;
+    PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
+    const int apl = NB * dA * K, fpl = NB * dB * (2 * K - 1);
+    const size_t szA = align256((size_t)apl * rows * ld), szF = align256((size_t)fpl * cols * ld);
+    const size_t szO = align256((size_t)J.njobs * rows * cols * 4);
+    int rc = ensure(C, &C->ws, &C->ws_bytes, szA + szF + szO + 256);
+    if (rc) return rc;
+    int8_t* A = reinterpret_cast<int8_t*>(C->ws);
+    int8_t* F = A + szA;
+    int32_t* out = reinterpret_cast<int32_t*>(F + szF);
+    long long* dcnt = reinterpret_cast<long long*>(reinterpret_cast<char*>(out) + szO);
+    int* mism = C->d_err + 8;
+    // random digits in [-128, 127]: keep every class contraction inside int32
+    if ((long long)kdim * K * std::min(dA, dB) * 16384LL > 2147483647LL) return MFFTB_ERR_ARG;
+    gen_u16_kernel<<<C->num_sms * 4, 256, 0, C->stream>>>(reinterpret_cast<uint16_t*>(A),
+                                                          (long long)(szA + szF) / 2, 0x5EEDull);
+    CUDA_OK(cudaGetLastError());
+    CUDA_OK(cudaMemsetAsync(C->d_err, 0, 64, C->stream));
+    PwLaunch L{};
+    L.A = A;
+    L.lda = ld;
+    L.a_plane_bytes = (long long)rows * ld;
+    L.a_planes = apl;
+    L.F = F;
+    L.ldf = ld;
+    L.f_plane_bytes = (long long)cols * ld;
+    L.f_planes = fpl;
+    L.rows = rows;
+    L.cols = cols;
+    L.kdim = kdim;
+    L.jobs = J;
+    L.block_n = block_n;
+    L.out = out;
+    L.out_plane = (long long)rows * cols;
+    L.ldo = cols;
+    L.err = C->d_err;
+    L.timeout_ns = C->timeout_ns;
+    L.num_sms = C->num_sms;
+    if ((rc = pointwise_launch(L, C->stream))) return set_err(C, rc, "pointwise launch failed");
+    if ((rc = pointwise_check_launch(L, mism, dcnt, C->stream))) return rc;
+    rc = mfftgpu_sync(C);
+    if (rc) return rc;
+    int h = 0;
+    CUDA_OK(cudaMemcpy(&h, mism, sizeof h, cudaMemcpyDeviceToHost));
+    *mismatches = h;
+    return MFFTB_OK;
+}
+
+int mfftgpu_selftest_timeout(mfftgpu_ctx* C, unsigned long long timeout_ns) {
+    if (!C || timeout_ns == 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const int n = 256;
+    int rc = ensure(C, &C->ws, &C->ws_bytes, (size_t)3 * n * n * 4);
+    if (rc) return rc;
+    CUDA_OK(cudaMemsetAsync(C->d_err, 0, sizeof(int), C->stream));
+    PwLaunch L{};
+    L.A = reinterpret_cast<int8_t*>(C->ws);
+    L.lda = n;
+    L.a_plane_bytes = (long long)n * n;
+    L.a_planes = 1;
+    L.F = reinterpret_cast<int8_t*>(C->ws) + (size_t)n * n;
+    L.ldf = n;
+    L.f_plane_bytes = (long long)n * n;
+    L.f_planes = 1;
+    L.rows = n;
+    L.cols = n;
+    L.kdim = n;
+    L.jobs = PwJobs{1, 1, 1, 1, 1, 1};
+    L.block_n = 256;
+    L.out = reinterpret_cast<int32_t*>(C->ws + (size_t)2 * n * n);
+    L.out_plane = (long long)n * n;
+    L.ldo = n;
+    L.err = C->d_err;
+    L.timeout_ns = timeout_ns;
+    L.num_sms = C->num_sms;
+    L.stall_producer = 1;
+    if ((rc = pointwise_launch(L, C->stream))) return rc;
+    return mfftgpu_sync(C);  // expected: MFFTGPU_ERR_TIMEOUT, context still usable
+}
+
+float mfftgpu_decode_words_f32(uint32_t* w, int nw, int bit_off, int S) {
+    return decode_words_host(w, nw, bit_off, S);
+}
+
+}  // extern "C"

@@ -1,0 +1,127 @@
+// fwd.cu -- Kernel 2a: forward MFFT transform of digit planes.
+//
+// Reference semantics: pack blocks of S digits into ring coefficients
+// 0..S-1 of Z[y]/(y^K+1) (src/mfft.c:322-336) and evaluate the block
+// polynomial at the NB points omega^j = y^(g j) (src/mfft.c:339-351 with the
+// op lists of :163-258).  Every twiddle is a signed permutation (a
+// negacyclic shift, src/roots.c:14-24), so each transformed coefficient is
+// a signed sum of one digit from each of the nc non-zero blocks:
+//
+//     Xhat_j[c] = sum_beta  s * X[beta*S + c'],   c' = (c - g j beta) mod 2K
+//                                                 (s = -1 when c' lands in [K, 2K))
+//
+// The kernel evaluates these sums directly for 4 consecutive elements per
+// thread (the digit planes of a CTA's 1024 elements stay in L1) and writes
+// each value as d signed int8 digits.  For B it writes the F stack the
+// pointwise kernel expects: F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "runtime.h"
+
+namespace mfftb {
+
+template <int DB>
+__device__ __forceinline__ void load4(const void* D, long long off, int (&v)[4]) {
+    if (DB == 1) {
+        char4 c = __ldg(reinterpret_cast<const char4*>(reinterpret_cast<const int8_t*>(D) + off));
+        v[0] = c.x;
+        v[1] = c.y;
+        v[2] = c.z;
+        v[3] = c.w;
+    } else if (DB == 2) {
+        short4 c = __ldg(reinterpret_cast<const short4*>(reinterpret_cast<const int16_t*>(D) + off));
+        v[0] = c.x;
+        v[1] = c.y;
+        v[2] = c.z;
+        v[3] = c.w;
+    } else {
+        int4 c = __ldg(reinterpret_cast<const int4*>(reinterpret_cast<const int32_t*>(D) + off));
+        v[0] = c.x;
+        v[1] = c.y;
+        v[2] = c.z;
+        v[3] = c.w;
+    }
+}
+
+__device__ __forceinline__ void store4(int8_t* p, int a, int b, int c, int d) {
+    char4 v;
+    v.x = (signed char)a;
+    v.y = (signed char)b;
+    v.z = (signed char)c;
+    v.w = (signed char)d;
+    *reinterpret_cast<char4*>(p) = v;
+}
+
+template <int DB>
+__global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
+    const long long e0 = 4 * (blockIdx.x * (long long)blockDim.x + threadIdx.x);
+    if (e0 >= a.nelem) return;
+    const int mask2K = 2 * a.K - 1;  // 2K is a power of two
+    const int nplanes_j = a.f_stack ? (2 * a.K - 1) : a.K;
+    for (int j = 0; j < a.NB; ++j) {
+        const int step = (a.g * j) & mask2K;
+        for (int c = 0; c < a.K; ++c) {
+            int x[4] = {0, 0, 0, 0};
+            int e = 0;  // g * j * beta mod 2K
+            for (int beta = 0; beta < a.nc; ++beta, e = (e + step) & mask2K) {
+                int r = (c - e) & mask2K;
+                int sgn = 1;
+                if (r >= a.K) {
+                    r -= a.K;
+                    sgn = -1;
+                }
+                if (r >= a.S) continue;
+                const int m = (beta << a.lgS) + r;
+                if (m >= a.Lb) continue;
+                int v[4];
+                load4<DB>(a.D, (long long)m * a.dplane + e0, v);
+                x[0] += sgn * v[0];
+                x[1] += sgn * v[1];
+                x[2] += sgn * v[2];
+                x[3] += sgn * v[3];
+            }
+            // d signed int8 digits: balanced 7-bit low digits, top digit rest
+            for (int dd = 0; dd < a.d; ++dd) {
+                int dg[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if (dd < a.d - 1) {
+                        int lo = ((x[q] + 64) & 127) - 64;
+                        dg[q] = lo;
+                        x[q] = (x[q] - lo) >> 7;
+                    } else {
+                        dg[q] = x[q];
+                    }
+                }
+                if (!a.f_stack) {
+                    long long plane = ((long long)j * a.d + dd) * nplanes_j + c;
+                    store4(a.out + plane * a.oplane + e0, dg[0], dg[1], dg[2], dg[3]);
+                } else {
+                    long long base = ((long long)j * a.d + dd) * nplanes_j;
+                    store4(a.out + (base + (a.K - 1 - c)) * a.oplane + e0, dg[0], dg[1], dg[2],
+                           dg[3]);
+                    if (c >= 1)
+                        store4(a.out + (base + (2 * a.K - 1 - c)) * a.oplane + e0, -dg[0], -dg[1],
+                               -dg[2], -dg[3]);
+                }
+            }
+        }
+    }
+}
+
+int forward_launch(const FwdArgs& a, cudaStream_t stream) {
+    if (a.nelem % 4 || a.d < 1 || a.d > 4) return MFFTB_ERR_ARG;
+    const int threads = 256;
+    long long blocks = (a.nelem / 4 + threads - 1) / threads;
+    if (blocks <= 0) return MFFTB_OK;
+    if ((1 << a.lgS) != a.S || (1 << a.lgK) != a.K) return MFFTB_ERR_ARG;
+    if (a.dbytes == 1) forward_kernel<1><<<(unsigned)blocks, threads, 0, stream>>>(a);
+    else if (a.dbytes == 2) forward_kernel<2><<<(unsigned)blocks, threads, 0, stream>>>(a);
+    else forward_kernel<4><<<(unsigned)blocks, threads, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+}  // namespace mfftb

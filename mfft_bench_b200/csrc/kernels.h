@@ -1,0 +1,87 @@
+// kernels.h -- argument blocks and launchers of the HBM-bound kernels
+// (pack, forward transform, inverse transform + fold + carry, fp32 scan).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mfftb {
+
+enum PackFmt {
+    PACK_U16PL = 0,    // uint16 limb planes [L16][n][n] (unsigned or two's complement)
+    PACK_I64 = 1,      // int64 row-major [n][n]
+    PACK_F32 = 2,      // fp32 row-major [n][n] on a fixed-point grid
+    PACK_I32LIMB = 3,  // int32 limb planes [L][n][n], limbs are the digits (conv_mfft)
+};
+
+struct PackArgs {
+    int fmt;
+    const void* src;
+    int n;             // source matrix dimension
+    int row0;          // first source row (straight layout; row-block sharding)
+    int L16;           // PACK_U16PL / PACK_I32LIMB: limb planes in the source
+    int W;             // two's complement / magnitude width of integer entries
+    int is_signed;
+    int S_grid;        // PACK_F32: grid scale SA or SB
+    int lo_bit;        // PACK_F32: first live bit of the window on the grid
+    int trunc_rel;     // PACK_F32: 16*L_grid - lo_bit (bits at/above the grid top are dropped)
+    int b;             // digit bits
+    int Lb;            // digit planes to produce
+    void* dst;         // int8 (or int32 for PACK_I32LIMB) planes [Lb][rows][ld]
+    int rows, ld;      // output plane geometry
+    long long plane;   // elements per output plane
+    int transpose;     // 1: output row = source column
+    int* err;
+};
+int pack_launch(const PackArgs& a, cudaStream_t stream);
+
+struct FwdArgs {
+    const void* D;     // digit planes [Lb][..]: int8, int16 or int32 (dbytes 1, 2, 4)
+    int dbytes;
+    long long dplane;  // elements per digit plane
+    int Lb;
+    long long nelem;   // elements per plane to transform (rows * ld), multiple of 4
+    int S, NB, K, g, nc, d;
+    int lgS, lgK;      // log2 of S and K (all plan sizes are powers of two)
+    int f_stack;       // 0: write Ahat [j][da][c]; 1: write F [j][db][r] (2K-1 planes)
+    int8_t* out;
+    long long oplane;  // bytes per output plane
+    int* err;
+};
+int forward_launch(const FwdArgs& a, cudaStream_t stream);
+
+enum InvOut {
+    INV_U16 = 0,   // normalised two's complement 16-bit limb planes [RL][rows][ldo]
+    INV_I64 = 1,   // unnormalised int64 limb-convolution planes [P][rows][ldo] (limb mode)
+    INV_F32 = 2,   // fp32 [rows][ldo], rounded once (fpx_decode_f32 semantics)
+};
+
+struct InvArgs {
+    const int32_t* acc;   // [njobs][rows][lda] int32 job planes of the pointwise step
+    long long acc_plane;
+    int lda;
+    int rows, cols;       // valid output rows / columns
+    int S, NB, K, g, nW, nchunk;
+    int log2NB, lgS, lgK, lgE;
+    int b;                // radix bits of the output positions
+    int positions;        // radix-2^b positions to fold and carry
+    int out_kind;
+    void* out;
+    long long out_plane;  // elements between output planes
+    int ldo;
+    int RL;               // INV_U16: limbs to emit; INV_I64: planes to emit
+    int bit_off;          // INV_F32: true grid position of internal bit 0
+    int S_scale;          // INV_F32: SA + SB
+    int elems;            // elements per CTA (power of two, <= 32)
+    int* err;
+};
+int inverse_launch(const InvArgs& a, cudaStream_t stream);
+
+// fp32 exponent scan of src/fpfixed.c:40-54: out[0] = min e2, out[1] = max e2,
+// out[2] = any finite non-zero (e2 = frexp exponent - 24).
+int scan_f32_launch(const float* X, long long count, int* out3, cudaStream_t stream);
+
+// test-only host entry: the device decode rule run on the CPU
+float decode_words_host(uint32_t* w, int nw, int bit_off, int S);
+
+}  // namespace mfftb

@@ -1,0 +1,197 @@
+// pack.cu -- Kernel 1: split matrix entries into signed digit planes.
+//
+// Reference semantics: the entry-to-limb-plane layout of src/mfftbench.h:74-82
+// (plane-major, limbs LSB first), the widening in mm_mfft (src/mfft.c:433-434),
+// the signed limb convention and the fp32 grid encoding of src/fpfixed.c:
+// 175-193.  The B200 path re-radixes every entry into b-bit digits (b <= 8)
+// so a transformed coefficient fits a small number of int8 tensor-core
+// digits:
+//   * integers (u16 limb planes, int64): digit m is the bit field
+//     [m*b, m*b+b) of the two's complement value; the top digit is
+//     sign-extended, all others are unsigned.  Local bit extraction, no carry
+//     chain, identical value.
+//   * fp32: digit m of |x| * 2^(off - lo_bit) (the entry's position on the
+//     fixed-point grid relative to the live window), times sign(x).
+//   * limb mode (conv_mfft): the caller's int32 limbs are the digits.
+// Output planes are [Lb][rows][ld] (row r of the operand, contraction index
+// contiguous), int8 for b <= 7 and int16 for wider digits.  B is written transposed (row = output column) so both GEMM
+// operands are K-major.  Rows/columns beyond n are zero.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "runtime.h"
+
+namespace mfftb {
+
+// ---------------------------------------------------------------- digit of one entry
+__device__ __forceinline__ int digit_u16pl(const uint16_t* src, long long nn, long long idx, int L,
+                                           int m, int b, int W, int is_signed) {
+    const int p = m * b;
+    const int u = p >> 4, sh = p & 15;
+    const uint32_t lo = u < L ? __ldg(src + (long long)u * nn + idx) : 0u;
+    const uint32_t hi = (u + 1) < L ? __ldg(src + (long long)(u + 1) * nn + idx) : 0u;
+    const uint32_t v = ((hi << 16) | lo) >> sh;
+    if (is_signed && p + b >= W) {
+        // top digit: bits [p, W) sign-extended (W - p is in [1, b])
+        const int keep = W - p;
+        return (int32_t)(v << (32 - keep)) >> (32 - keep);
+    }
+    return (int)(v & ((1u << b) - 1u));
+}
+
+__device__ __forceinline__ int digit_f32(float x, int m, int b, int S_grid, int lo_bit,
+                                         int trunc_rel) {
+    if (x == 0.0f || !isfinite(x)) return 0;
+    int e;
+    float mf = frexpf(x, &e);
+    uint32_t mi = (uint32_t)(fabsf(mf) * 16777216.0f);
+    int off = e - 24 + S_grid;
+    if (off < 0) return 0;                // below the grid (src/fpfixed.c:184)
+    const int rel = off - lo_bit;         // >= 0 by construction of lo_bit
+    const int p = m * b;
+    int lim = trunc_rel - p;              // bits of this digit inside the grid
+    if (lim <= 0) return 0;
+    uint64_t field;
+    if (p >= rel) {
+        int s = p - rel;
+        field = s >= 24 ? 0 : ((uint64_t)mi >> s);
+    } else {
+        int s = rel - p;
+        field = s >= b ? 0 : ((uint64_t)mi << s);
+    }
+    uint32_t mask = lim >= b ? ((1u << b) - 1u) : ((1u << lim) - 1u);
+    int d = (int)(field & mask);
+    return x < 0.0f ? -d : d;
+}
+
+template <int FMT>
+__device__ __forceinline__ int entry_digit(const PackArgs& a, int i, int j, int m) {
+    if (i < 0 || i >= a.n || j >= a.n) return 0;
+    const long long idx = (long long)i * a.n + j;
+    if (FMT == PACK_U16PL) {
+        return digit_u16pl(reinterpret_cast<const uint16_t*>(a.src), (long long)a.n * a.n, idx,
+                           a.L16, m, a.b, a.W, a.is_signed);
+    } else if (FMT == PACK_I64) {
+        int64_t x = __ldg(reinterpret_cast<const long long*>(a.src) + idx);
+        const int p = m * a.b;
+        if (p + a.b >= a.W) {
+            // top digit: bits [p, W) sign-extended (W <= 64)
+            int64_t t = (int64_t)((uint64_t)x << (64 - a.W)) >> (64 - a.W);
+            return (int)(t >> p);
+        }
+        return (int)(((uint64_t)x >> p) & ((1u << a.b) - 1u));
+    } else {
+        float x = __ldg(reinterpret_cast<const float*>(a.src) + idx);
+        return digit_f32(x, m, a.b, a.S_grid, a.lo_bit, a.trunc_rel);
+    }
+}
+
+// 32x32 element tile, PACK_MCH digit planes per block.  Straight: out row =
+// source row.  Transposed: out row = source column (B^T for the GEMM).
+constexpr int PACK_MCH = 8;
+
+template <int FMT, bool TRANSPOSE, typename OT>
+__global__ void __launch_bounds__(256) pack_digits_kernel(const PackArgs a) {
+    __shared__ OT tile[PACK_MCH][32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;     // output tile origin
+    const int m0 = blockIdx.z * PACK_MCH;
+    const int mcount = a.Lb - m0 < PACK_MCH ? a.Lb - m0 : PACK_MCH;
+    OT* out = reinterpret_cast<OT*>(a.dst);
+    if (!TRANSPOSE) {
+        for (int q = 0; q < 4; ++q) {
+            const int r = r0 + ty + 8 * q, c = c0 + tx;
+            if (r >= a.rows || c >= a.ld) continue;
+            for (int mm = 0; mm < mcount; ++mm) {
+                int d = entry_digit<FMT>(a, a.row0 + r, c, m0 + mm);
+                out[(long long)(m0 + mm) * a.plane + (long long)r * a.ld + c] = (OT)d;
+            }
+        }
+    } else {
+        // source element (i = c0 + ty + 8q [contraction index k], j = r0 + tx [output column])
+        for (int q = 0; q < 4; ++q) {
+            const int i = c0 + ty + 8 * q, j = r0 + tx;
+            for (int mm = 0; mm < mcount; ++mm)
+                tile[mm][ty + 8 * q][tx] = (OT)entry_digit<FMT>(a, i, j, m0 + mm);
+        }
+        __syncthreads();
+        for (int q = 0; q < 4; ++q) {
+            const int r = r0 + ty + 8 * q, c = c0 + tx;  // out row = j, out col = i
+            if (r >= a.rows || c >= a.ld) continue;
+            for (int mm = 0; mm < mcount; ++mm)
+                out[(long long)(m0 + mm) * a.plane + (long long)r * a.ld + c] = tile[mm][tx][ty + 8 * q];
+        }
+    }
+}
+
+// Limb mode: int32 limb planes [L][n][n] -> int32 digit planes, range-checked
+// (|limb| <= 65535 is the documented input contract of conv_mfft).
+template <bool TRANSPOSE>
+__global__ void __launch_bounds__(256) pack_limbs_kernel(const PackArgs a) {
+    __shared__ int32_t tile[32][33];
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32, m = blockIdx.z;
+    const int32_t* src = reinterpret_cast<const int32_t*>(a.src) + (long long)m * a.n * a.n;
+    int32_t* out = reinterpret_cast<int32_t*>(a.dst) + (long long)m * a.plane;
+    bool bad = false;
+    if (!TRANSPOSE) {
+        for (int q = 0; q < 4; ++q) {
+            const int r = r0 + ty + 8 * q, c = c0 + tx;
+            if (r >= a.rows || c >= a.ld) continue;
+            const int i = a.row0 + r;
+            int32_t v = (i < a.n && c < a.n) ? __ldg(src + (long long)i * a.n + c) : 0;
+            if (v > 65535 || v < -65535) bad = true;
+            out[(long long)r * a.ld + c] = v;
+        }
+    } else {
+        for (int q = 0; q < 4; ++q) {
+            const int i = c0 + ty + 8 * q, j = r0 + tx;
+            int32_t v = (i < a.n && j < a.n) ? __ldg(src + (long long)i * a.n + j) : 0;
+            if (v > 65535 || v < -65535) bad = true;
+            tile[ty + 8 * q][tx] = v;
+        }
+        __syncthreads();
+        for (int q = 0; q < 4; ++q) {
+            const int r = r0 + ty + 8 * q, c = c0 + tx;
+            if (r >= a.rows || c >= a.ld) continue;
+            out[(long long)r * a.ld + c] = tile[tx][ty + 8 * q];
+        }
+    }
+    if (bad) atomicCAS(a.err, 0, MFFTB_ERR_RANGE);
+}
+
+int pack_launch(const PackArgs& a, cudaStream_t stream) {
+    if (a.ld % 16 || a.rows <= 0 || a.Lb <= 0 || a.b < 1 || (a.b > 15 && a.fmt != PACK_I32LIMB))
+        return MFFTB_ERR_ARG;
+    dim3 block(256);
+    if (a.fmt == PACK_I32LIMB) {
+        dim3 grid((a.ld + 31) / 32, (a.rows + 31) / 32, a.Lb);
+        if (a.transpose) pack_limbs_kernel<true><<<grid, block, 0, stream>>>(a);
+        else pack_limbs_kernel<false><<<grid, block, 0, stream>>>(a);
+    } else {
+        dim3 grid((a.ld + 31) / 32, (a.rows + 31) / 32, (a.Lb + PACK_MCH - 1) / PACK_MCH);
+#define MFFTB_PACK(F)                                                                       \
+    if (a.b <= 7) {                                                                         \
+        if (a.transpose) pack_digits_kernel<F, true, int8_t><<<grid, block, 0, stream>>>(a);  \
+        else pack_digits_kernel<F, false, int8_t><<<grid, block, 0, stream>>>(a);             \
+    } else {                                                                                \
+        if (a.transpose) pack_digits_kernel<F, true, int16_t><<<grid, block, 0, stream>>>(a); \
+        else pack_digits_kernel<F, false, int16_t><<<grid, block, 0, stream>>>(a);            \
+    }
+        if (a.fmt == PACK_U16PL) {
+            MFFTB_PACK(PACK_U16PL)
+        } else if (a.fmt == PACK_I64) {
+            MFFTB_PACK(PACK_I64)
+        } else if (a.fmt == PACK_F32) {
+            MFFTB_PACK(PACK_F32)
+        } else {
+            return MFFTB_ERR_ARG;
+        }
+#undef MFFTB_PACK
+    }
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+}  // namespace mfftb

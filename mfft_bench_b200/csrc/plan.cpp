@@ -1,0 +1,132 @@
+// plan.cpp -- exact-plan search; see plan.h.
+#include "plan.h"
+
+#include <cmath>
+#include <cstring>
+
+namespace mfftb {
+
+static int next_pow2(int x) {
+    int r = 1;
+    while (r < x) r <<= 1;
+    return r;
+}
+
+// Split |x| <= M into d signed digits: d-1 balanced low digits in [-64, 63]
+// and a top digit; returns d (0 if more than 4 would be needed) and the
+// per-digit magnitude bounds.
+static int split_bounds(long long M, int bounds[4]) {
+    for (int d = 1; d <= 4; ++d) {
+        long long T = M;
+        for (int i = 0; i < d - 1; ++i) {
+            bounds[i] = (int)(T < 64 ? T : 64);
+            T = (T + 64) / 128;
+        }
+        if (T <= 127) {
+            bounds[d - 1] = (int)T;
+            for (int i = d; i < 4; ++i) bounds[i] = 0;
+            return d;
+        }
+    }
+    return 0;
+}
+
+static bool fill(Plan& p) {
+    const long long dmax = p.mode == PLAN_LIMB ? 65535 : (1LL << p.b) - 1;
+    p.ncA = (p.LbA + p.S - 1) / p.S;
+    p.ncB = (p.LbB + p.S - 1) / p.S;
+    p.NB = next_pow2(p.ncA + p.ncB);
+    if (p.NB < 2) p.NB = 2;
+    p.K = 2 * p.S;
+    if ((2 * p.K) % p.NB) return false;
+    p.g = 2 * p.K / p.NB;
+    const long long MA = p.ncA * dmax, MB = p.ncB * dmax;
+    p.dA = split_bounds(MA, p.boundA);
+    p.dB = split_bounds(MB, p.boundB);
+    if (!p.dA || !p.dB) return false;
+    p.nW = p.dA + p.dB - 1;
+    // int32 accumulator: a chunk of one class holds at most ceil(total/nchunk)
+    // segments, each a length-n contraction of two digit planes.
+    const long long lim = 2147483647LL;
+    int nchunk = 0;
+    for (int c = 1; c <= p.K && !nchunk; ++c) {
+        bool ok = true;
+        long long worst = 0;
+        for (int w = 0; w < p.nW && ok; ++w) {
+            int lo = w - (p.dB - 1) > 0 ? w - (p.dB - 1) : 0;
+            int hi = w < p.dA - 1 ? w : p.dA - 1;
+            int total = (hi - lo + 1) * p.K;
+            long long segmax = 0;
+            for (int da = lo; da <= hi; ++da) {
+                long long s = (long long)p.n_int * p.boundA[da] * p.boundB[w - da];
+                if (s > segmax) segmax = s;
+            }
+            long long per = (total + c - 1) / c;
+            long long bnd = per * segmax;
+            if (bnd > lim) ok = false;
+            if (bnd > worst) worst = bnd;
+        }
+        if (ok) {
+            nchunk = c;
+            p.acc_bound = worst;
+        }
+    }
+    if (!nchunk) return false;
+    p.nchunk = nchunk;
+    p.njobs = p.NB * p.K * p.nW * p.nchunk;
+    // inverse transform: |Chat| <= K * n * MA * MB, summed over NB points
+    p.inv_bound_log2 = std::log2((double)p.NB) + std::log2((double)p.K) +
+                       std::log2((double)p.n_int) + std::log2((double)MA) +
+                       std::log2((double)MB) + 1.0;
+    if (p.inv_bound_log2 > 62.0) return false;
+    p.positions = p.LbA + p.LbB - 1;
+    p.macs_per_elem = (double)p.NB * p.K * p.K * p.dA * p.dB * p.n_int;
+    return true;
+}
+
+static bool better(const Plan& a, const Plan& b) {
+    if (a.macs_per_elem != b.macs_per_elem) return a.macs_per_elem < b.macs_per_elem;
+    if (a.njobs != b.njobs) return a.njobs < b.njobs;
+    return a.NB * (2 * a.K - 1) * a.dB < b.NB * (2 * b.K - 1) * b.dB;
+}
+
+int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan* out) {
+    if (n <= 0 || wA <= 0 || wB <= 0 || !out) return 1;
+    Plan best;
+    bool have = false;
+    // value-mode digit planes are int8 for b <= 7 and int16 up to b = 15 (they
+    // feed only the forward transform; the tensor-core operands are the
+    // split transformed planes, always int8)
+    int b_lo = 2, b_hi = 15;
+    if (mode == PLAN_LIMB) b_lo = b_hi = 16;
+    else if (force_b > 0) {
+        if (force_b > 15) return 1;
+        b_lo = b_hi = force_b;
+    }
+    for (int b = b_lo; b <= b_hi; ++b) {
+        for (int sigma = 0; sigma <= 13; ++sigma) {
+            int S = 1 << sigma;
+            if (force_S > 0 && S != force_S) continue;
+            Plan p;
+            std::memset(&p, 0, sizeof p);
+            p.n = n;
+            p.n_int = (n + 15) / 16 * 16;
+            p.mode = mode;
+            p.b = b;
+            p.LbA = mode == PLAN_LIMB ? wA : (wA + b - 1) / b;
+            p.LbB = mode == PLAN_LIMB ? wB : (wB + b - 1) / b;
+            p.S = S;
+            if (S > 2 * (p.LbA > p.LbB ? p.LbA : p.LbB) && S > 1) continue;
+            if (!fill(p)) continue;
+            if (!have || better(p, best)) {
+                best = p;
+                have = true;
+            }
+        }
+    }
+    if (!have) return 2;
+    *out = best;
+    return 0;
+}
+
+}  // namespace mfftb

@@ -1,0 +1,50 @@
+// plan.h -- MFFT plan for the B200 path: limb radix, block size, transform
+// length, int8 digit split of the transformed planes and contraction chunks.
+//
+// The reference plans a fixed 16-bit limb radix with S = 2^floor(log2(L)/2)
+// (src/mfft.c:77-95) and multiplies transformed planes as int32 x int32 ->
+// int64 on CPU cores.  Here every product must run on tcgen05 kind::i8, so
+// the planner searches the limb radix b, the block size S and the int8 digit
+// split jointly, minimising issued int8 MACs subject to exactness:
+//   * every transformed coefficient (a signed sum of nc digits) is split
+//     into d signed int8 digits (balanced 7-bit low digits, top digit <=127);
+//   * every int32 TMEM accumulator stays below 2^31 (chunked contraction);
+//   * the inverse transform stays below 2^62 in int64.
+// Exactness never depends on the plan; only speed does.
+#pragma once
+#include <cstdint>
+
+namespace mfftb {
+
+enum PlanMode {
+    PLAN_VALUE = 0,  // entries re-radixed into b-bit digits of |x| (sign applied)
+    PLAN_LIMB = 1,   // the caller's 16-bit limbs are the coefficients (conv_mfft)
+};
+
+struct Plan {
+    int n;          // matrix dimension
+    int n_int;      // internal dimension: n rounded up to a multiple of 16
+    int mode;       // PlanMode
+    int b;          // digit bits (16 in PLAN_LIMB)
+    int LbA, LbB;   // digits (coefficients) per entry of A / B
+    int S, NB, K, g;
+    int ncA, ncB;   // nonzero input blocks of A / B
+    int dA, dB;     // int8 digits per transformed value
+    int nW;         // digit-weight classes dA + dB - 1
+    int nchunk;     // contraction chunks per job
+    int njobs;      // NB * K * nW * nchunk
+    int boundA[4], boundB[4];  // |digit| bounds of the split transformed values
+    int positions;  // radix-2^b output positions produced (LbA + LbB - 1)
+    long long acc_bound;       // worst int32 accumulator magnitude
+    double inv_bound_log2;     // log2 of the worst inverse-transform magnitude
+    double macs_per_elem;      // int8 MACs per output element = NB*K*K*dA*dB*n
+};
+
+// Returns 0 and fills *p on success.  wA / wB: magnitude bits per entry in
+// PLAN_VALUE, limb counts in PLAN_LIMB.  force_b > 0 pins the digit width
+// (PLAN_VALUE only); force_S > 0 pins the block size.
+// Bytes per element of the digit planes the pack kernel writes.
+inline int plan_digit_bytes(const Plan& p) { return p.mode == PLAN_LIMB ? 4 : (p.b <= 7 ? 1 : 2); }
+int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan* p);
+
+}  // namespace mfftb

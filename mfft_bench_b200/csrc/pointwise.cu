@@ -88,7 +88,10 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
         int issued_parity[PW_STAGES];
         for (int s = 0; s < PW_STAGES; ++s) issued_parity[s] = -1;
         const uint32_t tx_bytes = PW_A_STAGE_BYTES + p.block_n * PW_BK;
-        for (long long tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+        // stall_producer: nothing is ever loaded, so every consumer wait must
+        // run into its deadline and the kernel must still end cleanly
+        const long long first_tile = p.stall_producer ? p.num_tiles : (long long)blockIdx.x;
+        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
             int q, mt, nt, j, t, w, ch, s0, s1;
             pw_tile_decode(p, tile, q, mt, nt);
             pw_job_decode(p.jobs, q, j, t, w, ch);
@@ -274,6 +277,7 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     p.ldo = L.ldo;
     p.err = L.err;
     p.timeout_ns = L.timeout_ns;
+    p.stall_producer = L.stall_producer;
 
     CUtensorMap tmA, tmF;
     int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);

@@ -60,6 +60,7 @@ struct PwParams {
     int ldo;           // output row stride (elements)
     int* err;          // device status word (0 = ok)
     unsigned long long timeout_ns;
+    int stall_producer;  // self-test of the bounded waits: the producer issues nothing
 };
 
 // Segment s of job q: which A plane and which F plane feed it.  Shared by

@@ -39,6 +39,7 @@ struct PwLaunch {
     int* err;
     unsigned long long timeout_ns;
     int num_sms;
+    int stall_producer;       // self-test only: see PwParams
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

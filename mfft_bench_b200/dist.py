@@ -1,0 +1,83 @@
+"""Row-block sharding of one exact product across GPUs (one process per GPU).
+
+C's row block r depends only on A's row block r and all of B, so rank r owns
+rows [r0, r1) of A and C.  The exchange steps are the only collectives:
+
+1. B is all-gathered from the row blocks each rank holds (raw entries: for
+   the 64-bit configuration that is 8 bytes per entry, the smallest form B
+   takes anywhere on the path -- its int8 digit planes are 16 B/entry and the
+   transformed F stack 120 B/entry), then every rank packs and transforms B
+   locally;
+2. C's row blocks are gathered to rank 0 plane by plane with grouped
+   point-to-point transfers, straight into the plane-major [RL][n][n]
+   layout of the reference (no gather primitive, no re-layout pass).
+
+The helpers work on any torch.distributed backend (NCCL on GPUs, gloo on
+CPU tensors in the tests).
+"""
+from __future__ import annotations
+
+
+def row_range(n: int, world: int, rank: int, align: int = 128):
+    """Balanced split of n rows into world blocks, boundaries on `align`
+    multiples where possible (whole tcgen05 row tiles per rank)."""
+    if world <= 0 or not (0 <= rank < world):
+        raise ValueError("bad world/rank")
+    units = (n + align - 1) // align
+    lo = units * rank // world
+    hi = units * (rank + 1) // world
+    return min(n, lo * align), min(n, hi * align)
+
+
+def all_ranges(n: int, world: int, align: int = 128):
+    return [row_range(n, world, r, align) for r in range(world)]
+
+
+def allgather_rows(local, full, n_cols: int, ranges, group=None):
+    """Gather row blocks (row-major, n_cols per row) of every rank into
+    `full` on every rank.  Unequal blocks are handled with one broadcast per
+    rank from its own slice."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    sizes = {(r1 - r0) for r0, r1 in ranges}
+    r0, r1 = ranges[rank]
+    if len(sizes) == 1:
+        dist.all_gather_into_tensor(full.view(-1), local.view(-1), group=group)
+        return full
+    full.view(-1)[r0 * n_cols:r1 * n_cols].copy_(local.view(-1))
+    for src in range(world):
+        a, b = ranges[src]
+        if b > a:
+            dist.broadcast(full.view(-1)[a * n_cols:b * n_cols], src=src, group=group)
+    return full
+
+
+def gather_planes_to_root(local, full, n: int, RL: int, ranges, group=None, root: int = 0):
+    """local: [RL][rows_r][n] output rows of this rank (flat).  On the root,
+    full: [RL][n][n] (flat) receives every rank's rows plane by plane."""
+    import torch.distributed as dist
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    r0, r1 = ranges[rank]
+    rows = r1 - r0
+    lv = local.view(RL, rows, n) if rows else None
+    ops = []
+    if rank == root:
+        fv = full.view(RL, n, n)
+        if rows:
+            fv[:, r0:r1, :].copy_(lv)
+        for src in range(world):
+            a, b = ranges[src]
+            if src == root or b <= a:
+                continue
+            for w in range(RL):
+                ops.append(dist.P2POp(dist.irecv, fv[w, a:b, :], src, group=group))
+    elif rows:
+        for w in range(RL):
+            ops.append(dist.P2POp(dist.isend, lv[w].contiguous() if not lv[w].is_contiguous()
+                                  else lv[w], root, group=group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    return full

@@ -1,0 +1,215 @@
+"""C-ABI and host-logic tests that need no GPU.
+
+* the library loads and exports every symbol include/*.h declares;
+* reference-compatible host helpers (mfft_plan_init, bigmat_rand,
+  normalize_planes, fpx_decode_f32) behave like the reference;
+* the int8 planner's exactness invariants hold over a sweep of shapes;
+* the fp32 rounding rule shared with the device matches the oracle,
+  including ties, sticky bits, subnormal results and overflow;
+* without a GPU every product entry point returns a status, never crashes.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import mfft_bench_b200 as m
+from mfft_bench_b200 import _lib
+
+
+def test_exports_every_declared_symbol():
+    names = _lib.declared_functions()
+    assert len(names) > 40
+    missing = [s for s in names if not hasattr(_lib.lib, s)]
+    assert not missing, missing
+
+
+def test_product_library_is_not_the_oracle():
+    import os
+    assert os.path.basename(m.LIB_PATH) == "libmfftb200.so"
+    assert not hasattr(_lib.lib, "orc_conv_mfft")
+
+
+def test_plan_init_semantics(oracle):
+    for L in range(1, 80):
+        for sigma in range(0, 9):
+            p = m.mfft_plan_init(L, sigma)
+            q = oracle.plan(L, sigma)
+            assert (p is None) == (q is None), (L, sigma)
+            if p is not None:
+                assert (p.S, p.NB, p.K, p.g, p.nprod, p.rec) == (q.S, q.NB, q.K, q.g, q.nprod, 0)
+
+
+def test_bigmat_rand_matches_reference_stream(oracle):
+    for n, L, seed in ((5, 3, 12345), (16, 64, 12345 ^ 0xABCDEF), (1, 1, 0)):
+        assert np.array_equal(m.bigmat_rand(n, L, seed), oracle.bigmat_rand(n, L, seed))
+
+
+def test_normalize_planes_matches_reference(oracle):
+    rng = np.random.default_rng(0)
+    n = 9
+    for P, RL in ((1, 3), (7, 9), (15, 33), (15, 4)):
+        acc = rng.integers(-(1 << 50), 1 << 50, P * n * n, dtype=np.int64)
+        assert np.array_equal(m.normalize_planes(acc, P, n, RL),
+                              oracle.normalize_planes(acc, P, n, RL))
+
+
+def test_kernel_names():
+    assert _lib.lib.kernel_name(2) == b"packed"
+    assert _lib.lib.kernel_name(12) == b"sm100"
+    assert _lib.lib.kernel_from_name(b"sm100") == 12
+    assert _lib.lib.kernel_from_name(b"nope") == -1
+
+
+# ---------------------------------------------------------------- planner invariants
+def _split_ok(M, d, bounds):
+    """Brute-force the digit split of every |x| <= M at the extremes."""
+    for x in (M, -M, M - 1, -(M - 1), 0, 64, -64, 63, -65, 8191, -8191):
+        if abs(x) > M:
+            continue
+        v = x
+        for i in range(d):
+            if i < d - 1:
+                lo = ((v + 64) & 127) - 64
+                if abs(lo) > bounds[i]:
+                    return False
+                v = (v - lo) >> 7
+            else:
+                if abs(v) > bounds[i] or abs(v) > 127:
+                    return False
+    return True
+
+
+@pytest.mark.parametrize("n", [1, 16, 64, 200, 1024, 4096, 16384])
+@pytest.mark.parametrize("mode,w", [(0, 8), (0, 64), (0, 256), (0, 1024), (0, 8192), (0, 68),
+                                    (1, 1), (1, 4), (1, 16), (1, 64), (1, 512)])
+def test_plan_exactness_invariants(n, mode, w):
+    try:
+        pi = m.plan_info(n, mode, w)
+    except m.MfftError:
+        # only acceptable when no int8 plan can be exact (huge limb mode)
+        assert mode == 1 and w >= 512 and n >= 4096
+        return
+    dmax = 65535 if mode == 1 else (1 << pi["b"]) - 1
+    assert pi["acc_bound"] < 2 ** 31
+    assert pi["inv_bound_log2"] <= 62
+    assert pi["NB"] >= pi["ncA"] + pi["ncB"] and (2 * pi["K"]) % pi["NB"] == 0
+    assert pi["K"] == 2 * pi["S"]
+    if mode == 0:
+        assert pi["LbA"] * pi["b"] >= w
+    else:
+        assert pi["LbA"] == w and pi["b"] == 16
+    MA = pi["ncA"] * dmax
+    # recompute the split bounds independently
+    T, bounds = MA, []
+    for i in range(pi["dA"] - 1):
+        bounds.append(min(64, T))
+        T = (T + 64) // 128
+    bounds.append(T)
+    assert T <= 127 and _split_ok(MA, pi["dA"], bounds)
+    assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
+    assert pi["int8_macs"] == pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"] * float(pi["n_int"]) ** 3
+
+
+def test_bench_plans_are_single_digit():
+    """The bench configurations run with one int8 digit per transformed value."""
+    for n, w in ((16384, 64), (1024, 256)):
+        pi = m.plan_info(n, 0, w)
+        assert pi["dA"] == pi["dB"] == 1 and pi["nchunk"] == 1
+
+
+# ---------------------------------------------------------------- fp32 rounding rule
+def _words_from_cw(cw, nw):
+    carry, words = 0, [0] * nw
+    for k in range(2 * nw):
+        v = (int(cw[k]) if k < len(cw) else 0) + carry
+        words[k >> 1] |= (v & 0xFFFF) << (16 * (k & 1))
+        carry = v >> 16
+    return words
+
+
+def test_decode_rule_matches_oracle(oracle):
+    rng = np.random.default_rng(11)
+    L = 32
+    cases = []
+    for _ in range(3000):
+        cw = np.zeros(2 * L - 1, np.int64)
+        k = rng.integers(1, 6)
+        pos = rng.integers(0, 2 * L - 1, k)
+        for p in pos:
+            cw[p] += int(rng.integers(-(1 << 40), 1 << 40))
+        S = int(rng.integers(0, 1100))
+        cases.append((cw, S))
+    # exact ties and near-ties around the 24-bit rounding point, with and without sticky
+    for top in (0x1000001, 0x1000003, 0x1FFFFFF, 0xFFFFFF8, 0x2000001):
+        for lowbits in (0, 1, 0x8000, 0x4000):
+            cw = np.zeros(2 * L - 1, np.int64)
+            cw[3] = top
+            cw[2] = lowbits
+            for S in (100, 0, 250, 400, 900, 1030):
+                cases.append((cw.copy(), S))
+                cases.append((-cw, S))
+    cases.append((np.zeros(2 * L - 1, np.int64), 512))
+    for cw, S in cases:
+        want = np.float32(oracle.decode_f32_entry(cw, L, S))
+        got = np.float32(m.decode_words_f32(_words_from_cw(cw, 36), 0, S))
+        assert want.view(np.uint32) == got.view(np.uint32), (cw.nonzero(), S, want, got)
+
+
+def test_decode_rule_bit_offset_equivalence():
+    """Shifting the integer by 2^k and passing bit_off = k is the same number."""
+    rng = np.random.default_rng(5)
+    for _ in range(500):
+        v = int(rng.integers(1, 1 << 62)) * int(rng.integers(1, 1 << 40))
+        if rng.integers(0, 2):
+            v = -v
+        k = int(rng.integers(0, 40))
+        S = int(rng.integers(0, 300))
+        w1 = [(v << k) >> (32 * i) & 0xFFFFFFFF for i in range(6)]
+        w2 = [v >> (32 * i) & 0xFFFFFFFF for i in range(6)]
+        a = np.float32(m.decode_words_f32(w1, 0, S))
+        b = np.float32(m.decode_words_f32(w2, k, S))
+        assert a.view(np.uint32) == b.view(np.uint32)
+
+
+def test_fpx_host_decode_matches_reference(reflib):
+    """Drop-in fpx_encode / fpx_decode_f32 (host side) vs the reference's own."""
+    from mfft_bench_b200._lib import FpxCtx, lib
+    from oracle.oracle import RefFpx
+    rng = np.random.default_rng(2)
+    n = 24
+    A = (rng.standard_normal(n * n) * np.exp2(rng.integers(-30, 30, n * n))).astype(np.float32)
+    B = (rng.standard_normal(n * n)).astype(np.float32)
+    for fb in (512, 0):
+        ours, ref = FpxCtx(), RefFpx()
+        assert lib.fpx_init(C.byref(ours), A.ctypes.data, B.ctypes.data, n, fb) == 0
+        assert reflib.lib.fpx_init(C.byref(ref), A, B, n, fb) == 0
+        assert (ours.L, ours.SA, ours.SB, ours.spreadA) == (ref.L, ref.SA, ref.SB, ref.spreadA)
+        lib.fpx_encode(C.byref(ours), A.ctypes.data, B.ctypes.data)
+        reflib.lib.fpx_encode(C.byref(ref), A, B)
+        nn = n * n
+        a32 = np.ctypeslib.as_array(ours.A32, shape=(ours.L * nn,))
+        assert np.array_equal(a32, np.ctypeslib.as_array(ref.A32, shape=(ref.L * nn,)))
+        # same random Cw planes into both, decode both
+        cw = rng.integers(-(1 << 45), 1 << 45, (2 * ours.L - 1) * nn, dtype=np.int64)
+        np.ctypeslib.as_array(ours.Cw, shape=cw.shape)[:] = cw
+        np.ctypeslib.as_array(ref.Cw, shape=cw.shape)[:] = cw
+        o1 = np.empty(nn, np.float32)
+        o2 = np.empty(nn, np.float32)
+        lib.fpx_decode_f32(C.byref(ours), o1.ctypes.data)
+        reflib.lib.fpx_decode_f32(C.byref(ref), o2)
+        assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+        lib.fpx_free(C.byref(ours))
+        reflib.lib.fpx_free(C.byref(ref))
+
+
+# ---------------------------------------------------------------- no GPU: statuses, not crashes
+def test_no_device_statuses():
+    if m.device_count() > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(m.MfftError) as e:
+        m.Context(0)
+    assert e.value.status == 6  # MFFTGPU_ERR_NODEVICE
+    A = m.bigmat_rand(4, 2, 1)
+    with pytest.raises(m.MfftError):
+        m.mm_mfft(A, A, 4, 2)

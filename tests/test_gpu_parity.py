@@ -1,0 +1,177 @@
+"""GPU parity: the B200 path through its C ABI vs the reference's outputs.
+
+Bit-exact equality is required everywhere (integer path: every output limb;
+fp32 path: every output float, compared as bits).
+"""
+import numpy as np
+import pytest
+
+import mfft_bench_b200 as m
+from conftest import load_fixture
+
+pytestmark = pytest.mark.gpu
+SA, SB = 12345, 12345 ^ 0xABCDEF
+
+
+# ---------------------------------------------------------------- the tcgen05 kernel alone
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,dA,dB,nchunk,bn", [
+    (256, 256, 256, 2, 1, 1, 1, 1, 256),
+    (128, 64, 128, 1, 1, 1, 1, 1, 64),
+    (200, 208, 144, 2, 4, 2, 2, 2, 128),
+    (64, 64, 64, 4, 8, 1, 1, 1, 64),
+    (1000, 1008, 1000, 2, 4, 3, 2, 3, 256),
+    (384, 512, 520, 8, 8, 1, 1, 1, 256),
+])
+def test_pointwise_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA, dB, nchunk, bn):
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, nchunk, bn) == 0
+
+
+# ---------------------------------------------------------------- golden fixtures
+@pytest.mark.parametrize("n,L", [(8, 8), (16, 64), (48, 16)])
+def test_unsigned_fixture(ctx, n, L):
+    f = load_fixture(f"mm_mfft_u_n{n}_L{L}.npz")
+    assert np.array_equal(ctx.mm_u16(f["A"], f["B"], n, L), f["out"])
+    # the same product through the reference-named drop-in symbol
+    assert np.array_equal(m.mm_mfft(f["A"], f["B"], n, L), f["out"])
+
+
+def test_c1_digest(ctx, oracle, golden):
+    n, L = 64, 512
+    A, B = m.bigmat_rand(n, L, SA), m.bigmat_rand(n, L, SB)
+    out = ctx.mm_u16(A, B, n, L)
+    rec = next(c for c in golden["unsigned"] if c["n"] == n and c["L"] == L)
+    assert f"{oracle.digest(out):016x}" == rec["digest"]
+
+
+@pytest.mark.parametrize("n,L", [(32, 4), (64, 4), (48, 16)])
+def test_signed_fixture(ctx, n, L):
+    f = load_fixture(f"signed_n{n}_L{L}.npz")
+    assert np.array_equal(ctx.mm_u16(f["A"], f["B"], n, L, signed=True), f["out"])
+    assert np.array_equal(m.mm_mfft_signed(f["A"], f["B"], n, L), f["out"])
+    # conv_mfft: the unnormalised int64 planes, bit for bit
+    assert np.array_equal(ctx.conv_i32(f["A32"], f["B32"], n, L), f["cw"])
+    assert np.array_equal(m.conv_mfft(f["A32"], f["B32"], n, L), f["cw"])
+    if L == 4:
+        x = f["A"].reshape(4, n * n).astype(np.uint64)
+        y = f["B"].reshape(4, n * n).astype(np.uint64)
+        xa = sum(x[u] << np.uint64(16 * u) for u in range(4)).view(np.int64)
+        ya = sum(y[u] << np.uint64(16 * u) for u in range(4)).view(np.int64)
+        assert np.array_equal(ctx.mm_i64(xa, ya, n, RL=9), f["out"])
+
+
+@pytest.mark.parametrize("n,fb", [(64, 512), (64, 0), (96, 512)])
+def test_fp32_fixture(ctx, n, fb):
+    f = load_fixture(f"fp32_n{n}_w{fb}.npz")
+    got = ctx.fp32(f["A"], f["B"], n, fb)
+    assert np.array_equal(got.view(np.uint32), f["C"].view(np.uint32))
+    assert np.array_equal(m.fpx_gemm_f32(f["A"], f["B"], n, fb).view(np.uint32),
+                          f["C"].view(np.uint32))
+    # the reference's own call sequence through the drop-in symbols
+    fx = m.Fpx(f["A"], f["B"], n, fb)
+    fx.encode()
+    fx.conv()
+    out = fx.decode_f32()
+    fx.free()
+    assert np.array_equal(out.view(np.uint32), f["C"].view(np.uint32))
+
+
+# ---------------------------------------------------------------- vs the oracle, random shapes
+@pytest.mark.parametrize("n,L", [(1, 1), (1, 4), (3, 2), (17, 3), (100, 4), (128, 16), (200, 8),
+                                 (33, 64), (256, 2)])
+def test_unsigned_random(ctx, oracle, n, L):
+    A, B = oracle.bigmat_rand(n, L, 7 + n), oracle.bigmat_rand(n, L, 9 + L)
+    got = ctx.mm_u16(A, B, n, L).reshape(2 * L + 1, n, n)
+    if oracle.plan(L) is not None and n <= 128:
+        assert np.array_equal(got.ravel(), oracle.mm_mfft(A, B, n, L))
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 3000)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 3000)]
+    want = oracle.entries(A, B, n, L, False, rows, cols)
+    assert np.array_equal(got[:, rows, cols], want)
+
+
+@pytest.mark.parametrize("n,L", [(5, 1), (40, 4), (96, 16), (130, 5), (64, 32)])
+def test_signed_random(ctx, oracle, n, L):
+    A, B = oracle.signed_planes(n, L, 3 + n), oracle.signed_planes(n, L, 5 + L)
+    got = ctx.mm_u16(A, B, n, L, signed=True).reshape(2 * L + 1, n, n)
+    assert np.array_equal(got.ravel(), oracle.mm_signed(A, B, n, L)) if n <= 96 else True
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 3000)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 3000)]
+    assert np.array_equal(got[:, rows, cols], oracle.entries(A, B, n, L, True, rows, cols))
+
+
+def test_extreme_values(ctx, oracle):
+    """All-ones (max unsigned), INT64_MIN / INT64_MAX, zeros."""
+    n, L = 48, 4
+    A = np.full(L * n * n, 0xFFFF, np.uint16)
+    B = np.full(L * n * n, 0xFFFF, np.uint16)
+    assert np.array_equal(ctx.mm_u16(A, B, n, L), oracle.mm_mfft(A, B, n, L))
+    x = np.full(n * n, np.iinfo(np.int64).min, np.int64)
+    y = np.full(n * n, np.iinfo(np.int64).max, np.int64)
+    x[1::3] = np.iinfo(np.int64).max
+    y[::5] = np.iinfo(np.int64).min
+    got = ctx.mm_i64(x, y, n, RL=9)
+    want = oracle.mm_signed(oracle.int64_to_planes(x, n), oracle.int64_to_planes(y, n), n, 4)
+    assert np.array_equal(got, want)
+    z = np.zeros(L * n * n, np.uint16)
+    assert not ctx.mm_u16(z, A, n, L).any()
+
+
+@pytest.mark.parametrize("RL", [1, 3, 8, 12])
+def test_short_and_long_output(ctx, oracle, RL):
+    """RL below 2L+1 truncates mod 2^(16 RL); above it sign-extends."""
+    n, L = 32, 4
+    A, B = oracle.signed_planes(n, L, 1), oracle.signed_planes(n, L, 2)
+    full = oracle.mm_signed(A, B, n, L, RL=12)
+    got = ctx.mm_u16(A, B, n, L, signed=True, RL=RL)
+    assert np.array_equal(got, full[: RL * n * n])
+
+
+@pytest.mark.parametrize("n,L", [(8, 2), (24, 8), (16, 32), (70, 3)])
+def test_conv_mixed_sign_limbs(ctx, oracle, n, L):
+    """conv_mfft semantics on arbitrary-sign limbs in [-65535, 65535]."""
+    rng = np.random.default_rng(n * L)
+    A32 = rng.integers(-65535, 65536, L * n * n).astype(np.int32)
+    B32 = rng.integers(-65535, 65536, L * n * n).astype(np.int32)
+    assert np.array_equal(ctx.conv_i32(A32, B32, n, L), oracle.conv_limbplane(A32, B32, n, L))
+
+
+def test_fp32_random_ranges(ctx, oracle):
+    rng = np.random.default_rng(4)
+    n = 72
+    for fb, spread in ((512, 20), (0, 20), (0, 60), (128, 30), (96, 5)):
+        A = (rng.standard_normal(n * n) * np.exp2(rng.integers(-spread, spread, n * n))).astype(np.float32)
+        B = (rng.standard_normal(n * n) * np.exp2(rng.integers(-spread, spread, n * n))).astype(np.float32)
+        A[::11] = 0.0
+        B[3::7] = -0.0
+        A[5] = np.inf
+        B[9] = np.nan
+        rows = np.repeat(np.arange(n), n)
+        cols = np.tile(np.arange(n), n)
+        want = oracle.fpx_entries(A, B, n, fb, rows, cols)
+        got = ctx.fp32(A, B, n, fb)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), fb
+
+
+# ---------------------------------------------------------------- device-resident entry points
+def test_device_pointer_path_and_row_ranges(ctx, oracle):
+    import torch
+    n, L = 200, 4
+    A, B = oracle.signed_planes(n, L, 21), oracle.signed_planes(n, L, 22)
+    full = ctx.mm_u16(A, B, n, L, signed=True).reshape(9, n, n)
+    dA = torch.from_numpy(A.view(np.int16)).cuda().view(torch.uint16)
+    dB = torch.from_numpy(B.view(np.int16)).cuda().view(torch.uint16)
+    for r0, r1 in ((0, n), (0, 64), (64, 130), (130, 200), (199, 200)):
+        out = ctx.mm_u16(dA, dB, n, L, signed=True, rows=(r0, r1))
+        ctx.sync()
+        got = out.view(torch.int16).cpu().numpy().view(np.uint16).reshape(9, r1 - r0, n)
+        assert np.array_equal(got, full[:, r0:r1, :]), (r0, r1)
+
+
+def test_device_generators_match_host(ctx):
+    import torch
+    n, L = 33, 5
+    dm = torch.empty(n * n * L, dtype=torch.uint16, device="cuda")
+    ctx.gen_bigmat(dm, n, L, 12345)
+    ctx.sync()
+    assert np.array_equal(dm.view(torch.int16).cpu().numpy().view(np.uint16),
+                          m.bigmat_rand(n, L, 12345))
