@@ -118,6 +118,24 @@ int mfftgpu_fp32_dev(mfftgpu_ctx *ctx, const float *A, const float *B, int n, in
 int mfftgpu_fp32(mfftgpu_ctx *ctx, const float *A, const float *B, int n, int force_bits,
                  float *C);
 
+/* Exact product of signed 64-bit row-major matrices, like mfftgpu_mm_i64_dev,
+ * but with no device allocation at all: for callers that may not call
+ * cudaMalloc (a framework that owns all device memory through its own pool,
+ * or a latency-critical path that cannot take cudaMalloc's implicit device
+ * synchronisation).  No counterpart in the reference.
+ * A, B, out: device pointers the caller allocated (out: RL planes of n*n).
+ * Every intermediate lives in one fixed 32 MiB static device array per GPU,
+ * held by each GPU that loads the library until the process exits; n > 256
+ * does not fit and returns MFFTGPU_ERR_ARG.  The work is enqueued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream) on the current
+ * device, and the call waits for that stream to return the status of the
+ * device-side checks.  The first call on each device looks up the array's
+ * device address; make that first call before any stream capture.  All
+ * calls share the one array: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller. */
+int mfftgpu_mm_i64_noalloc(const int64_t *A, const int64_t *B, int n, uint16_t *out, int RL,
+                           void *stream);
+
 /* --- device-side input generators (bench workloads) ------------------------
  * bigmat_rand (src/bigmat.c:20-35) evaluated in parallel: draw i of the
  * splitmix64 stream from `seed` is a pure function of (seed, i). */

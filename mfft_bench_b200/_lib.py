@@ -86,6 +86,7 @@ _sig("mfftgpu_gen_bigmat_dev", i32, vp, vp, i32, i32, u64)
 _sig("mfftgpu_gen_int64_dev", i32, vp, vp, sz, u64)
 _sig("mfftgpu_selftest_timeout", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_gen_normal_f32", None, vp, vp, sz, u64)
+_sig("mfftgpu_mm_i64_noalloc", i32, vp, vp, i32, vp, i32, vp)
 _sig("mfftgpu_decode_words_f32", C.c_float, vp, i32, i32, i32)
 _sig("mfftgpu_selftest_pointwise", i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32,
      C.POINTER(C.c_longlong))

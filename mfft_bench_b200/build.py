@@ -29,7 +29,7 @@ CU_FLAGS = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra"]
 C_FLAGS = ["-O2", "-std=gnu11", "-fPIC", "-Wall", "-Wextra", "-fopenmp"]
 
-CU_SOURCES = ["pointwise.cu", "pack.cu", "fwd.cu", "inv.cu", "engine.cu"]
+CU_SOURCES = ["pointwise.cu", "pack.cu", "fwd.cu", "inv.cu", "engine.cu", "noalloc.cu"]
 CXX_SOURCES = ["plan.cpp"]
 C_SOURCES = ["refapi.c"]
 
