@@ -217,7 +217,12 @@ def reference_line(args):
 
 # ---------------------------------------------------------------------------- B200 arm
 class Workload:
-    """Device-resident inputs and one exact product per step."""
+    """Device-resident inputs and one exact product per step.
+
+    With world > 1, rank r owns rows [r0, r1) of A, B and C (row-block
+    sharding).  Each step all-gathers B from the ranks' row blocks, computes
+    this rank's rows of C, and gathers C's rows to rank 0 in the reference's
+    plane-major layout."""
 
     def __init__(self, name, ctx, torch, rank, world, device):
         from mfft_bench_b200 import dist as D
@@ -230,45 +235,54 @@ class Workload:
         self.rows = self.r1 - self.r0
         dev = device
         if w["kind"] == "i64":
-            self.RL = 9
-            full_A = torch.empty(n * n, dtype=torch.int64, device=dev)
-            ctx.gen_int64(full_A, SEED_A)
-            self.B_local = torch.empty(self.rows * n, dtype=torch.int64, device=dev)
-            full_B = torch.empty(n * n, dtype=torch.int64, device=dev)
-            ctx.gen_int64(full_B, SEED_B)
-            self.bytes_in = 8
+            self.RL, self.planes, self.bytes_in = 9, 1, 8
+            A = torch.empty(n * n, dtype=torch.int64, device=dev)
+            B = torch.empty(n * n, dtype=torch.int64, device=dev)
+            ctx.gen_int64(A, SEED_A)
+            ctx.gen_int64(B, SEED_B)
         elif w["kind"] == "u16":
             L = w["L"]
-            self.RL = RL_OF(L)
-            full_A = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
-            full_B = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
-            ctx.gen_bigmat(full_A, n, L, SEED_A)
-            ctx.gen_bigmat(full_B, n, L, SEED_B)
-            self.bytes_in = 2 * L
+            self.RL, self.planes, self.bytes_in = RL_OF(L), L, 2 * L
+            A = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
+            B = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
+            ctx.gen_bigmat(A, n, L, SEED_A)
+            ctx.gen_bigmat(B, n, L, SEED_B)
         else:
             from mfft_bench_b200 import gen_normal_f32
-            self.RL = 1
-            A, B = gen_normal_f32(n, SEED_A)
-            full_A = torch.from_numpy(A).to(dev)
-            full_B = torch.from_numpy(B).to(dev)
-            self.bytes_in = 4
+            self.RL, self.planes, self.bytes_in = 1, 1, 4
+            hA, hB = gen_normal_f32(n, SEED_A)
+            A = torch.from_numpy(hA).to(dev)
+            B = torch.from_numpy(hB).to(dev)
         ctx.sync()
-        self.A, self.B = full_A, full_B
-        # this rank's share of B (rows), gathered every step in sharded runs
-        if world > 1 and w["kind"] != "u16":
-            self.B_local = full_B.view(n, -1)[self.r0:self.r1].contiguous().view(-1)
-        self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=torch.float32
-                               if w["kind"] == "f32" else torch.uint16, device=dev)
-        self.full_out = None
-        if world > 1 and rank == 0:
-            self.full_out = torch.empty(self.RL * n * n, dtype=self.out.dtype, device=dev)
+        self.A, self.B = A, B
+        # this rank's row block of every B plane (what it owns before the gather)
+        P = self.planes
+        self.B_local = B.view(P, n, n)[:, self.r0:self.r1, :].contiguous().view(-1) \
+            if world > 1 else None
+        odt = torch.float32 if w["kind"] == "f32" else torch.uint16
+        self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=odt, device=dev)
+        self.full_out = self.out if world == 1 else (
+            torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
+
+    def gather_B(self):
+        from mfft_bench_b200 import dist as D
+        P, n = self.planes, self.n
+        rows = self.rows
+        Bv = self.B.view(P, n * n)
+        for u in range(P):
+            loc = self.B_local.view(P, rows * n)[u] if rows else self.B_local[:0]
+            D.allgather_rows(self._as_gatherable(loc), self._as_gatherable(Bv[u]), n, self.ranges)
+
+    def _as_gatherable(self, t):
+        # NCCL has no uint16: move 16-bit limbs as int16 (same bytes)
+        return t.view(self.torch.int16) if t.dtype == self.torch.uint16 else t
 
     def step(self):
         """One product; sharded across ranks when world > 1."""
         from mfft_bench_b200 import dist as D
         w, ctx, n = self.w, self.ctx, self.n
-        if self.world > 1 and w["kind"] != "u16":
-            D.allgather_rows(self.B_local, self.B, n, self.ranges)
+        if self.world > 1:
+            self.gather_B()
         rows = (self.r0, self.r1)
         if w["kind"] == "i64":
             ctx.mm_i64(self.A, self.B, n, RL=self.RL, out=self.out, rows=rows)
@@ -278,25 +292,26 @@ class Workload:
         else:
             ctx.fp32(self.A, self.B, n, w["force_bits"], out=self.out, rows=rows)
         if self.world > 1:
-            D.gather_planes_to_root(self.out, self.full_out, n, self.RL, self.ranges)
+            full = self._as_gatherable(self.full_out) if self.full_out is not None else None
+            D.gather_planes_to_root(self._as_gatherable(self.out), full, n, self.RL, self.ranges)
 
 
 def e2e_measure(ctx, wl, steps, torch):
-    """The same product through the host-pointer C ABI: pinned host inputs,
-    H2D + compute + D2H inside the timed region every step."""
+    """The same product through the host-pointer C ABI (one GPU): pinned host
+    inputs, H2D + compute + D2H inside the timed region every step."""
     w, n = wl.w, wl.n
     hA = wl.A.cpu().pin_memory()
     hB = wl.B.cpu().pin_memory()
     hout = torch.empty(wl.RL * n * n, dtype=wl.out.dtype).pin_memory()
-    import numpy as np  # noqa: F401
+
+    def u16(t):
+        return t.view(torch.int16).numpy().view("uint16")
 
     def run():
         if w["kind"] == "i64":
             ctx.mm_i64(hA.numpy(), hB.numpy(), n, RL=wl.RL, out=hout.numpy())
         elif w["kind"] == "u16":
-            ctx.mm_u16(hA.view(torch.int16).numpy().view("uint16"),
-                       hB.view(torch.int16).numpy().view("uint16"), n, w["L"],
-                       signed=w["signed"], RL=wl.RL, out=hout.view(torch.int16).numpy().view("uint16"))
+            ctx.mm_u16(u16(hA), u16(hB), n, w["L"], signed=w["signed"], RL=wl.RL, out=u16(hout))
         else:
             ctx.fp32(hA.numpy(), hB.numpy(), n, w["force_bits"], out=hout.numpy())
 
@@ -312,17 +327,56 @@ def e2e_measure(ctx, wl, steps, torch):
             "d2h_bytes_per_step": d2h, "steps": steps}
 
 
+def e2e_measure_dist(wl, steps, torch, dist, device):
+    """N GPUs: every rank copies its own row blocks of A and B from pinned
+    host memory, the step runs (B all-gather, rows of C, gather to rank 0)
+    and rank 0 reads the whole C back.  Time = max over ranks."""
+    n, P = wl.n, wl.planes
+    rows = wl.rows
+    Av = wl.A.view(P, n, n)
+    hA = Av[:, wl.r0:wl.r1, :].contiguous().cpu().pin_memory()
+    hB = wl.B_local.cpu().pin_memory()
+    hout = torch.empty(wl.RL * n * n, dtype=wl.out.dtype).pin_memory() if wl.rank == 0 else None
+
+    def run():
+        Av[:, wl.r0:wl.r1, :].copy_(hA.view(P, rows, n).to(device, non_blocking=True))
+        wl.B_local.copy_(hB.to(device, non_blocking=True))
+        wl.step()
+        if wl.rank == 0:
+            hout.copy_(wl.full_out, non_blocking=True)
+        torch.cuda.synchronize()
+
+    run()
+    ts = []
+    for _ in range(steps):
+        dist.barrier()
+        t0 = time.perf_counter()
+        run()
+        ts.append(time.perf_counter() - t0)
+    t = torch.tensor([statistics.mean(ts)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    h2d = 2 * n * n * wl.bytes_in
+    d2h = wl.RL * n * n * (4 if wl.w["kind"] == "f32" else 2)
+    return {"value": float(t.item()), "unit": "s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": steps,
+            "note": "each rank uploads its row blocks; rank 0 downloads all of C"}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="c5", choices=sorted(WORKLOADS))
+    ap.add_argument("--n", type=int, default=0,
+                    help="override the workload's matrix size (small profiling cases)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.n > 0:
+        WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], n=args.n)
 
     rank = env_int("RANK", 0)
     world = env_int("WORLD_SIZE", 1)
@@ -430,7 +484,7 @@ def main():
         if world == 1:
             line["e2e"] = e2e_measure(ctx, wl, min(3, args.steps), torch)
         else:
-            line["e2e"] = None
+            line["e2e"] = e2e_measure_dist(wl, min(3, args.steps), torch, dist, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             n_s = CPU_SAMPLE_N[args.workload]

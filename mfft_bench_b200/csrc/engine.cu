@@ -47,6 +47,7 @@ struct mfftgpu_ctx {
     float phase_ms[5] = {};
     bool phase_valid = true;
     int launches = 0;
+    int raster = 0, group_m = 0;  // pointwise tile order (tuning)
     Plan last_plan{};
     bool have_plan = false;
     char msg[512] = {};
@@ -278,6 +279,8 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.err = C->d_err;
         L.timeout_ns = C->timeout_ns;
         L.num_sms = C->num_sms;
+        L.raster = C->raster;
+        L.group_m = C->group_m;
         tick(2);
         if ((rc = pointwise_launch(L, st))) return set_err(C, rc, "pointwise launch failed");
         ++C->launches;
@@ -420,6 +423,8 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     cudaMemGetInfo(&fr, &tot);
     C->ws_limit = (size_t)(0.55 * (double)fr);
     if (const char* s = getenv("MFFTGPU_WS_GB")) C->ws_limit = (size_t)(atof(s) * 1073741824.0);
+    if (const char* s = getenv("MFFTGPU_RASTER")) C->raster = atoi(s);
+    if (const char* s = getenv("MFFTGPU_GROUP_M")) C->group_m = atoi(s);
     cudaMemset(C->d_err, 0, 64);
     *out = C;
     return MFFTB_OK;

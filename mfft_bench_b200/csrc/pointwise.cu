@@ -20,18 +20,42 @@
 
 namespace mfftb {
 
+// Tile order.  raster 0: job-major, then groups of group_m row tiles x all
+// column tiles.  raster 1: evaluation point j outermost; inside, groups of
+// group_m row tiles x all column tiles, and for each (row tile, column tile)
+// the NI = K*nW*nchunk jobs of point j back to back -- they read the same A
+// rows and overlapping windows of the same F planes, so concurrent CTAs
+// share operand tiles in L2.
 __device__ __forceinline__ void pw_tile_decode(const PwParams& p, long long tile, int& q, int& mt,
                                                int& nt) {
-    long long per_job = (long long)p.tiles_m * p.tiles_n;
-    q = (int)(tile / per_job);
-    int r = (int)(tile % per_job);
-    int group = PW_GROUP_M * p.tiles_n;
-    int g = r / group;
-    int first_m = g * PW_GROUP_M;
-    int gm = p.tiles_m - first_m < PW_GROUP_M ? p.tiles_m - first_m : PW_GROUP_M;
-    int local = r % group;
-    mt = first_m + local % gm;
-    nt = local / gm;
+    const int GM = p.group_m;
+    if (p.raster == 0) {
+        long long per_job = (long long)p.tiles_m * p.tiles_n;
+        q = (int)(tile / per_job);
+        int r = (int)(tile % per_job);
+        int group = GM * p.tiles_n;
+        int g = r / group;
+        int first_m = g * GM;
+        int gm = p.tiles_m - first_m < GM ? p.tiles_m - first_m : GM;
+        int local = r % group;
+        mt = first_m + local % gm;
+        nt = local / gm;
+        return;
+    }
+    const int NI = p.jobs.K * p.jobs.nW * p.jobs.nchunk;
+    const long long per_j = (long long)p.tiles_m * p.tiles_n * NI;
+    const int j = (int)(tile / per_j);
+    long long r = tile % per_j;
+    const long long group = (long long)GM * p.tiles_n * NI;
+    const int g = (int)(r / group);
+    const int first_m = g * GM;
+    const int gm = p.tiles_m - first_m < GM ? p.tiles_m - first_m : GM;
+    long long local = r % group;
+    const int inner = (int)(local % NI);
+    local /= NI;
+    mt = first_m + (int)(local % gm);
+    nt = (int)(local / gm);
+    q = j * NI + inner;
 }
 
 __global__ void __launch_bounds__(PW_THREADS, 1)
@@ -278,6 +302,8 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     p.err = L.err;
     p.timeout_ns = L.timeout_ns;
     p.stall_producer = L.stall_producer;
+    p.raster = L.raster;
+    p.group_m = L.group_m > 0 ? L.group_m : PW_GROUP_M;
 
     CUtensorMap tmA, tmF;
     int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);

@@ -61,6 +61,8 @@ struct PwParams {
     int* err;          // device status word (0 = ok)
     unsigned long long timeout_ns;
     int stall_producer;  // self-test of the bounded waits: the producer issues nothing
+    int raster;          // 0: job-major; 1: point-major, the K*nW*nchunk jobs of a tile innermost
+    int group_m;         // row tiles per raster group
 };
 
 // Segment s of job q: which A plane and which F plane feed it.  Shared by

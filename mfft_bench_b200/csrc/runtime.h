@@ -40,6 +40,7 @@ struct PwLaunch {
     unsigned long long timeout_ns;
     int num_sms;
     int stall_producer;       // self-test only: see PwParams
+    int raster, group_m;      // tile order (see PwParams); 0 = defaults
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

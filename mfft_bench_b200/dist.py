@@ -33,38 +33,49 @@ def all_ranges(n: int, world: int, align: int = 128):
     return [row_range(n, world, r, align) for r in range(world)]
 
 
+def _bytes(t):
+    import torch
+    return t.contiguous().view(-1).view(torch.uint8)
+
+
 def allgather_rows(local, full, n_cols: int, ranges, group=None):
-    """Gather row blocks (row-major, n_cols per row) of every rank into
-    `full` on every rank.  Unequal blocks are handled with one broadcast per
-    rank from its own slice."""
+    """Gather row blocks (row-major, n_cols elements per row) of every rank
+    into `full` on every rank.  Data moves as raw bytes (any element type;
+    16-bit limbs included).  Unequal blocks are handled with one broadcast
+    per rank from its own slice."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
+    row = n_cols * full.element_size()
+    fb = full.view(-1).view(__import__("torch").uint8)
+    lb = _bytes(local)
     sizes = {(r1 - r0) for r0, r1 in ranges}
     r0, r1 = ranges[rank]
     if len(sizes) == 1:
-        dist.all_gather_into_tensor(full.view(-1), local.view(-1), group=group)
+        dist.all_gather_into_tensor(fb, lb, group=group)
         return full
-    full.view(-1)[r0 * n_cols:r1 * n_cols].copy_(local.view(-1))
+    fb[r0 * row:r1 * row].copy_(lb)
     for src in range(world):
         a, b = ranges[src]
         if b > a:
-            dist.broadcast(full.view(-1)[a * n_cols:b * n_cols], src=src, group=group)
+            dist.broadcast(fb[a * row:b * row], src=src, group=group)
     return full
 
 
 def gather_planes_to_root(local, full, n: int, RL: int, ranges, group=None, root: int = 0):
     """local: [RL][rows_r][n] output rows of this rank (flat).  On the root,
     full: [RL][n][n] (flat) receives every rank's rows plane by plane."""
+    import torch
     import torch.distributed as dist
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     r0, r1 = ranges[rank]
     rows = r1 - r0
-    lv = local.view(RL, rows, n) if rows else None
+    es = local.element_size()
+    lv = local.view(-1).view(torch.uint8).view(RL, rows, n * es) if rows else None
     ops = []
     if rank == root:
-        fv = full.view(RL, n, n)
+        fv = full.view(-1).view(torch.uint8).view(RL, n, n * es)
         if rows:
             fv[:, r0:r1, :].copy_(lv)
         for src in range(world):

@@ -1,0 +1,101 @@
+"""Multi-process (gloo, world size 2) tests of the row-block sharding logic.
+
+The GPU compute of a rank is replaced here by the CPU oracle computing that
+rank's rows; what is under test is the orchestration of mfft_bench_b200.dist:
+the row split, the all-gather of B's row blocks (equal and unequal blocks),
+and the plane-by-plane gather of C's rows into the plane-major [RL][n][n]
+layout on rank 0.
+"""
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, n, L, align, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from mfft_bench_b200 import dist as D
+        from oracle.oracle import Oracle
+        o = Oracle()
+        ranges = D.all_ranges(n, world, align)
+        r0, r1 = ranges[rank]
+        rows = r1 - r0
+        RL = 2 * L + 1
+        A = o.signed_planes(n, L, 11)
+        B = o.signed_planes(n, L, 12)
+        # 1. B all-gather, plane by plane, from this rank's row blocks
+        Bv = B.reshape(L, n, n)
+        gathered = torch.zeros(L * n * n, dtype=torch.int16)
+        for u in range(L):
+            loc = torch.from_numpy(Bv[u, r0:r1, :].copy().view(np.int16).ravel())
+            D.allgather_rows(loc, gathered.view(L, n * n)[u], n, ranges)
+        assert np.array_equal(gathered.numpy().view(np.uint16), B), "B all-gather"
+        # 2. this rank's rows of C (oracle stands in for the GPU), gather to rank 0
+        ii = np.repeat(np.arange(r0, r1), n)
+        jj = np.tile(np.arange(n), rows)
+        mine = o.entries(A, B, n, L, True, ii, jj, RL) if rows else np.zeros((RL, 0), np.uint16)
+        local = torch.from_numpy(np.ascontiguousarray(mine).view(np.int16).ravel())
+        full = torch.zeros(RL * n * n, dtype=torch.int16) if rank == 0 else None
+        D.gather_planes_to_root(local, full, n, RL, ranges)
+        if rank == 0:
+            want = o.mm_signed(A, B, n, L)
+            assert np.array_equal(full.numpy().view(np.uint16), want), "C gather"
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, never hang it
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("n,L,align", [(64, 4, 16), (100, 2, 16), (40, 3, 128)])
+def test_sharded_product_orchestration(n, L, align):
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, n, L, align, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    msgs = []
+    while not errq.empty():
+        msgs.append(errq.get())
+    assert not alive, "a rank did not finish"
+    assert all(p.exitcode == 0 for p in procs), msgs
+
+
+def test_row_ranges_cover_and_align():
+    sys.path.insert(0, ROOT)
+    from mfft_bench_b200 import dist as D
+    for n in (1, 100, 128, 1000, 16384):
+        for world in (1, 2, 3, 4, 8):
+            rs = D.all_ranges(n, world)
+            assert rs[0][0] == 0 and rs[-1][1] == n
+            for (a, b), (c, d) in zip(rs, rs[1:]):
+                assert b == c and a <= b
+            for a, b in rs[:-1]:
+                assert a % 128 == 0 and (b % 128 == 0 or b == n)
+    rs = D.all_ranges(16384, 8)
+    assert {b - a for a, b in rs} == {2048}
