@@ -263,6 +263,16 @@ class Workload:
         self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=odt, device=dev)
         self.full_out = self.out if world == 1 else (
             torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
+        # sharded runs compute a rank's rows in sub-blocks and ship each one to
+        # rank 0 while the next computes (B is transformed once per step)
+        self.subs = D.plan_subblocks(self.ranges, 2 if world > 1 else 1)
+        self.nsub = len(self.subs[0])
+        self.sub_out = []
+        off = 0
+        for a, b in self.subs[rank]:
+            cnt = self.RL * (b - a) * n
+            self.sub_out.append(self.out[off:off + cnt])
+            off += cnt
 
     def gather_B(self):
         from mfft_bench_b200 import dist as D
@@ -281,19 +291,30 @@ class Workload:
         """One product; sharded across ranks when world > 1."""
         from mfft_bench_b200 import dist as D
         w, ctx, n = self.w, self.ctx, self.n
-        if self.world > 1:
-            self.gather_B()
-        rows = (self.r0, self.r1)
+        if self.world == 1:
+            self._compute((self.r0, self.r1), self.out)
+            return
+        self.gather_B()
+        works = []
+        for si in range(self.nsub):
+            a, b = self.subs[self.rank][si]
+            ctx.set_reuse_b(si > 0)  # B is packed/transformed on the first sub-block of each step
+            self._compute((a, b), self.sub_out[si])
+            seg = [self.subs[r][si] for r in range(self.world)]
+            works += D.gather_sub_to_root_async(self.sub_out[si], self.full_out, n, self.RL, seg)
+        ctx.set_reuse_b(False)
+        for wk in works:
+            wk.wait()
+
+    def _compute(self, rows, out):
+        w, ctx, n = self.w, self.ctx, self.n
         if w["kind"] == "i64":
-            ctx.mm_i64(self.A, self.B, n, RL=self.RL, out=self.out, rows=rows)
+            ctx.mm_i64(self.A, self.B, n, RL=self.RL, out=out, rows=rows)
         elif w["kind"] == "u16":
-            ctx.mm_u16(self.A, self.B, n, w["L"], signed=w["signed"], RL=self.RL, out=self.out,
+            ctx.mm_u16(self.A, self.B, n, w["L"], signed=w["signed"], RL=self.RL, out=out,
                        rows=rows)
         else:
-            ctx.fp32(self.A, self.B, n, w["force_bits"], out=self.out, rows=rows)
-        if self.world > 1:
-            full = self._as_gatherable(self.full_out) if self.full_out is not None else None
-            D.gather_planes_to_root(self._as_gatherable(self.out), full, n, self.RL, self.ranges)
+            ctx.fp32(self.A, self.B, n, w["force_bits"], out=out, rows=rows)
 
 
 def e2e_measure(ctx, wl, steps, torch):

@@ -61,6 +61,12 @@ int mfftgpu_set_stream(mfftgpu_ctx *ctx, void *cuda_stream);
 int mfftgpu_set_workspace_limit(mfftgpu_ctx *ctx, size_t bytes);
 int mfftgpu_set_timeout_ns(mfftgpu_ctx *ctx, unsigned long long ns);
 int mfftgpu_sync(mfftgpu_ctx *ctx);
+/* While on, a product whose B (same pointer, size, format and plan) matches
+ * the previous product's reuses the transformed B planes kept in the
+ * workspace instead of packing and transforming B again -- e.g. for a row
+ * range split into several calls.  The caller guarantees B's contents did not
+ * change; turning it off drops the cached planes. */
+int mfftgpu_set_reuse_b(mfftgpu_ctx *ctx, int on);
 const char *mfftgpu_last_error(mfftgpu_ctx *ctx);
 const char *mfftgpu_status_string(int status);
 int mfftgpu_device_count(void);
@@ -149,10 +155,13 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
 
 /* Self-test of the tcgen05 pointwise kernel: random int8 Ahat/F planes for
  * the given job shape, the kernel's int32 job planes compared element by
- * element with a CUDA-core evaluation of the same job table.  *mismatches
- * receives the number of differing elements. */
+ * element with a CUDA-core evaluation of the same job table.  variant: 0 the
+ * product path's choice, 1 one CTA per 128-row tile, 2 CTA pairs (256-row
+ * tiles, tcgen05 cta_group::2).  *mismatches receives the number of
+ * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
-                               int dA, int dB, int nchunk, int block_n, long long *mismatches);
+                               int dA, int dB, int nchunk, int block_n, int variant,
+                               long long *mismatches);
 
 /* Self-test of the bounded device waits: launches the pointwise kernel with
  * a producer that never loads, so its consumers must give up after

@@ -66,6 +66,7 @@ _sig("mfftgpu_set_stream", i32, vp, vp)
 _sig("mfftgpu_set_workspace_limit", i32, vp, sz)
 _sig("mfftgpu_set_timeout_ns", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_sync", i32, vp)
+_sig("mfftgpu_set_reuse_b", i32, vp, i32)
 _sig("mfftgpu_last_error", C.c_char_p, vp)
 _sig("mfftgpu_status_string", C.c_char_p, i32)
 _sig("mfftgpu_device_count", i32)
@@ -88,7 +89,7 @@ _sig("mfftgpu_selftest_timeout", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_gen_normal_f32", None, vp, vp, sz, u64)
 _sig("mfftgpu_mm_i64_noalloc", i32, vp, vp, i32, vp, i32, vp)
 _sig("mfftgpu_decode_words_f32", C.c_float, vp, i32, i32, i32)
-_sig("mfftgpu_selftest_pointwise", i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32,
+_sig("mfftgpu_selftest_pointwise", i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
      C.POINTER(C.c_longlong))
 
 # reference-compatible ABI

@@ -101,6 +101,11 @@ class Context:
     def sync(self):
         self._check(lib.mfftgpu_sync(self._h), "sync")
 
+    def set_reuse_b(self, on=True):
+        """Reuse the previous product's transformed B when B is the same
+        buffer (unchanged contents are the caller's promise)."""
+        self._check(lib.mfftgpu_set_reuse_b(self._h, 1 if on else 0), "set_reuse_b")
+
     def phase_ms(self):
         out = (C.c_float * 5)()
         lib.mfftgpu_last_phase_ms(self._h, out)
@@ -190,10 +195,11 @@ class Context:
         self._check(lib.mfftgpu_gen_int64_dev(self._h, _ptr(x), x.numel(), seed), "gen_int64")
         return x
 
-    def selftest_pointwise(self, rows, cols, kdim, NB, K, dA=1, dB=1, nchunk=1, block_n=256):
+    def selftest_pointwise(self, rows, cols, kdim, NB, K, dA=1, dB=1, nchunk=1, block_n=256,
+                           variant=0):
         mism = C.c_longlong(-1)
         self._check(lib.mfftgpu_selftest_pointwise(self._h, rows, cols, kdim, NB, K, dA, dB,
-                                                   nchunk, block_n, C.byref(mism)),
+                                                   nchunk, block_n, variant, C.byref(mism)),
                     "selftest_pointwise")
         return mism.value
 

@@ -162,10 +162,84 @@ __global__ void __launch_bounds__(256) pack_limbs_kernel(const PackArgs a) {
     if (bad) atomicCAS(a.err, 0, MFFTB_ERR_RANGE);
 }
 
+// int64 entries into int8 digit planes, 4 digits per 32-bit store.
+// Straight (A): a thread owns 4 consecutive columns of one row.
+// Transposed (B): a 64 x 64 tile of entries is staged in shared memory and a
+// thread emits 4 consecutive contraction indices of one output row.
+__device__ __forceinline__ int digit_of_i64(int64_t x, int p, int b, int W) {
+    if (p + b >= W) {
+        int64_t t = (int64_t)((uint64_t)x << (64 - W)) >> (64 - W);
+        return (int)(t >> p);
+    }
+    return (int)(((uint64_t)x >> p) & ((1u << b) - 1u));
+}
+
+__device__ __forceinline__ uint32_t pack4(int d0, int d1, int d2, int d3) {
+    return (uint32_t)(d0 & 0xFF) | ((uint32_t)(d1 & 0xFF) << 8) | ((uint32_t)(d2 & 0xFF) << 16) |
+           ((uint32_t)(d3 & 0xFF) << 24);
+}
+
+__global__ void __launch_bounds__(256) pack_i64_straight_kernel(const PackArgs a) {
+    const long long t = blockIdx.x * 256LL + threadIdx.x;
+    const int groups = a.ld / 4;
+    const int r = (int)(t / groups), c0 = (int)(t % groups) * 4;
+    if (r >= a.rows) return;
+    const int i = a.row0 + r;
+    const long long* src = reinterpret_cast<const long long*>(a.src);
+    int64_t x[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        x[q] = (i < a.n && c0 + q < a.n) ? __ldg(src + (long long)i * a.n + c0 + q) : 0;
+    uint8_t* out = reinterpret_cast<uint8_t*>(a.dst) + (long long)r * a.ld + c0;
+    for (int m = 0; m < a.Lb; ++m) {
+        const int p = m * a.b;
+        *reinterpret_cast<uint32_t*>(out + (long long)m * a.plane) =
+            pack4(digit_of_i64(x[0], p, a.b, a.W), digit_of_i64(x[1], p, a.b, a.W),
+                  digit_of_i64(x[2], p, a.b, a.W), digit_of_i64(x[3], p, a.b, a.W));
+    }
+}
+
+__global__ void __launch_bounds__(256) pack_i64_transposed_kernel(const PackArgs a) {
+    __shared__ int64_t tile[64][65];
+    const int k0 = blockIdx.x * 64, j0 = blockIdx.y * 64;  // contraction / output-row origin
+    const long long* src = reinterpret_cast<const long long*>(a.src);
+    for (int e = threadIdx.x; e < 64 * 64; e += 256) {
+        const int kk = e >> 6, jj = e & 63;  // coalesced along j
+        const int k = k0 + kk, j = j0 + jj;
+        tile[kk][jj] = (k < a.n && j < a.n) ? __ldg(src + (long long)k * a.n + j) : 0;
+    }
+    __syncthreads();
+    uint8_t* out = reinterpret_cast<uint8_t*>(a.dst);
+    for (int w = threadIdx.x; w < 64 * 16; w += 256) {
+        const int jj = w >> 4, kq = (w & 15) * 4;  // 16 threads per output row
+        const int r = j0 + jj, c = k0 + kq;
+        if (r >= a.rows || c >= a.ld) continue;
+        const int64_t x0 = tile[kq][jj], x1 = tile[kq + 1][jj], x2 = tile[kq + 2][jj],
+                      x3 = tile[kq + 3][jj];
+        uint8_t* o = out + (long long)r * a.ld + c;
+        for (int m = 0; m < a.Lb; ++m) {
+            const int p = m * a.b;
+            *reinterpret_cast<uint32_t*>(o + (long long)m * a.plane) =
+                pack4(digit_of_i64(x0, p, a.b, a.W), digit_of_i64(x1, p, a.b, a.W),
+                      digit_of_i64(x2, p, a.b, a.W), digit_of_i64(x3, p, a.b, a.W));
+        }
+    }
+}
+
 int pack_launch(const PackArgs& a, cudaStream_t stream) {
     if (a.ld % 16 || a.rows <= 0 || a.Lb <= 0 || a.b < 1 || (a.b > 15 && a.fmt != PACK_I32LIMB))
         return MFFTB_ERR_ARG;
     dim3 block(256);
+    if (a.fmt == PACK_I64 && a.b <= 7 && a.plane % 4 == 0) {
+        if (a.transpose) {
+            dim3 grid((a.ld + 63) / 64, (a.rows + 63) / 64);
+            pack_i64_transposed_kernel<<<grid, block, 0, stream>>>(a);
+        } else {
+            const long long threads = (long long)a.rows * (a.ld / 4);
+            pack_i64_straight_kernel<<<(unsigned)((threads + 255) / 256), block, 0, stream>>>(a);
+        }
+        return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+    }
     if (a.fmt == PACK_I32LIMB) {
         dim3 grid((a.ld + 31) / 32, (a.rows + 31) / 32, a.Lb);
         if (a.transpose) pack_limbs_kernel<true><<<grid, block, 0, stream>>>(a);

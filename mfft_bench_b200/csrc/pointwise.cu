@@ -246,6 +246,211 @@ __global__ void __launch_bounds__(PW_THREADS, 1)
     if (warp == 1) tmem_dealloc(tmem_base, PW_TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- CTA-pair variant
+// Same job table, tiles of 256 rows x 256 columns per CTA pair (a cluster of
+// two CTAs on two SMs).  The leader CTA issues tcgen05.mma.cta_group::2
+// (M = 256, N = 256): A rows 0-127 come from the leader's shared memory and
+// 128-255 from the peer's; the 256 B rows (output columns) are split 128/128
+// the same way, so each SM streams 32 KB per 128-byte k-step instead of 48 KB
+// for the same MACs, and the ring is 6 stages deep.  Each CTA's TMEM holds
+// its 128 output rows.  Both CTAs' TMA loads complete on the leader's "full"
+// barrier; the leader's commits arrive on both CTAs' "empty" / "TMEM full"
+// barriers; both epilogues arrive on the leader's "TMEM empty" barrier.
+constexpr int PW2_STAGES = 6;
+constexpr int PW2_BN = 256;
+constexpr int PW2_A_BYTES = 128 * PW_BK;
+constexpr int PW2_B_BYTES = (PW2_BN / 2) * PW_BK;
+constexpr int PW2_SMEM_BYTES = 1024 + PW2_STAGES * (PW2_A_BYTES + PW2_B_BYTES) + 256;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
+    pointwise2_i8_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmF, const PwParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + PW2_STAGES * PW2_A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + PW2_STAGES * PW2_B_BYTES);
+    const uint32_t bar_full = smem_u32(bars);
+    const uint32_t bar_empty = smem_u32(bars + PW2_STAGES);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * PW2_STAGES);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * PW2_STAGES + 2);
+    const uint32_t bar_drain = smem_u32(bars + 2 * PW2_STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PW2_STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const long long pair = blockIdx.x >> 1;
+    const long long npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PW2_STAGES; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(bar_tfull + 8 * a, 1);
+            mbar_init(bar_tempty + 8 * a, 2 * 128);
+        }
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmF);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), PW_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();  // barrier inits and TMEM allocation visible to the pair
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const unsigned long long tmo = p.timeout_ns;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------ TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[PW2_STAGES];
+        for (int s = 0; s < PW2_STAGES; ++s) issued_parity[s] = -1;
+        const uint32_t tx_bytes = 2 * (PW2_A_BYTES + PW2_B_BYTES);
+        const long long first_tile = p.stall_producer ? p.num_tiles : pair;
+        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            for (int s = s0; s < s1; ++s) {
+                int pa, pf;
+                pw_segment_planes(p.jobs, j, t, w, s, pa, pf);
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                                           global_timer_ns() + tmo))
+                        goto producer_done;
+                    const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
+                    if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                    tma_load_3d_pair(smem_u32(sA + stage * PW2_A_BYTES), &tmA, full_leader,
+                                     kb * PW_BK, mt * 256 + (int)rank * 128, pa);
+                    tma_load_3d_pair(smem_u32(sB + stage * PW2_B_BYTES), &tmF, full_leader,
+                                     kb * PW_BK, nt * PW2_BN + (int)rank * (PW2_BN / 2), pf);
+                    issued_parity[stage] = (int)phase;
+                    if (++stage == PW2_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    producer_done:
+        // every stage this CTA loaded is consumed by the pair's MMA (which
+        // implies the load landed) before the CTA may leave
+        for (int s = 0; s < PW2_STAGES; ++s)
+            if (issued_parity[s] >= 0)
+                if (!mbar_wait_deadline(bar_empty + 8 * s, (uint32_t)issued_parity[s],
+                                        global_timer_ns() + tmo))
+                    *abort_flag = 1;
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------ MMA issuer (leader only)
+        const uint32_t idesc = idesc_i8(256, PW2_BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            const int nsteps = (s1 - s0) * p.kblocks;
+            if (!mbar_wait_bounded(bar_tempty + 8 * acc, acc_phase ^ 1, abort_flag,
+                                   global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+            for (int it = 0; it < nsteps; ++it) {
+                if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                       global_timer_ns() + tmo))
+                    goto mma_done;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(sA + stage * PW2_A_BYTES);
+                const uint32_t b0 = smem_u32(sB + stage * PW2_B_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < PW_BK / 32; ++kk) {
+                    mma_i8_pair(d_tmem, sdesc_kmajor_sw128(a0 + kk * 32),
+                                sdesc_kmajor_sw128(b0 + kk * 32), idesc, (it | kk) != 0 ? 1u : 0u);
+                }
+                mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                if (++stage == PW2_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_pair_mc(bar_tfull + 8 * acc, 0x3);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    mma_done:
+        mma_commit_pair(bar_drain);
+        if (!mbar_wait_deadline(bar_drain, 0, global_timer_ns() + tmo)) *abort_flag = 1;
+    } else if (warp >= 2) {
+        // ------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
+            int q, mt, nt, j, t, w, ch, s0, s1;
+            pw_tile_decode(p, tile, q, mt, nt);
+            pw_job_decode(p.jobs, q, j, t, w, ch);
+            pw_chunk_range(p.jobs, w, ch, s0, s1);
+            if (!mbar_wait_bounded(bar_tfull + 8 * acc, acc_phase, abort_flag,
+                                   global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const bool empty_job = (s1 <= s0);
+            const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+            const int col0 = nt * PW2_BN;
+            int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
+            const int colmax = p.cols - col0;
+            for (int c = 0; c < PW2_BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                       (uint32_t)(acc * 256 + c * 32),
+                                   v);
+                tmem_ld_wait();
+                if (row < p.rows) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        const int col = c * 32 + e;
+                        if (col < colmax) {
+                            int4 o;
+                            o.x = empty_job ? 0 : (int)v[e];
+                            o.y = empty_job ? 0 : (int)v[e + 1];
+                            o.z = empty_job ? 0 : (int)v[e + 2];
+                            o.w = empty_job ? 0 : (int)v[e + 3];
+                            *reinterpret_cast<int4*>(orow + col) = o;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(mapa_shared(bar_tempty + 8 * acc, 0));
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // neither CTA leaves while the pair may still signal it
+    tc_fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicCAS(p.err, 0, MFFTB_ERR_TIMEOUT);
+    if (warp == 1) tmem_dealloc_pair(tmem_base, PW_TMEM_COLS);
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -285,15 +490,18 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     if (reinterpret_cast<uintptr_t>(L.A) % 16 || reinterpret_cast<uintptr_t>(L.F) % 16 ||
         reinterpret_cast<uintptr_t>(L.out) % 16)
         return MFFTB_ERR_ARG;
+    // CTA pairs when both dimensions fill at least one 256 x 256 pair tile
+    const bool pair = L.variant == 2 || (L.variant == 0 && L.block_n == 256 && L.rows >= 256 &&
+                                         L.cols >= 256 && L.num_sms >= 2);
     PwParams p;
     p.jobs = L.jobs;
     p.rows = L.rows;
     p.cols = L.cols;
     p.kdim = L.kdim;
     p.kblocks = (L.kdim + PW_BK - 1) / PW_BK;
-    p.block_n = L.block_n;
+    p.block_n = pair ? PW2_BN : L.block_n;
     if (p.block_n != 64 && p.block_n != 128 && p.block_n != 256) return MFFTB_ERR_ARG;
-    p.tiles_m = (L.rows + PW_BM - 1) / PW_BM;
+    p.tiles_m = pair ? (L.rows + 255) / 256 : (L.rows + PW_BM - 1) / PW_BM;
     p.tiles_n = (L.cols + p.block_n - 1) / p.block_n;
     p.num_tiles = (long long)p.tiles_m * p.tiles_n * L.jobs.njobs;
     p.out = L.out;
@@ -303,20 +511,41 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     p.timeout_ns = L.timeout_ns;
     p.stall_producer = L.stall_producer;
     p.raster = L.raster;
-    p.group_m = L.group_m > 0 ? L.group_m : PW_GROUP_M;
+    p.group_m = L.group_m > 0 ? L.group_m : (pair ? PW_GROUP_M / 2 : PW_GROUP_M);
 
     CUtensorMap tmA, tmF;
     int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);
     if (rc) return rc;
-    rc = make_map(&tmF, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, p.block_n);
+    rc = make_map(&tmF, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes,
+                  pair ? PW2_BN / 2 : p.block_n);
     if (rc) return rc;
 
-    static bool attr_set = false;
-    if (!attr_set) {
+    if (pair) {
+        static int attr_dev = -1;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (attr_dev != dev) {
+            if (cudaFuncSetAttribute(pointwise2_i8_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     PW2_SMEM_BYTES) != cudaSuccess)
+                return MFFTB_ERR_CUDA;
+            attr_dev = dev;
+        }
+        long long pairs = L.num_sms / 2;
+        if (pairs > p.num_tiles) pairs = p.num_tiles;
+        if (pairs <= 0) return MFFTB_OK;
+        pointwise2_i8_kernel<<<(unsigned)(2 * pairs), PW_THREADS, PW2_SMEM_BYTES, stream>>>(tmA, tmF,
+                                                                                         p);
+        return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+    }
+    static int attr_dev1 = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev1 != dev) {
         if (cudaFuncSetAttribute(pointwise_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PW_SMEM_BYTES) != cudaSuccess)
             return MFFTB_ERR_CUDA;
-        attr_set = true;
+        attr_dev1 = dev;
     }
     long long grid = L.num_sms;
     if (grid > p.num_tiles) grid = p.num_tiles;

@@ -41,6 +41,7 @@ struct PwLaunch {
     int num_sms;
     int stall_producer;       // self-test only: see PwParams
     int raster, group_m;      // tile order (see PwParams); 0 = defaults
+    int variant;              // 0 auto, 1 one CTA per tile, 2 CTA pairs (256 x 256 tiles)
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

@@ -92,3 +92,57 @@ def gather_planes_to_root(local, full, n: int, RL: int, ranges, group=None, root
         for req in dist.batch_isend_irecv(ops):
             req.wait()
     return full
+
+
+def sub_ranges(r0: int, r1: int, nsub: int, align: int = 256):
+    """Split [r0, r1) into nsub pieces on `align` boundaries (fewer if short)."""
+    rows = r1 - r0
+    units = (rows + align - 1) // align
+    nsub = max(1, min(nsub, units))
+    cuts = [r0 + min(rows, (units * k // nsub) * align) for k in range(nsub + 1)]
+    return [(cuts[k], cuts[k + 1]) for k in range(nsub) if cuts[k + 1] > cuts[k]]
+
+
+def plan_subblocks(ranges, nsub: int, align: int = 256):
+    """Per rank, exactly the same number of sub-blocks (the smallest count
+    any rank can make, at least 1); each rank's last sub-block runs to the
+    end of its rows, and a rank without rows gets empty (r1, r1) blocks.
+    Returns subs[rank][k] = (a, b)."""
+    per = [sub_ranges(a, b, nsub, align) if b > a else [] for a, b in ranges]
+    k = max(1, min((len(x) for x in per if x), default=1))
+    out = []
+    for (a, b), x in zip(ranges, per):
+        if not x:
+            out.append([(b, b)] * k)
+            continue
+        x = x[:k]
+        x[-1] = (x[-1][0], b)
+        out.append(x)
+    return out
+
+
+def gather_sub_to_root_async(local, full, n: int, RL: int, seg_of_rank, group=None, root: int = 0):
+    """Post (without waiting) the transfers of one sub-block index: every
+    rank's rows seg_of_rank[r] = (a, b) go plane by plane into full
+    [RL][n][n] on the root; local is this rank's [RL][b-a][n] block.
+    Returns the list of work handles to wait on."""
+    import torch
+    import torch.distributed as dist
+    rank = dist.get_rank(group)
+    a0, b0 = seg_of_rank[rank]
+    es = local.element_size()
+    ops = []
+    if rank == root:
+        fv = full.view(-1).view(torch.uint8).view(RL, n, n * es)
+        if b0 > a0:
+            fv[:, a0:b0, :].copy_(local.view(-1).view(torch.uint8).view(RL, b0 - a0, n * es))
+        for src, (a, b) in enumerate(seg_of_rank):
+            if src == root or b <= a:
+                continue
+            for w in range(RL):
+                ops.append(dist.P2POp(dist.irecv, fv[w, a:b, :], src, group=group))
+    elif b0 > a0:
+        lv = local.view(-1).view(torch.uint8).view(RL, b0 - a0, n * es)
+        for w in range(RL):
+            ops.append(dist.P2POp(dist.isend, lv[w], root, group=group))
+    return dist.batch_isend_irecv(ops) if ops else []

@@ -56,9 +56,27 @@ def _worker(rank, world, port, n, L, align, errq):
         local = torch.from_numpy(np.ascontiguousarray(mine).view(np.int16).ravel())
         full = torch.zeros(RL * n * n, dtype=torch.int16) if rank == 0 else None
         D.gather_planes_to_root(local, full, n, RL, ranges)
+        want = o.mm_signed(A, B, n, L) if rank == 0 else None
         if rank == 0:
-            want = o.mm_signed(A, B, n, L)
             assert np.array_equal(full.numpy().view(np.uint16), want), "C gather"
+        # 3. sub-blocks shipped asynchronously while the next one is computed
+        subs = D.plan_subblocks(ranges, 2, align=16)
+        nsub = len(subs[0])
+        assert all(len(x) == nsub for x in subs)
+        full2 = torch.zeros(RL * n * n, dtype=torch.int16) if rank == 0 else None
+        works, keep = [], []
+        for si in range(nsub):
+            a, b = subs[rank][si]
+            ii = np.repeat(np.arange(a, b), n)
+            jj = np.tile(np.arange(n), b - a)
+            blk = o.entries(A, B, n, L, True, ii, jj, RL) if b > a else np.zeros((RL, 0), np.uint16)
+            t = torch.from_numpy(np.ascontiguousarray(blk).view(np.int16).ravel())
+            keep.append(t)
+            works += D.gather_sub_to_root_async(t, full2, n, RL, [x[si] for x in subs])
+        for wk in works:
+            wk.wait()
+        if rank == 0:
+            assert np.array_equal(full2.numpy().view(np.uint16), want), "async sub-block gather"
         dist.barrier()
         dist.destroy_process_group()
     except Exception as e:  # report to the parent, never hang it
@@ -84,6 +102,21 @@ def test_sharded_product_orchestration(n, L, align):
         msgs.append(errq.get())
     assert not alive, "a rank did not finish"
     assert all(p.exitcode == 0 for p in procs), msgs
+
+
+def test_subblock_plan_covers_every_row():
+    sys.path.insert(0, ROOT)
+    from mfft_bench_b200 import dist as D
+    for n in (100, 1000, 2048, 16384):
+        for world in (1, 2, 3, 8):
+            rng = D.all_ranges(n, world)
+            for nsub in (1, 2, 3):
+                subs = D.plan_subblocks(rng, nsub)
+                assert len({len(x) for x in subs}) == 1
+                for (a, b), x in zip(rng, subs):
+                    assert x[0][0] == a and x[-1][1] == b
+                    for (p, q), (r, t) in zip(x, x[1:]):
+                        assert q == r
 
 
 def test_row_ranges_cover_and_align():

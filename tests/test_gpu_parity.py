@@ -23,7 +23,20 @@ SA, SB = 12345, 12345 ^ 0xABCDEF
     (384, 512, 520, 8, 8, 1, 1, 1, 256),
 ])
 def test_pointwise_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA, dB, nchunk, bn):
-    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, nchunk, bn) == 0
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, nchunk, bn, variant=1) == 0
+
+
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,dA,dB,nchunk", [
+    (256, 256, 256, 2, 1, 1, 1, 1),
+    (512, 256, 128, 1, 2, 1, 1, 1),
+    (300, 272, 144, 2, 4, 2, 2, 2),
+    (1000, 1008, 1000, 2, 4, 3, 2, 3),
+    (768, 1024, 520, 8, 8, 1, 1, 1),
+    (2048, 2048, 2048, 2, 8, 1, 1, 1),
+])
+def test_pointwise_pair_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA, dB, nchunk):
+    """The CTA-pair (tcgen05 cta_group::2, 256 x 256 tiles) variant."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, nchunk, 256, variant=2) == 0
 
 
 # ---------------------------------------------------------------- golden fixtures
