@@ -51,6 +51,7 @@ WORKLOADS = {
 CPU_SAMPLE_N = {"c1": 64, "c2": 256, "c3": 128, "c4": 256, "c5": 512}
 
 METRIC = "s per exact n x n W-bit matmul; effective int8 TOPS vs tcgen05 int8 peak"
+SUBBLOCKS = 1
 
 
 # ---------------------------------------------------------------------------- helpers
@@ -263,9 +264,12 @@ class Workload:
         self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=odt, device=dev)
         self.full_out = self.out if world == 1 else (
             torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
-        # sharded runs compute a rank's rows in sub-blocks and ship each one to
-        # rank 0 while the next computes (B is transformed once per step)
-        self.subs = D.plan_subblocks(self.ranges, 2 if world > 1 else 1)
+        # optionally (--subblocks > 1) a rank computes its rows in sub-blocks
+        # and ships each one to rank 0 while the next computes (B is transformed
+        # once per step).  Off by default: NCCL's copy kernels then share the
+        # SMs with the persistent pointwise kernel, which cost more than the
+        # overlap saved on 8 GPUs.
+        self.subs = D.plan_subblocks(self.ranges, SUBBLOCKS if world > 1 else 1)
         self.nsub = len(self.subs[0])
         self.sub_out = []
         off = 0
@@ -315,6 +319,33 @@ class Workload:
                        rows=rows)
         else:
             ctx.fp32(self.A, self.B, n, w["force_bits"], out=out, rows=rows)
+
+
+def cublas_int8_sustained(torch, stream, seconds=2.0, n=8192):
+    """Same-run context for the power-capped roofline: cuBLASLt int8 GEMM
+    (torch._int_mm, int8 x int8 -> int32) run back to back for `seconds`,
+    timed with CUDA events.  A library GEMM, used only as a yardstick."""
+    try:
+        a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        iters = 0
+        e0.record(stream)
+        while time.perf_counter() - t0 < seconds:
+            for _ in range(20):
+                torch._int_mm(a, b)
+            iters += 20
+            torch.cuda.synchronize()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        return 2.0 * n ** 3 * iters / (ms * 1e-3) / 1e12
+    except Exception:
+        return None
 
 
 def e2e_measure(ctx, wl, steps, torch):
@@ -393,9 +424,14 @@ def main():
                     help="override the workload's matrix size (small profiling cases)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-int8-ref", action="store_true")
+    ap.add_argument("--subblocks", type=int, default=1,
+                    help="row sub-blocks per rank whose gathers overlap the next block's compute")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global SUBBLOCKS
+    SUBBLOCKS = max(1, args.subblocks)
     if args.n > 0:
         WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], n=args.n)
 
@@ -482,7 +518,7 @@ def main():
             macs_rank = macs * (wl.rows / n)
             achieved = 2 * macs_rank / (pw_ms * 1e-3) / 1e12
             line["roofline"] = {
-                "bound": "tensor", "kernel": "pointwise_i8_kernel (tcgen05 kind::i8)",
+                "bound": "tensor", "kernel": ("pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)" if wl.rows >= 256 and n >= 256 else "pointwise_i8_kernel (tcgen05 kind::i8)"),
                 "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
                 "frac": achieved / peak_int8, "traffic": None,
                 "peak_basis": f"2 x bf16_tflops_sustained ({peak_kind} MEASURED_PEAKS.json)",
@@ -501,6 +537,11 @@ def main():
             line["roofline"]["traffic"] = tr["bytes_per_launch"]
             line["roofline"]["traffic_note"] = tr.get("note")
 
+    if world == 1 and "roofline" in line and not args.no_int8_ref:
+        ref_tops = cublas_int8_sustained(torch, stream)
+        line["roofline"]["int8_cublas_sustained_tops"] = ref_tops
+        if ref_tops:
+            line["roofline"]["frac_vs_cublas_int8_sustained"] = line["roofline"]["achieved"] / ref_tops
     if not args.no_e2e:
         if world == 1:
             line["e2e"] = e2e_measure(ctx, wl, min(3, args.steps), torch)
