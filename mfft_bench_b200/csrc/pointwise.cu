@@ -451,6 +451,234 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, PW_TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- t-grouped CTA-pair variant
+// For single-digit plans (nW = nchunk = 1, K a multiple of 4).  The K jobs
+// (j, t) of one evaluation point share their A operand (Ahat_j, all c1) and
+// read overlapping windows of the F stack (plane K-1-t+c1).  A CTA pair
+// computes 4 of them at once -- t = t0..t0+3, one 256 x 128 TMEM accumulator
+// each (4 x 128 = 512 columns) -- from stages that hold 2 consecutive c1
+// planes of A (2 x 16 KB per CTA) and the 5 F planes those 8 (c1, t) pairs
+// need (5 x 8 KB): 72 KB per stage feed 32 pair MMAs (256 x 128 x 32), so
+// every operand byte loaded into shared memory is used 3.2 times on average
+// instead of once.
+constexpr int PW3_STAGES = 3;
+constexpr int PW3_TG = 4;             // jobs per tile group
+constexpr int PW3_CPS = 2;            // c1 planes per stage
+constexpr int PW3_NF = PW3_TG + PW3_CPS - 1;
+constexpr int PW3_BN = 128;           // output columns per pair tile (MMA N)
+constexpr int PW3_A_BYTES = 128 * PW_BK;             // one A plane tile per CTA
+constexpr int PW3_F_BYTES = (PW3_BN / 2) * PW_BK;    // one F plane half-tile per CTA
+constexpr int PW3_STAGE_BYTES = PW3_CPS * PW3_A_BYTES + PW3_NF * PW3_F_BYTES;
+constexpr int PW3_SMEM_BYTES = 1024 + PW3_STAGES * PW3_STAGE_BYTES + 256;
+
+__device__ __forceinline__ void pw3_tile_decode(const PwParams& p, long long tile, int& j, int& t0,
+                                                int& mt, int& nt) {
+    const int ngroups = p.jobs.K / PW3_TG;
+    const long long per_sj = (long long)p.tiles_m * p.tiles_n;
+    const int sj = (int)(tile / per_sj);
+    const int r = (int)(tile % per_sj);
+    const int GM = p.group_m;
+    const int group = GM * p.tiles_n;
+    const int g = r / group;
+    const int first_m = g * GM;
+    const int gm = p.tiles_m - first_m < GM ? p.tiles_m - first_m : GM;
+    const int local = r % group;
+    mt = first_m + local % gm;
+    nt = local / gm;
+    j = sj / ngroups;
+    t0 = (sj % ngroups) * PW3_TG;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
+    pointwise3_i8_kernel(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmF, const PwParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PW3_STAGES * PW3_STAGE_BYTES);
+    const uint32_t bar_full = smem_u32(bars);
+    const uint32_t bar_empty = smem_u32(bars + PW3_STAGES);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * PW3_STAGES);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * PW3_STAGES + 1);
+    const uint32_t bar_drain = smem_u32(bars + 2 * PW3_STAGES + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PW3_STAGES + 3);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const long long pair = blockIdx.x >> 1;
+    const long long npairs = gridDim.x >> 1;
+    const int K = p.jobs.K;
+    const int cps_per_kb = K / PW3_CPS;
+    const int steps_per_tile = p.kblocks * cps_per_kb;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PW3_STAGES; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_tfull, 1);
+        mbar_init(bar_tempty, 2 * 128);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmF);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), PW_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const unsigned long long tmo = p.timeout_ns;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------ TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[PW3_STAGES];
+        for (int s = 0; s < PW3_STAGES; ++s) issued_parity[s] = -1;
+        const uint32_t tx_bytes = 2 * PW3_STAGE_BYTES;
+        const long long first_tile = p.stall_producer ? p.num_tiles : pair;
+        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            int j, t0, mt, nt;
+            pw3_tile_decode(p, tile, j, t0, mt, nt);
+            const int a_base = j * K;              // Ahat planes of point j (dA = 1)
+            const int f_base = j * (2 * K - 1);    // F planes of point j (dB = 1)
+            for (int cp = 0; cp < cps_per_kb; ++cp) {
+                const int c = cp * PW3_CPS;
+                const int p_lo = K - PW3_TG - t0 + c;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                                           global_timer_ns() + tmo))
+                        goto producer_done;
+                    const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
+                    if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                    uint8_t* st = smem + stage * PW3_STAGE_BYTES;
+#pragma unroll
+                    for (int cc = 0; cc < PW3_CPS; ++cc)
+                        tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
+                                         kb * PW_BK, mt * 256 + (int)rank * 128, a_base + c + cc);
+#pragma unroll
+                    for (int f = 0; f < PW3_NF; ++f)
+                        tma_load_3d_pair(
+                            smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
+                            full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
+                            f_base + p_lo + f);
+                    issued_parity[stage] = (int)phase;
+                    if (++stage == PW3_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    producer_done:
+        for (int s = 0; s < PW3_STAGES; ++s)
+            if (issued_parity[s] >= 0)
+                if (!mbar_wait_deadline(bar_empty + 8 * s, (uint32_t)issued_parity[s],
+                                        global_timer_ns() + tmo))
+                    *abort_flag = 1;
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------ MMA issuer (leader only)
+        const uint32_t idesc = idesc_i8(256, PW3_BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            for (int it = 0; it < steps_per_tile; ++it) {
+                if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                       global_timer_ns() + tmo))
+                    goto mma_done;
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + stage * PW3_STAGE_BYTES);
+#pragma unroll
+                for (int cc = 0; cc < PW3_CPS; ++cc) {
+#pragma unroll
+                    for (int tt = 0; tt < PW3_TG; ++tt) {
+                        const int fi = PW3_TG - 1 - tt + cc;  // F plane K-1-(t0+tt)+(c+cc) - p_lo
+                        const uint32_t a0 = st + cc * PW3_A_BYTES;
+                        const uint32_t b0 = st + PW3_CPS * PW3_A_BYTES + fi * PW3_F_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < PW_BK / 32; ++kk)
+                            mma_i8_pair(tmem_base + (uint32_t)(tt * PW3_BN),
+                                        sdesc_kmajor_sw128(a0 + kk * 32),
+                                        sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                        (it | cc | kk) != 0 ? 1u : 0u);
+                    }
+                }
+                mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                if (++stage == PW3_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_pair_mc(bar_tfull, 0x3);
+            acc_phase ^= 1;
+        }
+    mma_done:
+        mma_commit_pair(bar_drain);
+        if (!mbar_wait_deadline(bar_drain, 0, global_timer_ns() + tmo)) *abort_flag = 1;
+    } else if (warp >= 2) {
+        // ------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
+            int j, t0, mt, nt;
+            pw3_tile_decode(p, tile, j, t0, mt, nt);
+            if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+            const int col0 = nt * PW3_BN;
+            const int colmax = p.cols - col0;
+            for (int tt = 0; tt < PW3_TG; ++tt) {
+                const int q = j * K + t0 + tt;  // job (j, t) with one digit class, one chunk
+                int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
+                for (int c = 0; c < PW3_BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                           (uint32_t)(tt * PW3_BN + c * 32),
+                                       v);
+                    tmem_ld_wait();
+                    if (row < p.rows) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 4) {
+                            const int col = c * 32 + e;
+                            if (col < colmax) {
+                                int4 o;
+                                o.x = (int)v[e];
+                                o.y = (int)v[e + 1];
+                                o.z = (int)v[e + 2];
+                                o.w = (int)v[e + 3];
+                                *reinterpret_cast<int4*>(orow + col) = o;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(mapa_shared(bar_tempty, 0));
+            acc_phase ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    tc_fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicCAS(p.err, 0, MFFTB_ERR_TIMEOUT);
+    if (warp == 1) tmem_dealloc_pair(tmem_base, PW_TMEM_COLS);
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -490,20 +718,28 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     if (reinterpret_cast<uintptr_t>(L.A) % 16 || reinterpret_cast<uintptr_t>(L.F) % 16 ||
         reinterpret_cast<uintptr_t>(L.out) % 16)
         return MFFTB_ERR_ARG;
-    // CTA pairs when both dimensions fill at least one 256 x 256 pair tile
-    const bool pair = L.variant == 2 || (L.variant == 0 && L.block_n == 256 && L.rows >= 256 &&
-                                         L.cols >= 256 && L.num_sms >= 2);
+    // t-grouped CTA pairs for single-digit plans, CTA pairs when both
+    // dimensions fill at least one 256 x 256 pair tile, single CTAs otherwise
+    const bool grouped_ok = L.jobs.nW == 1 && L.jobs.nchunk == 1 && L.jobs.K % PW3_TG == 0 &&
+                            L.jobs.dA == 1 && L.jobs.dB == 1 && L.rows >= 256 && L.cols >= 128 &&
+                            L.num_sms >= 2;
+    const bool grouped = L.variant == 3 ? grouped_ok : (L.variant == 0 && grouped_ok);
+    if (L.variant == 3 && !grouped_ok) return MFFTB_ERR_ARG;
+    const bool pair = !grouped && (L.variant == 2 || (L.variant == 0 && L.block_n == 256 &&
+                                                      L.rows >= 256 && L.cols >= 256 &&
+                                                      L.num_sms >= 2));
     PwParams p;
     p.jobs = L.jobs;
     p.rows = L.rows;
     p.cols = L.cols;
     p.kdim = L.kdim;
     p.kblocks = (L.kdim + PW_BK - 1) / PW_BK;
-    p.block_n = pair ? PW2_BN : L.block_n;
+    p.block_n = grouped ? PW3_BN : (pair ? PW2_BN : L.block_n);
     if (p.block_n != 64 && p.block_n != 128 && p.block_n != 256) return MFFTB_ERR_ARG;
-    p.tiles_m = pair ? (L.rows + 255) / 256 : (L.rows + PW_BM - 1) / PW_BM;
+    p.tiles_m = (pair || grouped) ? (L.rows + 255) / 256 : (L.rows + PW_BM - 1) / PW_BM;
     p.tiles_n = (L.cols + p.block_n - 1) / p.block_n;
-    p.num_tiles = (long long)p.tiles_m * p.tiles_n * L.jobs.njobs;
+    p.num_tiles = (long long)p.tiles_m * p.tiles_n *
+                  (grouped ? (long long)(L.jobs.njobs / PW3_TG) : (long long)L.jobs.njobs);
     p.out = L.out;
     p.out_plane = L.out_plane;
     p.ldo = L.ldo;
@@ -511,14 +747,33 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     p.timeout_ns = L.timeout_ns;
     p.stall_producer = L.stall_producer;
     p.raster = L.raster;
-    p.group_m = L.group_m > 0 ? L.group_m : (pair ? PW_GROUP_M / 2 : PW_GROUP_M);
+    p.group_m = L.group_m > 0 ? L.group_m : ((pair || grouped) ? PW_GROUP_M / 2 : PW_GROUP_M);
 
     CUtensorMap tmA, tmF;
     int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);
     if (rc) return rc;
     rc = make_map(&tmF, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes,
-                  pair ? PW2_BN / 2 : p.block_n);
+                  grouped ? PW3_BN / 2 : (pair ? PW2_BN / 2 : p.block_n));
     if (rc) return rc;
+
+    if (grouped) {
+        static int attr_dev3 = -1;
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (attr_dev3 != dev) {
+            if (cudaFuncSetAttribute(pointwise3_i8_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     PW3_SMEM_BYTES) != cudaSuccess)
+                return MFFTB_ERR_CUDA;
+            attr_dev3 = dev;
+        }
+        long long pairs = L.num_sms / 2;
+        if (pairs > p.num_tiles) pairs = p.num_tiles;
+        if (pairs <= 0) return MFFTB_OK;
+        pointwise3_i8_kernel<<<(unsigned)(2 * pairs), PW_THREADS, PW3_SMEM_BYTES, stream>>>(tmA,
+                                                                                         tmF, p);
+        return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+    }
 
     if (pair) {
         static int attr_dev = -1;
