@@ -48,7 +48,8 @@ struct mfftgpu_ctx {
     bool phase_valid = true;
     int launches = 0;
     int raster = 0, group_m = 0;  // pointwise tile order (tuning)
-    int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs
+    int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs, 3 grouped
+    int wave_sync = 1;            // wave alignment of the t-grouped kernel
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
     bool b_valid = false;
@@ -310,6 +311,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.raster = C->raster;
         L.group_m = C->group_m;
         L.variant = C->pw_variant;
+        L.wave_counter = C->wave_sync ? reinterpret_cast<unsigned int*>(C->d_err + 32) : nullptr;
         tick(2);
         if ((rc = pointwise_launch(L, st))) return set_err(C, rc, "pointwise launch failed");
         ++C->launches;
@@ -436,7 +438,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
         return MFFTB_ERR_CUDA;
     }
     if (cudaStreamCreateWithFlags(&C->stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaMalloc(&C->d_err, 64) != cudaSuccess) {
+        cudaMalloc(&C->d_err, 256) != cudaSuccess) {
         delete C;
         return MFFTB_ERR_CUDA;
     }
@@ -455,7 +457,8 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_RASTER")) C->raster = atoi(s);
     if (const char* s = getenv("MFFTGPU_GROUP_M")) C->group_m = atoi(s);
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
-    cudaMemset(C->d_err, 0, 64);
+    if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
+    cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
 }
@@ -826,6 +829,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.timeout_ns = C->timeout_ns;
     L.num_sms = C->num_sms;
     L.variant = variant;
+    L.wave_counter = reinterpret_cast<unsigned int*>(C->d_err + 32);
     if ((rc = pointwise_launch(L, C->stream))) return set_err(C, rc, "pointwise launch failed");
     if ((rc = pointwise_check_launch(L, mism, dcnt, C->stream))) return rc;
     rc = mfftgpu_sync(C);

@@ -545,7 +545,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         for (int s = 0; s < PW3_STAGES; ++s) issued_parity[s] = -1;
         const uint32_t tx_bytes = 2 * PW3_STAGE_BYTES;
         const long long first_tile = p.stall_producer ? p.num_tiles : pair;
-        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+        bool align = p.wave_counter != nullptr;
+        long long wave = 0;
+        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag;
+             tile += npairs, ++wave) {
+            if (align && (wave + 1) * npairs <= p.num_tiles) {
+                atomicAdd(p.wave_counter, 1u);
+                const unsigned target = gridDim.x * (unsigned)(wave + 1);
+                const uint64_t dl = global_timer_ns() + 2000000ull;  // 2 ms
+                while (*reinterpret_cast<volatile unsigned*>(p.wave_counter) < target) {
+                    if (global_timer_ns() > dl) {
+                        align = false;  // give up aligning; never wait again
+                        break;
+                    }
+                }
+            }
             int j, t0, mt, nt;
             pw3_tile_decode(p, tile, j, t0, mt, nt);
             const int a_base = j * K;              // Ahat planes of point j (dA = 1)
@@ -748,6 +762,10 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     p.stall_producer = L.stall_producer;
     p.raster = L.raster;
     p.group_m = L.group_m > 0 ? L.group_m : ((pair || grouped) ? PW_GROUP_M / 2 : PW_GROUP_M);
+    p.wave_counter = grouped ? L.wave_counter : nullptr;
+    if (p.wave_counter &&
+        cudaMemsetAsync(p.wave_counter, 0, sizeof(unsigned int), stream) != cudaSuccess)
+        return MFFTB_ERR_CUDA;
 
     CUtensorMap tmA, tmF;
     int rc = make_map(&tmA, L.A, L.kdim, L.rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);

@@ -63,6 +63,11 @@ struct PwParams {
     int stall_producer;  // self-test of the bounded waits: the producer issues nothing
     int raster;          // 0: job-major; 1: point-major, the K*nW*nchunk jobs of a tile innermost
     int group_m;         // row tiles per raster group
+    // Wave alignment (t-grouped kernel): before each full wave of tiles the
+    // producers meet at this zeroed counter so CTAs that share operand tiles
+    // read them at about the same time (L2 reuse).  A timing hint only: a
+    // wait that runs past its deadline switches the alignment off.
+    unsigned int* wave_counter;
 };
 
 // Segment s of job q: which A plane and which F plane feed it.  Shared by

@@ -42,6 +42,7 @@ struct PwLaunch {
     int stall_producer;       // self-test only: see PwParams
     int raster, group_m;      // tile order (see PwParams); 0 = defaults
     int variant;              // 0 auto, 1 one CTA per tile, 2 CTA pairs (256 x 256 tiles)
+    unsigned int* wave_counter;  // optional 4-byte device word for wave alignment (see PwParams)
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);
