@@ -62,6 +62,11 @@ def env_int(k, d):
         return d
 
 
+PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
+              2: "pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)",
+              3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)"}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -518,7 +523,7 @@ def main():
             macs_rank = macs * (wl.rows / n)
             achieved = 2 * macs_rank / (pw_ms * 1e-3) / 1e12
             line["roofline"] = {
-                "bound": "tensor", "kernel": ("pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)" if wl.rows >= 256 and n >= 256 else "pointwise_i8_kernel (tcgen05 kind::i8)"),
+                "bound": "tensor", "kernel": PW_KERNELS.get(pi.get("pw_kernel"), "unknown"),
                 "achieved": achieved, "peak": peak_int8, "unit": "TFLOP/s",
                 "frac": achieved / peak_int8, "traffic": None,
                 "peak_basis": f"2 x bf16_tflops_sustained ({peak_kind} MEASURED_PEAKS.json)",

@@ -50,6 +50,8 @@ typedef struct {
     double inv_bound_log2;
     double int8_macs;        /* issued int8 MACs for the whole n x n product */
     double schoolbook_macs;  /* n^3 * LbA * LbB: the limb-plane schoolbook equivalent */
+    int pw_kernel;           /* plane-product kernel of the last product: 1 one CTA per
+                                tile, 2 CTA pairs, 3 t-grouped CTA pairs; 0 not run */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------

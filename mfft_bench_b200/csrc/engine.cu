@@ -58,6 +58,7 @@ struct mfftgpu_ctx {
         b_trunc = 0;
     Plan last_plan{};
     bool have_plan = false;
+    int last_pw_kernel = 0;
     char msg[512] = {};
 };
 
@@ -312,6 +313,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.group_m = C->group_m;
         L.variant = C->pw_variant;
         L.wave_counter = C->wave_sync ? reinterpret_cast<unsigned int*>(C->d_err + 32) : nullptr;
+        L.chosen = &C->last_pw_kernel;
         tick(2);
         if ((rc = pointwise_launch(L, st))) return set_err(C, rc, "pointwise launch failed");
         ++C->launches;
@@ -561,6 +563,7 @@ int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o)
 int mfftgpu_last_plan(mfftgpu_ctx* C, mfftgpu_plan_info* o) {
     if (!C || !o || !C->have_plan) return MFFTB_ERR_ARG;
     fill_info(C->last_plan, o);
+    o->pw_kernel = C->last_pw_kernel;
     return MFFTB_OK;
 }
 
@@ -588,6 +591,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->inv_bound_log2 = P.inv_bound_log2;
     o->int8_macs = P.macs_per_elem * (double)P.n_int * P.n_int;
     o->schoolbook_macs = (double)n * n * (double)n * P.LbA * P.LbB;
+    o->pw_kernel = 0;
 }
 
 // --------------------------------------------------------------------- integers

@@ -452,7 +452,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
 }
 
 // ---------------------------------------------------------------- t-grouped CTA-pair variant
-// For single-digit plans (nW = nchunk = 1, K a multiple of 4).  The K jobs
+// For plans with one contraction chunk and K a multiple of 4.  A tile group
+// is (point j, digit-weight class w, t0..t0+3); its stages walk the class's
+// digit pairs (da, db) in turn.  The K jobs
 // (j, t) of one evaluation point share their A operand (Ahat_j, all c1) and
 // read overlapping windows of the F stack (plane K-1-t+c1).  A CTA pair
 // computes 4 of them at once -- t = t0..t0+3, one 256 x 128 TMEM accumulator
@@ -471,8 +473,8 @@ constexpr int PW3_F_BYTES = (PW3_BN / 2) * PW_BK;    // one F plane half-tile pe
 constexpr int PW3_STAGE_BYTES = PW3_CPS * PW3_A_BYTES + PW3_NF * PW3_F_BYTES;
 constexpr int PW3_SMEM_BYTES = 1024 + PW3_STAGES * PW3_STAGE_BYTES + 256;
 
-__device__ __forceinline__ void pw3_tile_decode(const PwParams& p, long long tile, int& j, int& t0,
-                                                int& mt, int& nt) {
+__device__ __forceinline__ void pw3_tile_decode(const PwParams& p, long long tile, int& j, int& w,
+                                                int& t0, int& mt, int& nt) {
     const int ngroups = p.jobs.K / PW3_TG;
     const long long per_sj = (long long)p.tiles_m * p.tiles_n;
     const int sj = (int)(tile / per_sj);
@@ -485,8 +487,10 @@ __device__ __forceinline__ void pw3_tile_decode(const PwParams& p, long long til
     const int local = r % group;
     mt = first_m + local % gm;
     nt = local / gm;
-    j = sj / ngroups;
-    t0 = (sj % ngroups) * PW3_TG;
+    j = sj / (p.jobs.nW * ngroups);
+    const int rem = sj % (p.jobs.nW * ngroups);
+    w = rem / ngroups;
+    t0 = (rem % ngroups) * PW3_TG;
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
@@ -512,7 +516,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
     const long long npairs = gridDim.x >> 1;
     const int K = p.jobs.K;
     const int cps_per_kb = K / PW3_CPS;
-    const int steps_per_tile = p.kblocks * cps_per_kb;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PW3_STAGES; ++s) {
@@ -560,10 +563,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                     }
                 }
             }
-            int j, t0, mt, nt;
-            pw3_tile_decode(p, tile, j, t0, mt, nt);
-            const int a_base = j * K;              // Ahat planes of point j (dA = 1)
-            const int f_base = j * (2 * K - 1);    // F planes of point j (dB = 1)
+            int j, w, t0, mt, nt;
+            pw3_tile_decode(p, tile, j, w, t0, mt, nt);
+            const int npr = pw_class_pairs(p.jobs, w);
+            for (int pi = 0; pi < npr; ++pi) {
+            const int da = pw_class_first_da(p.jobs, w) + pi, db = w - da;
+            const int a_base = (j * p.jobs.dA + da) * K;            // Ahat planes (j, da, .)
+            const int f_base = (j * p.jobs.dB + db) * (2 * K - 1);  // F planes (j, db, .)
             for (int cp = 0; cp < cps_per_kb; ++cp) {
                 const int c = cp * PW3_CPS;
                 const int p_lo = K - PW3_TG - t0 + c;
@@ -591,6 +597,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                     }
                 }
             }
+            }
         }
     producer_done:
         for (int s = 0; s < PW3_STAGES; ++s)
@@ -605,6 +612,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         uint32_t phase = 0;
         uint32_t acc_phase = 0;
         for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            int j, w, t0, mt, nt;
+            pw3_tile_decode(p, tile, j, w, t0, mt, nt);
+            const int steps_per_tile = pw_class_pairs(p.jobs, w) * cps_per_kb * p.kblocks;
             if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
@@ -646,8 +656,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         const int quarter = warp & 3;
         uint32_t acc_phase = 0;
         for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
-            int j, t0, mt, nt;
-            pw3_tile_decode(p, tile, j, t0, mt, nt);
+            int j, w, t0, mt, nt;
+            pw3_tile_decode(p, tile, j, w, t0, mt, nt);
             if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
@@ -655,7 +665,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             const int col0 = nt * PW3_BN;
             const int colmax = p.cols - col0;
             for (int tt = 0; tt < PW3_TG; ++tt) {
-                const int q = j * K + t0 + tt;  // job (j, t) with one digit class, one chunk
+                const int q = (j * K + t0 + tt) * p.jobs.nW + w;  // job (j, t, w), one chunk
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
                 for (int c = 0; c < PW3_BN / 32; ++c) {
                     uint32_t v[32];
@@ -734,14 +744,14 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
         return MFFTB_ERR_ARG;
     // t-grouped CTA pairs for single-digit plans, CTA pairs when both
     // dimensions fill at least one 256 x 256 pair tile, single CTAs otherwise
-    const bool grouped_ok = L.jobs.nW == 1 && L.jobs.nchunk == 1 && L.jobs.K % PW3_TG == 0 &&
-                            L.jobs.dA == 1 && L.jobs.dB == 1 && L.rows >= 256 && L.cols >= 128 &&
-                            L.num_sms >= 2;
+    const bool grouped_ok = L.jobs.nchunk == 1 && L.jobs.K % PW3_TG == 0 && L.rows >= 256 &&
+                            L.cols >= 128 && L.num_sms >= 2;
     const bool grouped = L.variant == 3 ? grouped_ok : (L.variant == 0 && grouped_ok);
     if (L.variant == 3 && !grouped_ok) return MFFTB_ERR_ARG;
     const bool pair = !grouped && (L.variant == 2 || (L.variant == 0 && L.block_n == 256 &&
                                                       L.rows >= 256 && L.cols >= 256 &&
                                                       L.num_sms >= 2));
+    if (L.chosen) *L.chosen = grouped ? 3 : (pair ? 2 : 1);
     PwParams p;
     p.jobs = L.jobs;
     p.rows = L.rows;

@@ -41,8 +41,9 @@ struct PwLaunch {
     int num_sms;
     int stall_producer;       // self-test only: see PwParams
     int raster, group_m;      // tile order (see PwParams); 0 = defaults
-    int variant;              // 0 auto, 1 one CTA per tile, 2 CTA pairs (256 x 256 tiles)
+    int variant;              // 0 auto, 1 one CTA per tile, 2 CTA pairs, 3 t-grouped CTA pairs
     unsigned int* wave_counter;  // optional 4-byte device word for wave alignment (see PwParams)
+    int* chosen;              // optional host out: kernel used (1 single CTA, 2 pair, 3 grouped)
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

@@ -39,17 +39,21 @@ def test_pointwise_pair_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA, d
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, nchunk, 256, variant=2) == 0
 
 
-@pytest.mark.parametrize("rows,cols,kdim,NB,K", [
-    (256, 128, 128, 1, 4),
-    (256, 256, 256, 2, 8),
-    (300, 272, 144, 2, 4),
-    (1000, 1008, 1000, 2, 8),
-    (768, 1024, 520, 8, 8),
-    (2048, 2048, 2048, 4, 16),
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,dA,dB", [
+    (256, 128, 128, 1, 4, 1, 1),
+    (256, 256, 256, 2, 8, 1, 1),
+    (300, 272, 144, 2, 4, 1, 1),
+    (1000, 1008, 1000, 2, 8, 1, 1),
+    (768, 1024, 520, 8, 8, 1, 1),
+    (2048, 2048, 2048, 4, 16, 1, 1),
+    (512, 384, 256, 2, 8, 2, 2),
+    (300, 272, 144, 2, 4, 3, 2),
+    (1024, 1024, 512, 2, 16, 2, 2),
 ])
-def test_pointwise_grouped_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K):
-    """The t-grouped CTA-pair variant (4 jobs per tile, shared A and F tiles)."""
-    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 1, 1, 1, 256, variant=3) == 0
+def test_pointwise_grouped_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA, dB):
+    """The t-grouped CTA-pair variant (4 jobs per tile, shared A and F tiles),
+    single- and multi-digit plans."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, 1, 256, variant=3) == 0
 
 
 # ---------------------------------------------------------------- golden fixtures
