@@ -69,6 +69,11 @@ int mfftgpu_sync(mfftgpu_ctx *ctx);
  * range split into several calls.  The caller guarantees B's contents did not
  * change; turning it off drops the cached planes. */
 int mfftgpu_set_reuse_b(mfftgpu_ctx *ctx, int on);
+/* Kernel choice per stage, for comparisons; results are identical.
+ * stage 2 (plane products): 0 auto, 1 one CTA per tile, 2 CTA pairs,
+ *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
+ * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel. */
+int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
 const char *mfftgpu_last_error(mfftgpu_ctx *ctx);
 const char *mfftgpu_status_string(int status);
 int mfftgpu_device_count(void);

@@ -67,6 +67,7 @@ _sig("mfftgpu_set_workspace_limit", i32, vp, sz)
 _sig("mfftgpu_set_timeout_ns", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_sync", i32, vp)
 _sig("mfftgpu_set_reuse_b", i32, vp, i32)
+_sig("mfftgpu_set_kernel_variant", i32, vp, i32, i32)
 _sig("mfftgpu_last_error", C.c_char_p, vp)
 _sig("mfftgpu_status_string", C.c_char_p, i32)
 _sig("mfftgpu_device_count", i32)

@@ -106,6 +106,13 @@ class Context:
         buffer (unchanged contents are the caller's promise)."""
         self._check(lib.mfftgpu_set_reuse_b(self._h, 1 if on else 0), "set_reuse_b")
 
+    def set_kernel_variant(self, stage, variant):
+        """Pick the kernel of a stage ('pointwise' or 'inverse'; 0 = auto).
+        Every variant computes the same bits; this is for comparisons."""
+        sid = {"pointwise": 2, "inverse": 3}[stage]
+        self._check(lib.mfftgpu_set_kernel_variant(self._h, sid, int(variant)),
+                    "set_kernel_variant")
+
     def phase_ms(self):
         out = (C.c_float * 5)()
         lib.mfftgpu_last_phase_ms(self._h, out)

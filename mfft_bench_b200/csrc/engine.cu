@@ -50,6 +50,7 @@ struct mfftgpu_ctx {
     int raster = 0, group_m = 0;  // pointwise tile order (tuning)
     int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs, 3 grouped
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
+    int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
     bool b_valid = false;
@@ -346,6 +347,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         ia.elems = inv_elems(P);
         ia.lgE = log2i(ia.elems);
         ia.err = C->d_err;
+        ia.variant = C->inv_variant;
         tick(3);
         if ((rc = inverse_launch(ia, st))) return set_err(C, rc, "inverse launch failed (%d)", rc);
         ++C->launches;
@@ -460,6 +462,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_GROUP_M")) C->group_m = atoi(s);
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
+    if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
@@ -504,6 +507,19 @@ int mfftgpu_set_reuse_b(mfftgpu_ctx* C, int on) {
     C->reuse_b = on != 0;
     if (!on) C->b_valid = false;
     return MFFTB_OK;
+}
+
+int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
+    if (!C) return MFFTB_ERR_ARG;
+    if (stage == 2 && variant >= 0 && variant <= 3) {
+        C->pw_variant = variant;
+        return MFFTB_OK;
+    }
+    if (stage == 3 && variant >= 0 && variant <= 1) {
+        C->inv_variant = variant;
+        return MFFTB_OK;
+    }
+    return MFFTB_ERR_ARG;
 }
 
 int mfftgpu_set_profile(mfftgpu_ctx* C, int mode) {

@@ -341,6 +341,292 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
     out[(long long)row * a.ldo + col] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
 }
 
+// ---------------------------------------------------------------- lane variant
+// For integer-output plans with K in {8, 16, 32} and NB <= 32 (the W = 256 and
+// W = 1024 configurations).  K lanes own one element: lane c holds coefficient
+// c of all NB transformed ring elements in registers, so the radix-2 DIT
+// butterflies run in registers and each twiddle y^-e (a signed rotation of the
+// coefficients) is one warp shuffle.  The CTA stages its E elements' NB*K
+// values through shared memory first (coalesced 16-byte loads per plane).
+//
+// Carry propagation is split over the element's K lanes: lane s ripples the
+// positions [s*SEG, (s+1)*SEG) with carry-in 0 (pass 1).  With D_s the
+// segment's digits and M = SEG*b, the true carry-out is co_s + delta_s where
+// delta_s = floor((D_s + ci_s) / 2^M) and ci_s = co_{s-1} + delta_{s-1} is the
+// true carry-in.  Because every carry is below 2^(63-b) <= 2^(b*L) with
+// L = floor(62/b) and each segment has more than L digits, delta_s is -1, 0
+// or +1 and is fixed by the low L digits plus whether the higher digits are
+// all ones / all zeros; each lane tabulates delta_s for delta_{s-1} in
+// {-1, 0, 1} and a K-step shuffle chain resolves them.  Pass 2 ripples each
+// segment again from its exact carry-in and emits its 16-bit limbs (segment
+// boundaries sit on limb boundaries: SEG*b is a multiple of 16).
+constexpr int INVL_THREADS = 256;
+constexpr int INVL_UNROLL = 8;  // staging loads in flight per thread
+
+template <int LG>
+__host__ __device__ constexpr int bitrev_c(int j) {
+    int r = 0;
+    for (int i = 0; i < LG; ++i) r |= ((j >> i) & 1) << (LG - 1 - i);
+    return r;
+}
+__host__ __device__ constexpr int ilog2_c(int v) { return v <= 1 ? 0 : 1 + ilog2_c(v >> 1); }
+
+struct InvLaneGeom {
+    int seg;   // positions per lane
+    int pmax;  // (NB + 1) * S fold positions
+};
+
+__host__ __device__ inline int invl_seg(int positions, int K, int b) {
+    const int L = 62 / b;
+    int seg = (positions + K - 1) / K;
+    if (seg < L + 1) seg = L + 1;
+    int tz = 0;
+    while (tz < 4 && !((b >> tz) & 1)) ++tz;
+    const int m = 16 >> tz;  // SEG * b must be a multiple of 16
+    return (seg + m - 1) / m * m;
+}
+
+// One radix-2 DIT stage of butterfly span LEN over the lane's NB values,
+// then the next stage (compile-time recursion keeps every index constant).
+template <int NB, int K, int LEN>
+__device__ __forceinline__ void lane_dit(int64_t (&x)[NB], int c) {
+    if constexpr (LEN <= NB) {
+#pragma unroll
+        for (int st = 0; st < NB; st += LEN) {
+#pragma unroll
+            for (int k = 0; k < LEN / 2; ++k) {
+                const int e0 = (2 * K / LEN) * k;  // twiddle y^-(g (NB/LEN) k), e0 < K
+                int64_t t = x[st + k + LEN / 2];
+                if (e0 != 0) {
+                    // (y^-e0 v)[c] = v[c + e0], negated when c + e0 wraps past K
+                    t = __shfl_sync(0xffffffffu, t, (c + e0) & (K - 1), K);
+                    if (c + e0 >= K) t = -t;
+                }
+                const int64_t u = x[st + k];
+                x[st + k] = u + t;
+                x[st + k + LEN / 2] = u - t;
+            }
+        }
+        lane_dit<NB, K, 2 * LEN>(x, c);
+    }
+}
+
+template <int NB, int K>
+__global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const InvArgs a, int seg,
+                                                                       int vec_out) {
+    constexpr int EPW = 32 / K;                  // elements per warp
+    constexpr int E = (INVL_THREADS / 32) * EPW;  // elements per CTA
+    constexpr int NK = NB * K;
+    constexpr int LD = E + 1;                    // odd stride: conflict-free column reads
+    constexpr int VE = E / 4;
+    constexpr int S = K / 2;
+    constexpr int LGNB = ilog2_c(NB);
+    constexpr int PMAX = (NB + 1) * S;
+    constexpr unsigned FULL = 0xffffffffu;
+    extern __shared__ int64_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long e_base = (long long)blockIdx.x * E;
+    const long long total = (long long)a.rows * a.lda;
+    const int ncls = a.nW * a.nchunk;
+
+    // ---- phase 1: stage [NK][E] int64 = sum over digit classes w and chunks
+    // of 2^(7w) * acc; one pass per (class, chunk) plane set, INVL_UNROLL
+    // 16-byte loads in flight per thread.  Each thread revisits only its own
+    // smem words across passes, so no barrier is needed between them.
+    for (int k = 0; k < ncls; ++k) {
+        const int64_t f = (int64_t)1 << (7 * (k / a.nchunk));
+        for (int idx0 = threadIdx.x; idx0 < NK * VE; idx0 += INVL_UNROLL * INVL_THREADS) {
+            int4 r[INVL_UNROLL];
+#pragma unroll
+            for (int u = 0; u < INVL_UNROLL; ++u) {
+                const int idx = idx0 + u * INVL_THREADS;
+                const int q = idx / VE, v = idx % VE;
+                const long long e = e_base + 4 * v;
+                r[u] = make_int4(0, 0, 0, 0);
+                if (idx < NK * VE && e < total)
+                    r[u] = __ldg(reinterpret_cast<const int4*>(
+                        a.acc + (long long)(q * ncls + k) * a.acc_plane + e));
+            }
+#pragma unroll
+            for (int u = 0; u < INVL_UNROLL; ++u) {
+                const int idx = idx0 + u * INVL_THREADS;
+                if (idx < NK * VE) {
+                    const int q = idx / VE, v = idx % VE;
+                    int64_t* d = sm + q * LD + 4 * v;
+                    const int64_t s0 = (int64_t)r[u].x * f, s1 = (int64_t)r[u].y * f;
+                    const int64_t s2 = (int64_t)r[u].z * f, s3 = (int64_t)r[u].w * f;
+                    if (k == 0) {
+                        d[0] = s0;
+                        d[1] = s1;
+                        d[2] = s2;
+                        d[3] = s3;
+                    } else {
+                        d[0] += s0;
+                        d[1] += s1;
+                        d[2] += s2;
+                        d[3] += s3;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- phase 2: inverse DFT in registers, lane c = coefficient c
+    const int es = lane / K, c = lane % K;
+    const int ei = warp * EPW + es;
+    int64_t x[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) x[j] = sm[(bitrev_c<LGNB>(j) * K + c) * LD + ei];  // DIT order
+    lane_dit<NB, K, 2>(x, c);
+#pragma unroll
+    for (int j = 0; j < NB; ++j) x[j] >>= LGNB;  // exact division by NB
+    __syncthreads();  // staging reads done: the buffer is reused below
+
+    // ---- fold: position beta*S + c (c < S) = C_beta[c] + C_{beta-1}[c + S]
+    int64_t* pb = sm + (long long)warp * EPW * PMAX;  // this warp's [PMAX][EPW]
+#pragma unroll
+    for (int beta = 0; beta <= NB; ++beta) {
+        const int64_t hi = beta >= 1 ? __shfl_down_sync(FULL, x[beta - 1], S, K) : 0;
+        const int64_t lo = beta < NB ? x[beta] : 0;
+        if (c < S) pb[(beta * S + c) * EPW + es] = lo + hi;
+    }
+    __syncwarp();
+
+    // ---- carry: segment c of the element, two passes and a +-1 chain
+    const int P = a.positions, b = a.b, L = 62 / b;
+    const int64_t mask = (int64_t)((1ULL << b) - 1ULL);
+    const int p0 = c * seg;
+    const int p1 = min(P, p0 + seg);
+    const int64_t* mine = pb + es;
+    int64_t carry = 0, dlo = 0;
+    bool ones = true, zeros = true;
+    for (int p = p0, i = 0; p < p1; ++p, ++i) {
+        const int64_t v = mine[p * EPW] + carry;
+        const int64_t d = v & mask;
+        carry = v >> b;
+        if (i < L) {
+            dlo |= d << (b * i);
+        } else {
+            ones &= d == mask;
+            zeros &= d == 0;
+        }
+    }
+    int64_t co_prev = __shfl_up_sync(FULL, carry, 1, K);
+    if (c == 0) co_prev = 0;
+    int tab = 0;
+#pragma unroll
+    for (int xi = 0; xi < 3; ++xi) {
+        const int64_t sum = dlo + co_prev + (xi - 1);
+        const int64_t q = sum >> (b * L);
+        const int d = q >= 1 ? (ones ? 1 : 0) : (q <= -1 ? (zeros ? -1 : 0) : 0);
+        tab |= (d + 1) << (2 * xi);
+    }
+    int delta = 0, delta_prev = 0;
+#pragma unroll
+    for (int s = 1; s < K; ++s) {
+        const int t = __shfl_sync(FULL, tab, s, K);
+        if (c == s) delta_prev = delta;
+        delta = ((t >> (2 * (delta + 1))) & 3) - 1;
+    }
+    carry = c == 0 ? 0 : co_prev + delta_prev;
+
+    uint16_t* ob = reinterpret_cast<uint16_t*>(sm + (long long)E * PMAX);  // [RL][E]
+    const int RL = a.RL;
+    int w = p0 * b / 16;
+    uint64_t bits = 0;
+    int nb = 0;
+    for (int p = p0; p < p1; ++p) {
+        const int64_t v = mine[p * EPW] + carry;
+        bits |= ((uint64_t)v & (uint64_t)mask) << nb;
+        nb += b;
+        carry = v >> b;
+        while (nb >= 16) {
+            if (w < RL) ob[w * E + ei] = (uint16_t)(bits & 0xFFFFu);
+            bits >>= 16;
+            nb -= 16;
+            ++w;
+        }
+    }
+    if (p0 < P && p1 == P) {  // the top segment: sign-extend from the final carry
+        while (w < RL) {
+            const int need = 16 - nb;
+            bits |= ((uint64_t)carry & ((1ULL << need) - 1ULL)) << nb;
+            carry >>= need;
+            ob[w * E + ei] = (uint16_t)(bits & 0xFFFFu);
+            bits = 0;
+            nb = 0;
+            ++w;
+        }
+    }
+    __syncthreads();
+
+    // ---- store the CTA's limbs, plane by plane
+    uint16_t* out = reinterpret_cast<uint16_t*>(a.out);
+    if (vec_out) {  // element e is output index e: 16-byte stores of 8 elements
+        for (int idx = threadIdx.x; idx < RL * (E / 8); idx += INVL_THREADS) {
+            const int wv = idx / (E / 8), v = idx % (E / 8);
+            const long long e = e_base + 8 * v;
+            if (e < total)
+                *reinterpret_cast<uint4*>(out + (long long)wv * a.out_plane + e) =
+                    *reinterpret_cast<const uint4*>(ob + wv * E + 8 * v);
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < RL * E; idx += INVL_THREADS) {
+            const int wv = idx / E, i = idx % E;
+            const long long e = e_base + i;
+            if (e >= total) continue;
+            const int row = (int)(e / a.lda), col = (int)(e % a.lda);
+            if (row >= a.rows || col >= a.cols) continue;
+            out[(long long)wv * a.out_plane + (long long)row * a.ldo + col] = ob[wv * E + i];
+        }
+    }
+}
+
+template <int NB, int K>
+static int launch_lane(const InvArgs& a, cudaStream_t stream) {
+    constexpr int E = (INVL_THREADS / 32) * (32 / K);
+    constexpr int PMAX = (NB + 1) * (K / 2);
+    const size_t stage = (size_t)NB * K * (E + 1) * sizeof(int64_t);
+    const size_t carry = (size_t)E * PMAX * sizeof(int64_t) + (size_t)a.RL * E * sizeof(uint16_t);
+    const size_t smem = (stage > carry ? stage : carry + 16);
+    if (smem > 200 * 1024) return MFFTB_ERR_UNSUPPORTED;
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        if (cudaFuncSetAttribute(inverse_lane_kernel<NB, K>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 200 * 1024) != cudaSuccess)
+            return MFFTB_ERR_CUDA;
+        attr_dev = dev;
+    }
+    const int seg = invl_seg(a.positions, K, a.b);
+    const long long total = (long long)a.rows * a.lda;
+    const int vec_out = a.lda == a.ldo && a.cols == a.lda && a.lda % 8 == 0 &&
+                        a.out_plane % 8 == 0 && reinterpret_cast<uintptr_t>(a.out) % 16 == 0;
+    const long long blocks = (total + E - 1) / E;
+    if (blocks > 0)
+        inverse_lane_kernel<NB, K><<<(unsigned)blocks, INVL_THREADS, smem, stream>>>(a, seg, vec_out);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+// MFFTB_ERR_UNSUPPORTED when the lane variant does not cover the plan
+static int try_lane(const InvArgs& a, cudaStream_t stream) {
+    if (a.out_kind != INV_U16) return MFFTB_ERR_UNSUPPORTED;
+    if (a.positions > (a.NB + 1) * a.S || a.b < 2 || a.b > 15) return MFFTB_ERR_UNSUPPORTED;
+    if (a.lda % 4 || a.acc_plane % 4 || reinterpret_cast<uintptr_t>(a.acc) % 16)
+        return MFFTB_ERR_UNSUPPORTED;
+    if (invl_seg(a.positions, a.K, a.b) * a.K < a.positions) return MFFTB_ERR_UNSUPPORTED;
+#define INVL_CASE(nb, k) \
+    if (a.NB == nb && a.K == k) return launch_lane<nb, k>(a, stream);
+    INVL_CASE(16, 8) INVL_CASE(32, 8)
+    INVL_CASE(4, 16) INVL_CASE(8, 16) INVL_CASE(16, 16) INVL_CASE(32, 16)
+    INVL_CASE(4, 32) INVL_CASE(8, 32) INVL_CASE(16, 32) INVL_CASE(32, 32)
+#undef INVL_CASE
+    return MFFTB_ERR_UNSUPPORTED;
+}
+
 template <int NB, int K>
 static int launch_reg(const InvArgs& a, cudaStream_t stream) {
     const long long total = (long long)a.rows * a.lda;
@@ -366,6 +652,10 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
         if (a.NB == 2 && a.K == 2) return launch_reg<2, 2>(a, stream);
         if (a.NB == 4 && a.K == 2) return launch_reg<4, 2>(a, stream);
         if (a.NB == 2 && a.K == 8) return launch_reg<2, 8>(a, stream);
+    }
+    if (a.variant != 1) {
+        const int rc = try_lane(a, stream);
+        if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
     }
     const size_t smem = (size_t)NK * a.elems * sizeof(int64_t);
     if (smem > 200 * 1024) return MFFTB_ERR_ARG;

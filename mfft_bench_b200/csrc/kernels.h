@@ -74,6 +74,7 @@ struct InvArgs {
     int S_scale;          // INV_F32: SA + SB
     int elems;            // elements per CTA (power of two, <= 32)
     int* err;
+    int variant;          // 0 auto, 1 the generic shared-memory kernel only
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);
 

@@ -56,6 +56,46 @@ def test_pointwise_grouped_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, 1, 256, variant=3) == 0
 
 
+# ---------------------------------------------------------------- the inverse kernels
+@pytest.mark.parametrize("n,L,signed", [
+    (256, 16, True),    # b4 NB16 K16
+    (128, 64, False),   # b8 NB32 K16, 3 digit classes
+    (130, 32, True),    # b4 NB16 K32, padded rows (scalar stores)
+    (64, 128, False),   # b8 NB32 K32
+    (33, 9, True),      # b5 NB8 K16
+    (40, 17, False),    # b9 NB16 K8
+    (24, 25, True),     # b13 NB16 K8, 5 digit classes
+    (17, 113, False),   # b15 NB32 K16
+    (96, 41, True),     # b11 NB8 K32
+    (256, 12, False),   # b6 NB4 K32
+    (20, 49, True),     # b7 NB32 K16
+])
+def test_inverse_lane_kernel_vs_generic_and_oracle(ctx, oracle, n, L, signed):
+    """The lane-parallel inverse (warp-shuffle DFT, segmented carry) against
+    the generic shared-memory kernel and the oracle's exact entries."""
+    plan = m.plan_info(n, 0, 16 * L, 16 * L)
+    assert plan["NB"] * plan["K"] > 64 and plan["K"] in (8, 16, 32) and plan["NB"] <= 32
+    gen = oracle.signed_planes if signed else oracle.bigmat_rand
+    A, B = gen(n, L, 31 + n), gen(n, L, 37 + L)
+    RL = 2 * L + 1
+    got = ctx.mm_u16(A, B, n, L, signed=signed)
+    ctx.set_kernel_variant("inverse", 1)
+    try:
+        ref = ctx.mm_u16(A, B, n, L, signed=signed)
+    finally:
+        ctx.set_kernel_variant("inverse", 0)
+    assert np.array_equal(got, ref)
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 1500)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 1500)]
+    want = oracle.entries(A, B, n, L, signed, rows, cols)
+    assert np.array_equal(got.reshape(RL, n, n)[:, rows, cols], want)
+    # truncated and sign-extended outputs through the lane kernel
+    for rl in (1, L, RL + 3):
+        out = ctx.mm_u16(A, B, n, L, signed=signed, RL=rl)
+        full = oracle.entries(A, B, n, L, signed, rows, cols, max(rl, RL))
+        assert np.array_equal(out.reshape(rl, n, n)[:, rows, cols], full[:rl]), rl
+
+
 # ---------------------------------------------------------------- golden fixtures
 @pytest.mark.parametrize("n,L", [(8, 8), (16, 64), (48, 16)])
 def test_unsigned_fixture(ctx, n, L):
