@@ -62,6 +62,16 @@ def env_int(k, d):
         return d
 
 
+# DRAM bytes (read + write) of one pointwise launch, from a one-pass ncu
+# capture of dram__bytes_read.sum / dram__bytes_write.sum on the full
+# workload (profiles/pointwise3_i8_c5_dram.md).
+POINTWISE_TRAFFIC = {
+    "c5": {"bytes_per_launch": 1.02e12 + 52.27e9,
+           "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows): "
+                    "1.02 TB read + 52.3 GB written; algorithmic operand bytes of that "
+                    "launch 43.9 GB read + 46.7 GB of int32 job planes written")},
+}
+
 PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
               2: "pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)",
               3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)"}
@@ -534,13 +544,11 @@ def main():
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share
-    traffic_path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
-    if "roofline" in line and os.path.exists(traffic_path):
-        with open(traffic_path) as f:
-            tr = json.load(f).get(args.workload)
-        if tr:
-            line["roofline"]["traffic"] = tr["bytes_per_launch"]
-            line["roofline"]["traffic_note"] = tr.get("note")
+    tr = POINTWISE_TRAFFIC.get(args.workload)
+    if ("roofline" in line and tr and world == 1 and n == WORKLOADS[args.workload]["n"]
+            and pi.get("pw_kernel") == 3):
+        line["roofline"]["traffic"] = tr["bytes_per_launch"]
+        line["roofline"]["traffic_note"] = tr["note"]
 
     if world == 1 and "roofline" in line and not args.no_int8_ref:
         ref_tops = cublas_int8_sustained(torch, stream)
