@@ -142,11 +142,13 @@ def cpu_count():
 
 
 # ---------------------------------------------------------------------------- reference CPU work
-def _ref_sample(workload, n_s, reps):
+def _ref_sample(workload, n_s, reps, method="mfft"):
     """Run the reference's own CPU hot path (oracle/_ref, compiled from the
     reference sources) once on a sample of the workload; returns seconds of
     the reference's timed region (the product; encode/decode excluded as in
-    src/mlgemm.c:1103-1106)."""
+    src/mlgemm.c:1103-1106).  method "schoolbook" times the reference's
+    limb-plane comparator (conv_limbplane / mm_limbplane, src/methods.c:94-123)
+    instead of its MFFT."""
     import numpy as np
     from oracle.oracle import Oracle, RefLib
     r, o = RefLib(), Oracle()
@@ -166,9 +168,15 @@ def _ref_sample(workload, n_s, reps):
             A32, B32 = o.signlimb(A, n_s, L), o.signlimb(B, n_s, L)
         for _ in range(reps):
             t0 = time.perf_counter()
-            if signed:  # conv_mfft + normalize_planes (the reference's signed route)
-                cw = r.conv_mfft(A32, B32, n_s, L)
+            if signed:  # conv + normalize_planes (the reference's signed route)
+                if method == "schoolbook":
+                    cw = np.zeros((2 * L - 1) * n_s * n_s, np.int64)
+                    r.lib.conv_limbplane(cw, A32, B32, n_s, L, 2)
+                else:
+                    cw = r.conv_mfft(A32, B32, n_s, L)
                 r.normalize_planes(cw, 2 * L - 1, n_s, RL_OF(L))
+            elif method == "schoolbook":
+                r.mm_limbplane(A, B, n_s, L)
             else:
                 r.mm_mfft(A, B, n_s, L)
             best = min(best, time.perf_counter() - t0)
@@ -186,15 +194,18 @@ def _ref_sample(workload, n_s, reps):
         plan = r.plan(c.L)
         for _ in range(reps):
             t0 = time.perf_counter()
-            r.lib.conv_mfft(cw, A32, B32, n_s, c.L, C.byref(plan), 2)
+            if method == "schoolbook":
+                r.lib.conv_limbplane(cw, A32, B32, n_s, c.L, 2)
+            else:
+                r.lib.conv_mfft(cw, A32, B32, n_s, c.L, C.byref(plan), 2)
             best = min(best, time.perf_counter() - t0)
         r.lib.fpx_free(C.byref(c))
     return best
 
 
 def _ref_worker(args):
-    workload, n_s = args
-    return _ref_sample(workload, n_s, 1)
+    workload, n_s, method = args
+    return _ref_sample(workload, n_s, 1, method)
 
 
 def reference_line(args):
@@ -210,20 +221,21 @@ def reference_line(args):
     with ctx.Pool(T) as pool:
         for step in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            pool.map(_ref_worker, [(args.workload, n_s)] * T)
+            pool.map(_ref_worker, [(args.workload, n_s, args.method)] * T)
             dt = time.perf_counter() - t0
             if step >= args.warmup:
                 times.append(dt)
     per_round = statistics.mean(times)
     value = per_round * scale / T
-    sample = (f"reference conv path (oracle/_ref, packed leaf) at n={n_s}, {T} concurrent "
+    what = "limb-plane schoolbook" if args.method == "schoolbook" else "conv path"
+    sample = (f"reference {what} (oracle/_ref, packed leaf) at n={n_s}, {T} concurrent "
               f"processes per step, scaled by (n/{n_s})^3 = {scale:.0f}")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": per_round * 1e3, "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "int64", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
-                       "sample_n": n_s},
+                       "sample_n": n_s, "method": args.method},
             "cpu_baseline": {"value": value, "unit": "s", "cores": T, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": value, "unit": "s", "h2d_bytes_per_step": 0,
@@ -443,6 +455,9 @@ def main():
     ap.add_argument("--subblocks", type=int, default=1,
                     help="row sub-blocks per rank whose gathers overlap the next block's compute")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--method", default="mfft", choices=["mfft", "schoolbook"],
+                    help="mfft: the MFFT hot path (the headline); schoolbook: the limb-plane "
+                         "comparator on the same tensor-core kernel")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     global SUBBLOCKS
@@ -472,6 +487,7 @@ def main():
                                 device_id=device)
     stream = torch.cuda.current_stream()
     ctx = m.Context(local_rank, stream=stream)
+    ctx.set_method(args.method)
     wl = Workload(args.workload, ctx, torch, rank, world, device)
 
     def barrier():
@@ -521,7 +537,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8", "data": "synthetic (seeded splitmix64, reference generators)",
-            "config": {"workload": args.workload, "desc": w["desc"], "n": n,
+            "config": {"workload": args.workload, "desc": w["desc"], "n": n, "method": args.method,
                        "parallelism": f"row-blocks x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (no flush needed)"},
             "gpu_launches": (launches_per_step or 0) * args.steps,
@@ -563,11 +579,12 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             n_s = CPU_SAMPLE_N[args.workload]
-            t = _ref_sample(args.workload, n_s, 2)
+            t = _ref_sample(args.workload, n_s, 2, args.method)
             scale = (n / n_s) ** 3
             line["cpu_baseline"] = {
                 "value": t * scale, "unit": "s", "cores": 1, "kind": "reference",
-                "sample": (f"reference conv path (oracle/_ref, packed leaf, single thread as in "
+                "sample": (f"reference {'limb-plane schoolbook' if args.method == 'schoolbook' else 'conv path'} "
+                           f"(oracle/_ref, packed leaf, single thread as in "
                            f"the reference) at n={n_s}: {t:.3f} s, scaled by (n/{n_s})^3 = "
                            f"{scale:.0f}")}
         except Exception as e:  # the baseline is reported, never required

@@ -125,6 +125,20 @@ void mm_mfft_signed(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, uint
  * without the host round trip of the limb planes) */
 int fpx_gemm_f32(const float *A, const float *B, int n, int force_bits, float *C);
 
+/* The limb-plane schoolbook method on the same tensor-core kernel: exact,
+ * bit-identical to the MFFT entry points, with LbA*LbB digit-plane products
+ * instead of the transform's NB*K^2 (the reference's comparator rows:
+ * mm_limbplane / conv_limbplane src/methods.c:94-123 declared at
+ * src/mfftbench.h:100-106, and the GPU limb-*-exact rows of
+ * cuda/gemm_bench.cu:913-998). */
+void mm_limbplane(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, kernel_t k,
+                  uint16_t *out, int RL);                       /* src/methods.c:106-123 */
+void conv_limbplane(int64_t *Cw, const int32_t *A32, const int32_t *B32, int n, int L,
+                    kernel_t k);                                /* src/methods.c:94-104 */
+void mm_limbplane_signed(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, uint16_t *out,
+                         int RL);
+int fpx_gemm_f32_limbplane(const float *A, const float *B, int n, int force_bits, float *C);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,9 @@ typedef struct {
     double schoolbook_macs;  /* n^3 * LbA * LbB: the limb-plane schoolbook equivalent */
     int pw_kernel;           /* plane-product kernel of the last product: 1 one CTA per
                                 tile, 2 CTA pairs, 3 t-grouped CTA pairs; 0 not run */
+    int kind;                /* 0 MFFT; 1 limb-plane schoolbook (NB = 1, no transform:
+                                job t of chunk ch sums A_u B_(t-u), u in [ch*U, ch*U+U)) */
+    int U;                   /* schoolbook: digit planes of A per contraction chunk */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -69,6 +72,14 @@ int mfftgpu_sync(mfftgpu_ctx *ctx);
  * range split into several calls.  The caller guarantees B's contents did not
  * change; turning it off drops the cached planes. */
 int mfftgpu_set_reuse_b(mfftgpu_ctx *ctx, int on);
+/* Product method for value-mode products (mm_u16, mm_i64, fp32):
+ * 0 MFFT (default); 1 limb-plane schoolbook on the same tensor-core kernel
+ * (digit-plane products A_u B_v accumulated per output position, no
+ * transform) -- the GPU counterpart of the reference's mm_limbplane and
+ * limb-*-exact rows.  Limb-mode conv always uses MFFT.  Results are
+ * bit-identical either way. */
+int mfftgpu_set_method(mfftgpu_ctx *ctx, int method);
+int mfftgpu_get_method(mfftgpu_ctx *ctx);
 /* Kernel choice per stage, for comparisons; results are identical.
  * stage 2 (plane products): 0 auto, 1 one CTA per tile, 2 CTA pairs,
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
@@ -79,7 +90,8 @@ const char *mfftgpu_status_string(int status);
 int mfftgpu_device_count(void);
 
 /* Plan the product (mode 0: value re-radix, 1: limb mode as used by
- * conv_mfft).  wA/wB: magnitude bits (mode 0) or limb counts (mode 1). */
+ * conv_mfft, 2: value re-radix with the limb-plane schoolbook method).
+ * wA/wB: magnitude bits (modes 0, 2) or limb counts (mode 1). */
 int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info *out);
 /* The plan of the last product run on this context (the fp32 plan depends on
  * the exponent window of the data). */
@@ -164,11 +176,15 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * the given job shape, the kernel's int32 job planes compared element by
  * element with a CUDA-core evaluation of the same job table.  variant: 0 the
  * product path's choice, 1 one CTA per 128-row tile, 2 CTA pairs (256-row
- * tiles, tcgen05 cta_group::2).  *mismatches receives the number of
- * differing elements. */
+ * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs.  *mismatches receives
+ * the number of differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,
                                long long *mismatches);
+/* The same check for the schoolbook job table: LbA / LbB random int8 digit
+ * planes, chunks of U planes of A, every job (t, ch) with a term compared. */
+int mfftgpu_selftest_school(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int LbA, int LbB,
+                            int U, long long *mismatches);
 
 /* Self-test of the bounded device waits: launches the pointwise kernel with
  * a producer that never loads, so its consumers must give up after

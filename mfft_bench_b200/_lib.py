@@ -31,7 +31,8 @@ class PlanInfo(C.Structure):
                 ("n", "n_int", "mode", "b", "LbA", "LbB", "S", "NB", "K", "g", "ncA", "ncB",
                  "dA", "dB", "nW", "nchunk", "njobs", "positions")] + [
         ("acc_bound", C.c_longlong), ("inv_bound_log2", C.c_double),
-        ("int8_macs", C.c_double), ("schoolbook_macs", C.c_double), ("pw_kernel", C.c_int)]
+        ("int8_macs", C.c_double), ("schoolbook_macs", C.c_double), ("pw_kernel", C.c_int),
+        ("kind", C.c_int), ("U", C.c_int)]
 
     def as_dict(self):
         return {f: getattr(self, f) for f, _ in self._fields_}
@@ -68,6 +69,8 @@ _sig("mfftgpu_set_timeout_ns", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_sync", i32, vp)
 _sig("mfftgpu_set_reuse_b", i32, vp, i32)
 _sig("mfftgpu_set_kernel_variant", i32, vp, i32, i32)
+_sig("mfftgpu_set_method", i32, vp, i32)
+_sig("mfftgpu_get_method", i32, vp)
 _sig("mfftgpu_last_error", C.c_char_p, vp)
 _sig("mfftgpu_status_string", C.c_char_p, i32)
 _sig("mfftgpu_device_count", i32)
@@ -92,6 +95,7 @@ _sig("mfftgpu_mm_i64_noalloc", i32, vp, vp, i32, vp, i32, vp)
 _sig("mfftgpu_decode_words_f32", C.c_float, vp, i32, i32, i32)
 _sig("mfftgpu_selftest_pointwise", i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
      C.POINTER(C.c_longlong))
+_sig("mfftgpu_selftest_school", i32, vp, i32, i32, i32, i32, i32, i32, C.POINTER(C.c_longlong))
 
 # reference-compatible ABI
 _sig("kernel_name", C.c_char_p, i32)
@@ -110,6 +114,10 @@ _sig("fpx_encode", None, C.POINTER(FpxCtx), vp, vp)
 _sig("fpx_decode_f32", None, C.POINTER(FpxCtx), vp)
 _sig("fpx_free", None, C.POINTER(FpxCtx))
 _sig("fpx_gemm_f32", i32, vp, vp, i32, i32, vp)
+_sig("mm_limbplane", None, vp, vp, i32, i32, i32, vp, i32)
+_sig("mm_limbplane_signed", None, vp, vp, i32, i32, vp, i32)
+_sig("conv_limbplane", None, vp, vp, vp, i32, i32, i32)
+_sig("fpx_gemm_f32_limbplane", i32, vp, vp, i32, i32, vp)
 _sig("mfftb_last_status", i32)
 
 

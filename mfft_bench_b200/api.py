@@ -106,6 +106,12 @@ class Context:
         buffer (unchanged contents are the caller's promise)."""
         self._check(lib.mfftgpu_set_reuse_b(self._h, 1 if on else 0), "set_reuse_b")
 
+    def set_method(self, method):
+        """'mfft' (default) or 'schoolbook' (limb-plane digit products on the
+        same tensor-core kernel) for value-mode products; identical results."""
+        mid = {"mfft": 0, "schoolbook": 1}[method]
+        self._check(lib.mfftgpu_set_method(self._h, mid), "set_method")
+
     def set_kernel_variant(self, stage, variant):
         """Pick the kernel of a stage ('pointwise' or 'inverse'; 0 = auto).
         Every variant computes the same bits; this is for comparisons."""
@@ -210,6 +216,14 @@ class Context:
                     "selftest_pointwise")
         return mism.value
 
+    def selftest_school(self, rows, cols, kdim, LbA, LbB, U):
+        """Mismatching elements of the schoolbook job table on the tensor-core
+        kernel vs a CUDA-core evaluation (expected 0)."""
+        mism = C.c_longlong(-1)
+        self._check(lib.mfftgpu_selftest_school(self._h, rows, cols, kdim, LbA, LbB, U,
+                                                C.byref(mism)), "selftest_school")
+        return mism.value
+
     def selftest_timeout(self, timeout_ns=50_000_000):
         """Status of a pointwise launch whose producer never loads (expected:
         MFFTGPU_ERR_TIMEOUT = 4, and the context stays usable)."""
@@ -307,6 +321,42 @@ def fpx_gemm_f32(A, B, n, force_bits=512):
     rc = lib.fpx_gemm_f32(_ptr(A), _ptr(B), n, force_bits, _ptr(out))
     if rc:
         raise MfftError(rc, "fpx_gemm_f32")
+    return out
+
+
+def mm_limbplane(Apl, Bpl, n, L, kernel=KERNEL_SM100, RL=None):
+    """src/methods.c:106-123 through the drop-in C symbol ``mm_limbplane``
+    (schoolbook digit-plane products on the tensor cores)."""
+    RL = 2 * L + 1 if RL is None else RL
+    out = np.zeros(RL * n * n, np.uint16)
+    lib.mm_limbplane(_ptr(Apl), _ptr(Bpl), n, L, kernel, _ptr(out), RL)
+    _status("mm_limbplane")
+    return out
+
+
+def mm_limbplane_signed(Apl, Bpl, n, L, RL=None):
+    RL = 2 * L + 1 if RL is None else RL
+    out = np.zeros(RL * n * n, np.uint16)
+    lib.mm_limbplane_signed(_ptr(Apl), _ptr(Bpl), n, L, _ptr(out), RL)
+    _status("mm_limbplane_signed")
+    return out
+
+
+def conv_limbplane(A32, B32, n, L, kernel=KERNEL_SM100):
+    """src/methods.c:94-104 through the drop-in C symbol ``conv_limbplane``."""
+    cw = np.zeros((2 * L - 1) * n * n, np.int64)
+    lib.conv_limbplane(_ptr(cw), _ptr(A32), _ptr(B32), n, L, kernel)
+    _status("conv_limbplane")
+    return cw
+
+
+def fpx_gemm_f32_limbplane(A, B, n, force_bits=512):
+    out = np.empty(n * n, np.float32)
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    rc = lib.fpx_gemm_f32_limbplane(_ptr(A), _ptr(B), n, force_bits, _ptr(out))
+    if rc:
+        raise MfftError(rc, "fpx_gemm_f32_limbplane")
     return out
 
 

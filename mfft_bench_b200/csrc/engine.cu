@@ -51,12 +51,13 @@ struct mfftgpu_ctx {
     int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs, 3 grouped
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
     int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
+    int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
     bool b_valid = false;
     const void* b_ptr = nullptr;
     int b_fmt = -1, b_n = 0, b_b = 0, b_Lb = 0, b_S = 0, b_NB = 0, b_dB = 0, b_lo = 0, b_sgrid = 0,
-        b_trunc = 0;
+        b_trunc = 0, b_kind = 0;
     Plan last_plan{};
     bool have_plan = false;
     int last_pw_kernel = 0;
@@ -138,8 +139,11 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     const long long nn_int = (long long)n_int * n_int;
     const int rows = row_end - row_begin;
     if (rows <= 0) return MFFTB_OK;
-    const int fpl = P.NB * P.dB * (2 * P.K - 1);
-    const int apl = P.NB * P.dA * P.K;
+    // schoolbook plans multiply the digit planes themselves: no transform,
+    // no F stack, no A-hat planes
+    const bool school = P.kind == KIND_SCHOOL;
+    const int fpl = school ? 0 : P.NB * P.dB * (2 * P.K - 1);
+    const int apl = school ? 0 : P.NB * P.dA * P.K;
     const size_t szDB = align256((size_t)P.LbB * nn_int * dbytes);
     const size_t szF = align256((size_t)fpl * nn_int);
     const size_t per_row = (size_t)n_int * ((size_t)P.LbA * dbytes + apl + 4 * (size_t)P.njobs);
@@ -159,7 +163,8 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     int rc = ensure(C, &C->ws, &C->ws_bytes, szDB + szF + szDA + szAh + szAcc);
     if (rc) return rc;
     if (C->ws_bytes != had) C->b_valid = false;  // reallocated: the cached F is gone
-    const bool b_cached = C->reuse_b && C->b_valid && C->b_ptr == B.p && C->b_fmt == B.fmt &&
+    const bool b_cached = C->reuse_b && C->b_valid && C->b_kind == P.kind && C->b_ptr == B.p &&
+                          C->b_fmt == B.fmt &&
                           C->b_n == P.n && C->b_b == P.b && C->b_Lb == P.LbB && C->b_S == P.S &&
                           C->b_NB == P.NB && C->b_dB == P.dB && C->b_lo == B.lo_bit &&
                           C->b_sgrid == B.S_grid && C->b_trunc == B.trunc_rel;
@@ -234,11 +239,14 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         if ((rc = pack_launch(pb, st))) return set_err(C, rc, "pack(B) launch failed");
         ++C->launches;
         tock();
-        tick(1);
-        if ((rc = forward_launch(fb, st))) return set_err(C, rc, "forward(B) launch failed");
-        ++C->launches;
-        tock();
+        if (!school) {
+            tick(1);
+            if ((rc = forward_launch(fb, st))) return set_err(C, rc, "forward(B) launch failed");
+            ++C->launches;
+            tock();
+        }
         C->b_valid = true;
+        C->b_kind = P.kind;
         C->b_ptr = B.p;
         C->b_fmt = B.fmt;
         C->b_n = P.n;
@@ -285,24 +293,26 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         fa.f_stack = 0;
         fa.out = Ah;
         fa.oplane = R * n_int;
-        tick(1);
-        if ((rc = forward_launch(fa, st))) return set_err(C, rc, "forward(A) launch failed");
-        ++C->launches;
-        tock();
+        if (!school) {
+            tick(1);
+            if ((rc = forward_launch(fa, st))) return set_err(C, rc, "forward(A) launch failed");
+            ++C->launches;
+            tock();
+        }
 
         PwLaunch L{};
-        L.A = Ah;
+        L.A = school ? reinterpret_cast<const int8_t*>(DA) : Ah;
         L.lda = n_int;
         L.a_plane_bytes = R * n_int;
-        L.a_planes = apl;
-        L.F = F;
+        L.a_planes = school ? P.LbA : apl;
+        L.F = school ? reinterpret_cast<const int8_t*>(DB) : F;
         L.ldf = n_int;
         L.f_plane_bytes = nn_int;
-        L.f_planes = fpl;
+        L.f_planes = school ? P.LbB : fpl;
         L.rows = rb;
         L.cols = n_int;
         L.kdim = n_int;
-        L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs};
+        L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs, school ? 1 : 0, P.LbA, P.LbB, P.U};
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
         L.out = acc;
         L.out_plane = R * n_int;
@@ -348,6 +358,10 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         ia.lgE = log2i(ia.elems);
         ia.err = C->d_err;
         ia.variant = C->inv_variant;
+        ia.school = school ? 1 : 0;
+        ia.LbA = P.LbA;
+        ia.LbB = P.LbB;
+        ia.U = P.U;
         tick(3);
         if ((rc = inverse_launch(ia, st))) return set_err(C, rc, "inverse launch failed (%d)", rc);
         ++C->launches;
@@ -363,6 +377,10 @@ int check_rows(int n, int row_begin, int row_end) {
 }
 
 int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P) {
+    // the schoolbook method covers value-mode products; limb mode (conv)
+    // always runs the MFFT plan
+    if (C->method == 1 && mode == PLAN_VALUE && plan_search_school(n, wA, wB, 0, P) == 0)
+        return MFFTB_OK;
     int rc = plan_search(n, mode, wA, wB, 0, 0, P);
     if (rc)
         return set_err(C, MFFTB_ERR_PLAN, "no exact int8 plan for n=%d mode=%d widths %d/%d", n,
@@ -463,6 +481,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
+    if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
     cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
@@ -508,6 +527,14 @@ int mfftgpu_set_reuse_b(mfftgpu_ctx* C, int on) {
     if (!on) C->b_valid = false;
     return MFFTB_OK;
 }
+
+int mfftgpu_set_method(mfftgpu_ctx* C, int method) {
+    if (!C || method < 0 || method > 1) return MFFTB_ERR_ARG;
+    C->method = method;
+    return MFFTB_OK;
+}
+
+int mfftgpu_get_method(mfftgpu_ctx* C) { return C ? C->method : -1; }
 
 int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
     if (!C) return MFFTB_ERR_ARG;
@@ -571,7 +598,11 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o);
 int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o) {
     if (!o) return MFFTB_ERR_ARG;
     Plan P;
-    if (plan_search(n, mode, wA, wB, 0, 0, &P)) return MFFTB_ERR_PLAN;
+    if (mode == 2) {
+        if (plan_search_school(n, wA, wB, 0, &P)) return MFFTB_ERR_PLAN;
+    } else if (plan_search(n, mode, wA, wB, 0, 0, &P)) {
+        return MFFTB_ERR_PLAN;
+    }
     fill_info(P, o);
     return MFFTB_OK;
 }
@@ -608,6 +639,8 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->int8_macs = P.macs_per_elem * (double)P.n_int * P.n_int;
     o->schoolbook_macs = (double)n * n * (double)n * P.LbA * P.LbB;
     o->pw_kernel = 0;
+    o->kind = P.kind;
+    o->U = P.U;
 }
 
 // --------------------------------------------------------------------- integers
@@ -849,6 +882,63 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.timeout_ns = C->timeout_ns;
     L.num_sms = C->num_sms;
     L.variant = variant;
+    L.wave_counter = reinterpret_cast<unsigned int*>(C->d_err + 32);
+    if ((rc = pointwise_launch(L, C->stream))) return set_err(C, rc, "pointwise launch failed");
+    if ((rc = pointwise_check_launch(L, mism, dcnt, C->stream))) return rc;
+    rc = mfftgpu_sync(C);
+    if (rc) return rc;
+    int h = 0;
+    CUDA_OK(cudaMemcpy(&h, mism, sizeof h, cudaMemcpyDeviceToHost));
+    *mismatches = h;
+    return MFFTB_OK;
+}
+
+int mfftgpu_selftest_school(mfftgpu_ctx* C, int rows, int cols, int kdim, int LbA, int LbB,
+                            int U, long long* mismatches) {
+    if (!C || !mismatches || rows <= 0 || cols <= 0 || kdim <= 0 || cols % 16 || LbA < 1 ||
+        LbB < 1 || U < 1)
+        return MFFTB_ERR_ARG;
+    // random digits in [-128, 127]: a chunk of U plane products must fit int32
+    if ((long long)kdim * U * 16384LL > 2147483647LL) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const int ld = (kdim + 15) / 16 * 16;
+    const int T = (LbA + LbB - 1 + 3) / 4 * 4;
+    const int nchunk = (LbA + U - 1) / U;
+    PwJobs J{T, 1, 1, 1, nchunk, T * nchunk, 1, LbA, LbB, U};
+    const size_t szA = align256((size_t)LbA * rows * ld), szF = align256((size_t)LbB * cols * ld);
+    const size_t szO = align256((size_t)J.njobs * rows * cols * 4);
+    int rc = ensure(C, &C->ws, &C->ws_bytes, szA + szF + szO + 256);
+    if (rc) return rc;
+    C->b_valid = false;
+    int8_t* A = reinterpret_cast<int8_t*>(C->ws);
+    int8_t* F = A + szA;
+    int32_t* out = reinterpret_cast<int32_t*>(F + szF);
+    long long* dcnt = reinterpret_cast<long long*>(reinterpret_cast<char*>(out) + szO);
+    int* mism = C->d_err + 8;
+    gen_u16_kernel<<<C->num_sms * 4, 256, 0, C->stream>>>(reinterpret_cast<uint16_t*>(A),
+                                                          (long long)(szA + szF) / 2, 0x5C001ull);
+    CUDA_OK(cudaGetLastError());
+    CUDA_OK(cudaMemsetAsync(C->d_err, 0, 64, C->stream));
+    PwLaunch L{};
+    L.A = A;
+    L.lda = ld;
+    L.a_plane_bytes = (long long)rows * ld;
+    L.a_planes = LbA;
+    L.F = F;
+    L.ldf = ld;
+    L.f_plane_bytes = (long long)cols * ld;
+    L.f_planes = LbB;
+    L.rows = rows;
+    L.cols = cols;
+    L.kdim = kdim;
+    L.jobs = J;
+    L.block_n = 128;
+    L.out = out;
+    L.out_plane = (long long)rows * cols;
+    L.ldo = cols;
+    L.err = C->d_err;
+    L.timeout_ns = C->timeout_ns;
+    L.num_sms = C->num_sms;
     L.wave_counter = reinterpret_cast<unsigned int*>(C->d_err + 32);
     if ((rc = pointwise_launch(L, C->stream))) return set_err(C, rc, "pointwise launch failed");
     if ((rc = pointwise_check_launch(L, mism, dcnt, C->stream))) return rc;

@@ -635,7 +635,10 @@ static int launch_reg(const InvArgs& a, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
+static int school_carry_launch(const InvArgs& a, cudaStream_t stream);
+
 int inverse_launch(const InvArgs& a, cudaStream_t stream) {
+    if (a.school) return school_carry_launch(a, stream);
     const int NK = a.NB * a.K;
     if (a.elems < 1 || a.elems > 32 || NK * a.elems > INV_VPT * INV_THREADS) return MFFTB_ERR_ARG;
     if ((1 << a.log2NB) != a.NB || (1 << a.lgS) != a.S || (1 << a.lgK) != a.K ||
@@ -670,6 +673,109 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     const long long blocks = (total + a.elems - 1) / a.elems;
     if (blocks <= 0) return MFFTB_OK;
     inverse_kernel<<<(unsigned)blocks, INV_THREADS, smem, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- schoolbook carry
+// Schoolbook plans have no transform: position t of the product is
+// C_t = sum over the live chunks of job plane (t, ch).  One thread per
+// element streams the positions (coalesced across the warp), carries in
+// radix 2^b and formats the output as the other inverse kernels do.
+constexpr int SC_THREADS = 256;
+constexpr int SC_UNROLL = 8;
+
+__device__ __forceinline__ bool school_live(const InvArgs& a, int t, int ch) {
+    int lo = ch * a.U;
+    if (t - (a.LbB - 1) > lo) lo = t - (a.LbB - 1);
+    int hi = ch * a.U + a.U - 1;
+    if (t < hi) hi = t;
+    if (a.LbA - 1 < hi) hi = a.LbA - 1;
+    return lo <= hi;
+}
+
+__global__ void __launch_bounds__(SC_THREADS) school_carry_kernel(const InvArgs a) {
+    const long long e = blockIdx.x * (long long)SC_THREADS + threadIdx.x;
+    const long long total = (long long)a.rows * a.lda;
+    if (e >= total) return;
+    const int row = (int)(e / a.lda), col = (int)(e % a.lda);
+    if (row >= a.rows || col >= a.cols) return;
+    const long long o = (long long)row * a.ldo + col;
+    const int P = a.positions, b = a.b;
+    const uint64_t mask = (1ULL << b) - 1ULL;
+    int64_t carry = 0;
+    uint64_t bits = 0;
+    int nb = 0, w = 0;
+    uint32_t words[INV_MAXW];
+    int nw = 0;
+    uint16_t* out16 = reinterpret_cast<uint16_t*>(a.out);
+    for (int t0 = 0; t0 < P; t0 += SC_UNROLL) {
+        int64_t v[SC_UNROLL];
+#pragma unroll
+        for (int i = 0; i < SC_UNROLL; ++i) {
+            v[i] = 0;
+            const int t = t0 + i;
+            if (t < P)
+                for (int ch = 0; ch < a.nchunk; ++ch)
+                    if (school_live(a, t, ch))
+                        v[i] += __ldg(a.acc + (long long)(t * a.nchunk + ch) * a.acc_plane + e);
+        }
+#pragma unroll
+        for (int i = 0; i < SC_UNROLL; ++i) {
+            if (t0 + i >= P) break;
+            const int64_t x = v[i] + carry;
+            bits |= ((uint64_t)x & mask) << nb;
+            nb += b;
+            carry = x >> b;
+            if (a.out_kind == INV_U16) {
+                while (nb >= 16 && w < a.RL) {
+                    out16[(long long)w * a.out_plane + o] = (uint16_t)(bits & 0xFFFFu);
+                    bits >>= 16;
+                    nb -= 16;
+                    ++w;
+                }
+                if (nb >= 16) {  // past RL: drop the bits
+                    bits >>= 16;
+                    nb -= 16;
+                }
+            } else if (nb >= 32) {
+                if (nw < INV_MAXW) words[nw++] = (uint32_t)bits;
+                bits >>= 32;
+                nb -= 32;
+            }
+        }
+    }
+    if (a.out_kind == INV_U16) {
+        while (w < a.RL) {
+            const int need = 16 - nb;
+            bits |= ((uint64_t)carry & ((1ULL << need) - 1ULL)) << nb;
+            carry >>= need;
+            out16[(long long)w * a.out_plane + o] = (uint16_t)(bits & 0xFFFFu);
+            bits = 0;
+            nb = 0;
+            ++w;
+        }
+        return;
+    }
+    for (int k = 0; k < 3 && nw < INV_MAXW; ++k) {
+        const int need = 32 - nb;
+        bits |= ((uint64_t)carry & ((1ULL << need) - 1ULL)) << nb;
+        carry >>= need;
+        words[nw++] = (uint32_t)bits;
+        bits = 0;
+        nb = 0;
+    }
+    float* out = reinterpret_cast<float*>(a.out);
+    out[o] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
+}
+
+static int school_carry_launch(const InvArgs& a, cudaStream_t stream) {
+    if (a.out_kind == INV_I64) return MFFTB_ERR_UNSUPPORTED;
+    if (a.b < 1 || a.b > 15 || a.nchunk < 1 || a.U < 1) return MFFTB_ERR_ARG;
+    if (a.out_kind == INV_F32 && (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
+        return MFFTB_ERR_UNSUPPORTED;
+    const long long total = (long long)a.rows * a.lda;
+    const long long blocks = (total + SC_THREADS - 1) / SC_THREADS;
+    if (blocks > 0) school_carry_kernel<<<(unsigned)blocks, SC_THREADS, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 

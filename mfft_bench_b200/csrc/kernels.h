@@ -75,6 +75,10 @@ struct InvArgs {
     int elems;            // elements per CTA (power of two, <= 32)
     int* err;
     int variant;          // 0 auto, 1 the generic shared-memory kernel only
+    // schoolbook plans: acc holds job planes q = t * nchunk + ch (t < positions)
+    // of C_t = sum_u A_u B_(t-u); planes of jobs without terms are not read
+    int school;
+    int LbA, LbB, U;
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);
 

@@ -129,4 +129,59 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
     return 0;
 }
 
+int plan_search_school(int n, int wA, int wB, int force_b, Plan* out) {
+    if (n <= 0 || wA <= 0 || wB <= 0 || !out) return 1;
+    if (force_b > 7) return 1;
+    Plan best;
+    double best_cost = 0;
+    bool have = false;
+    const long long lim = 2147483647LL;
+    for (int b = force_b > 0 ? force_b : 2; b <= (force_b > 0 ? force_b : 7); ++b) {
+        Plan p;
+        std::memset(&p, 0, sizeof p);
+        p.kind = KIND_SCHOOL;
+        p.n = n;
+        p.n_int = (n + 15) / 16 * 16;
+        p.mode = PLAN_VALUE;
+        p.b = b;
+        p.LbA = (wA + b - 1) / b;
+        p.LbB = (wB + b - 1) / b;
+        p.positions = p.LbA + p.LbB - 1;
+        p.NB = 1;
+        p.K = (p.positions + 3) / 4 * 4;
+        p.S = p.K / 2;
+        p.g = 2;
+        p.ncA = p.LbA;
+        p.ncB = p.LbB;
+        p.dA = p.dB = p.nW = 1;
+        const long long dmax = (1LL << b) - 1;
+        p.boundA[0] = p.boundB[0] = (int)dmax;
+        const long long seg = (long long)p.n_int * dmax * dmax;  // one plane product
+        long long U = lim / seg;
+        if (U < 1) continue;
+        const int terms = p.LbA < p.LbB ? p.LbA : p.LbB;
+        if (U > p.LbA) U = p.LbA;
+        p.U = (int)U;
+        p.nchunk = (p.LbA + p.U - 1) / p.U;
+        p.acc_bound = (long long)(p.U < terms ? p.U : terms) * seg;
+        p.njobs = p.K * p.nchunk;
+        p.inv_bound_log2 = std::log2((double)terms) + std::log2((double)seg) + 1.0;
+        p.macs_per_elem = (double)p.LbA * p.LbB * p.n_int;
+        int live = 0;
+        for (int t = 0; t < p.positions; ++t)
+            for (int ch = 0; ch < p.nchunk; ++ch) live += school_job_live(p, t, ch);
+        // one int8 MAC ~ 1/250 of an HBM byte at the measured rates; a live job
+        // plane costs 8 B per element (written, then read by the carry)
+        const double cost = p.macs_per_elem + 2000.0 * live;
+        if (!have || cost < best_cost) {
+            best = p;
+            best_cost = cost;
+            have = true;
+        }
+    }
+    if (!have) return 2;
+    *out = best;
+    return 0;
+}
+
 }  // namespace mfftb

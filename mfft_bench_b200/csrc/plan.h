@@ -21,7 +21,13 @@ enum PlanMode {
     PLAN_LIMB = 1,   // the caller's 16-bit limbs are the coefficients (conv_mfft)
 };
 
+enum PlanKind {
+    KIND_MFFT = 0,    // transform, pointwise NB*K^2 plane products, inverse
+    KIND_SCHOOL = 1,  // limb-plane schoolbook: LbA*LbB digit-plane products, no transform
+};
+
 struct Plan {
+    int kind;       // PlanKind
     int n;          // matrix dimension
     int n_int;      // internal dimension: n rounded up to a multiple of 16
     int mode;       // PlanMode
@@ -38,6 +44,10 @@ struct Plan {
     long long acc_bound;       // worst int32 accumulator magnitude
     double inv_bound_log2;     // log2 of the worst inverse-transform magnitude
     double macs_per_elem;      // int8 MACs per output element = NB*K*K*dA*dB*n
+    // KIND_SCHOOL: job t (t < K, K = positions rounded up to 4) of chunk ch
+    // sums A_u * B_(t-u) over u in [ch*U, ch*U+U) with 0 <= t-u < LbB;
+    // NB = 1, dA = dB = nW = 1, njobs = K * nchunk.
+    int U;
 };
 
 // Returns 0 and fills *p on success.  wA / wB: magnitude bits per entry in
@@ -46,5 +56,17 @@ struct Plan {
 // Bytes per element of the digit planes the pack kernel writes.
 inline int plan_digit_bytes(const Plan& p) { return p.mode == PLAN_LIMB ? 4 : (p.b <= 7 ? 1 : 2); }
 int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan* p);
+// Schoolbook limb-plane plan (PLAN_VALUE only): digit width b in [2, 7] so
+// the digit planes are the int8 tensor-core operands themselves; the
+// contraction over u is chunked so every int32 accumulator stays < 2^31.
+// Minimises plane products plus the job-plane traffic.  force_b > 0 pins b.
+int plan_search_school(int n, int wA, int wB, int force_b, Plan* p);
+// Whether job (t, ch) of a schoolbook plan has any term.
+inline bool school_job_live(const Plan& p, int t, int ch) {
+    const int lo = t - (p.LbB - 1) > ch * p.U ? t - (p.LbB - 1) : ch * p.U;
+    int hi = t < p.LbA - 1 ? t : p.LbA - 1;
+    if (hi > ch * p.U + p.U - 1) hi = ch * p.U + p.U - 1;
+    return lo <= hi;
+}
 
 }  // namespace mfftb

@@ -487,10 +487,27 @@ __device__ __forceinline__ void pw3_tile_decode(const PwParams& p, long long til
     const int local = r % group;
     mt = first_m + local % gm;
     nt = local / gm;
+    if (p.jobs.school) {  // group sj = (t group, chunk); w carries the chunk
+        j = 0;
+        w = sj % p.jobs.nchunk;
+        t0 = (sj / p.jobs.nchunk) * PW3_TG;
+        return;
+    }
     j = sj / (p.jobs.nW * ngroups);
     const int rem = sj % (p.jobs.nW * ngroups);
     w = rem / ngroups;
     t0 = (rem % ngroups) * PW3_TG;
+}
+
+// Schoolbook tile (t0..t0+3, chunk ch): the union [lo, hi] of its jobs' u
+// ranges, walked in pairs of u per pipeline stage; returns the pair count.
+__device__ __forceinline__ int pw3_school_pairs(const PwJobs& J, int t0, int ch, int& lo) {
+    int l0, h0, l3, h3;
+    pw_school_range(J, t0, ch, l0, h0);
+    pw_school_range(J, t0 + PW3_TG - 1, ch, l3, h3);
+    lo = l0;
+    const int hi = h3;  // lo grows and hi grows with t: the union is [lo(t0), hi(t0+3)]
+    return hi >= lo ? (hi - lo + 2) / 2 : 0;
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
@@ -565,6 +582,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             }
             int j, w, t0, mt, nt;
             pw3_tile_decode(p, tile, j, w, t0, mt, nt);
+            if (p.jobs.school) {
+                int ulo;
+                const int npairs_u = pw3_school_pairs(p.jobs, t0, w, ulo);
+                for (int cp = 0; cp < npairs_u; ++cp) {
+                    const int c = ulo + 2 * cp;
+                    for (int kb = 0; kb < p.kblocks; ++kb) {
+                        if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                                               global_timer_ns() + tmo))
+                            goto producer_done;
+                        const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
+                        if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                        uint8_t* st = smem + stage * PW3_STAGE_BYTES;
+                        // A planes c, c+1; B planes t0+3-c-f in slot f (out-of-range
+                        // plane coordinates load zeros)
+#pragma unroll
+                        for (int cc = 0; cc < PW3_CPS; ++cc)
+                            tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
+                                             kb * PW_BK, mt * 256 + (int)rank * 128, c + cc);
+#pragma unroll
+                        for (int f = 0; f < PW3_NF; ++f)
+                            tma_load_3d_pair(
+                                smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
+                                full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
+                                t0 + PW3_TG - 1 - c - f);
+                        issued_parity[stage] = (int)phase;
+                        if (++stage == PW3_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                }
+                continue;
+            }
             const int npr = pw_class_pairs(p.jobs, w);
             for (int pi = 0; pi < npr; ++pi) {
             const int da = pw_class_first_da(p.jobs, w) + pi, db = w - da;
@@ -614,10 +664,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
             int j, w, t0, mt, nt;
             pw3_tile_decode(p, tile, j, w, t0, mt, nt);
-            const int steps_per_tile = pw_class_pairs(p.jobs, w) * cps_per_kb * p.kblocks;
+            int ulo = 0;
+            const int steps_per_tile =
+                p.jobs.school ? pw3_school_pairs(p.jobs, t0, w, ulo) * p.kblocks
+                              : pw_class_pairs(p.jobs, w) * cps_per_kb * p.kblocks;
+            if (steps_per_tile == 0) continue;  // schoolbook tile without terms
             if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
+            if (p.jobs.school) {
+                int rlo[PW3_TG], rhi[PW3_TG];
+#pragma unroll
+                for (int tt = 0; tt < PW3_TG; ++tt) pw_school_range(p.jobs, t0 + tt, w, rlo[tt], rhi[tt]);
+                uint32_t started = 0;
+                for (int it = 0; it < steps_per_tile; ++it) {
+                    if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                           global_timer_ns() + tmo))
+                        goto mma_done;
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + stage * PW3_STAGE_BYTES);
+                    const int c = ulo + 2 * (it / p.kblocks);
+#pragma unroll
+                    for (int cc = 0; cc < PW3_CPS; ++cc) {
+#pragma unroll
+                        for (int tt = 0; tt < PW3_TG; ++tt) {
+                            const int u = c + cc;
+                            if (u < rlo[tt] || u > rhi[tt]) continue;  // zero or foreign term
+                            const int fi = PW3_TG - 1 - tt + cc;       // B plane t0+tt-u
+                            const uint32_t a0 = st + cc * PW3_A_BYTES;
+                            const uint32_t b0 = st + PW3_CPS * PW3_A_BYTES + fi * PW3_F_BYTES;
+                            const uint32_t acc_on = (started >> tt) & 1u;
+#pragma unroll
+                            for (int kk = 0; kk < PW_BK / 32; ++kk)
+                                mma_i8_pair(tmem_base + (uint32_t)(tt * PW3_BN),
+                                            sdesc_kmajor_sw128(a0 + kk * 32),
+                                            sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                            (acc_on | (uint32_t)kk) != 0 ? 1u : 0u);
+                            started |= 1u << tt;
+                        }
+                    }
+                    mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                    if (++stage == PW3_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                mma_commit_pair_mc(bar_tfull, 0x3);
+                acc_phase ^= 1;
+                continue;
+            }
             for (int it = 0; it < steps_per_tile; ++it) {
                 if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
                                        global_timer_ns() + tmo))
@@ -658,6 +753,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
             int j, w, t0, mt, nt;
             pw3_tile_decode(p, tile, j, w, t0, mt, nt);
+            if (p.jobs.school) {
+                int ulo;
+                if (pw3_school_pairs(p.jobs, t0, w, ulo) == 0) continue;
+            }
             if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
@@ -665,7 +764,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             const int col0 = nt * PW3_BN;
             const int colmax = p.cols - col0;
             for (int tt = 0; tt < PW3_TG; ++tt) {
-                const int q = (j * K + t0 + tt) * p.jobs.nW + w;  // job (j, t, w), one chunk
+                int q = (j * K + t0 + tt) * p.jobs.nW + w;  // job (j, t, w), one chunk
+                if (p.jobs.school) {
+                    int lo, hi;
+                    pw_school_range(p.jobs, t0 + tt, w, lo, hi);
+                    if (lo > hi) continue;  // no term: the plane is never read
+                    q = (t0 + tt) * p.jobs.nchunk + w;
+                }
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
                 for (int c = 0; c < PW3_BN / 32; ++c) {
                     uint32_t v[32];
@@ -742,10 +847,15 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     if (reinterpret_cast<uintptr_t>(L.A) % 16 || reinterpret_cast<uintptr_t>(L.F) % 16 ||
         reinterpret_cast<uintptr_t>(L.out) % 16)
         return MFFTB_ERR_ARG;
-    // t-grouped CTA pairs for single-digit plans, CTA pairs when both
-    // dimensions fill at least one 256 x 256 pair tile, single CTAs otherwise
-    const bool grouped_ok = L.jobs.nchunk == 1 && L.jobs.K % PW3_TG == 0 && L.rows >= 256 &&
-                            L.cols >= 128 && L.num_sms >= 2;
+    // t-grouped CTA pairs for one-chunk plans, CTA pairs when both dimensions
+    // fill at least one 256 x 256 pair tile, single CTAs otherwise.  The
+    // schoolbook job table runs on the t-grouped kernel only, at any size
+    // (tiles past the operand edges load zeros).
+    const bool grouped_ok =
+        L.jobs.K % PW3_TG == 0 && L.num_sms >= 2 &&
+        (L.jobs.school ? (L.jobs.dA == 1 && L.jobs.dB == 1 && L.jobs.nW == 1 && L.jobs.U >= 1)
+                       : (L.jobs.nchunk == 1 && L.rows >= 256 && L.cols >= 128));
+    if (L.jobs.school && (!grouped_ok || (L.variant != 0 && L.variant != 3))) return MFFTB_ERR_ARG;
     const bool grouped = L.variant == 3 ? grouped_ok : (L.variant == 0 && grouped_ok);
     if (L.variant == 3 && !grouped_ok) return MFFTB_ERR_ARG;
     const bool pair = !grouped && (L.variant == 2 || (L.variant == 0 && L.block_n == 256 &&
@@ -856,10 +966,26 @@ __global__ void pointwise_simt_check_kernel(const int8_t* A, long long lda, long
     int q = (int)(idx / per_job);
     int r = (int)((idx % per_job) / cols);
     int c = (int)(idx % cols);
+    long long acc = 0;
+    if (J.school) {
+        const int t = q / J.nchunk, ch = q % J.nchunk;
+        int lo, hi;
+        pw_school_range(J, t, ch, lo, hi);
+        if (lo > hi) return;  // a job without terms is never written
+        for (int u = lo; u <= hi; ++u) {
+            const int8_t* a = A + u * a_plane + r * lda;
+            const int8_t* f = F + (t - u) * f_plane + c * ldf;
+            for (int k = 0; k < kdim; ++k) acc += (long long)a[k] * (long long)f[k];
+        }
+        int32_t got = out[q * out_plane + (long long)r * ldo + c];
+        if ((long long)got != acc) {
+            if (atomicAdd(mismatch, 1) == 0) *first_bad = idx;
+        }
+        return;
+    }
     int j, t, w, ch, s0, s1;
     pw_job_decode(J, q, j, t, w, ch);
     pw_chunk_range(J, w, ch, s0, s1);
-    long long acc = 0;
     for (int s = s0; s < s1; ++s) {
         int pa, pf;
         pw_segment_planes(J, j, t, w, s, pa, pf);

@@ -44,7 +44,24 @@ struct PwJobs {
     int nW;       // digit-weight classes = dA + dB - 1
     int nchunk;   // contraction chunks per (j, t, w)
     int njobs;    // NB * K * nW * nchunk
+    // Schoolbook limb-plane mode (school = 1): job q = t * nchunk + ch is
+    //     C_t = sum_u A_u * B_(t-u),  u in [ch*U, ch*U+U), 0 <= u < LbA,
+    //                                 0 <= t-u < LbB
+    // over the digit planes themselves (the "F" operand holds B's LbB digit
+    // planes in order; no transform, no signs).  K = number of t's (a
+    // multiple of 4), dA = dB = nW = 1.
+    int school;
+    int LbA, LbB, U;
 };
+
+// u range [lo, hi] of schoolbook job (t, ch); empty when lo > hi
+__host__ __device__ inline void pw_school_range(const PwJobs& J, int t, int ch, int& lo, int& hi) {
+    lo = ch * J.U;
+    if (t - (J.LbB - 1) > lo) lo = t - (J.LbB - 1);
+    hi = ch * J.U + J.U - 1;
+    if (t < hi) hi = t;
+    if (J.LbA - 1 < hi) hi = J.LbA - 1;
+}
 
 struct PwParams {
     PwJobs jobs;

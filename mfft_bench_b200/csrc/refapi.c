@@ -51,8 +51,10 @@ static int finish(mfftgpu_ctx *c, int rc, const char *what)
 static void account(mfftgpu_ctx *c, int n, int mode, int wA, int wB)
 {
     mfftgpu_plan_info pi;
-    if (mfftgpu_plan_info_get(n, mode, wA, wB, &pi) == 0)
-        g_kernel_calls = (long long)pi.NB * pi.K * pi.K * pi.dA * pi.dB;
+    /* plane products of the plan that ran (src/kernel.c:13 counts leaf calls) */
+    if ((c && mfftgpu_last_plan(c, &pi) == 0) || mfftgpu_plan_info_get(n, mode, wA, wB, &pi) == 0)
+        g_kernel_calls = pi.kind == 1 ? (long long)pi.LbA * pi.LbB
+                                      : (long long)pi.NB * pi.K * pi.K * pi.dA * pi.dB;
     if (g_mfft_profile && c) {
         float ms[5];
         mfftgpu_last_phase_ms(c, ms);
@@ -297,6 +299,77 @@ void conv_mfft(int64_t *Cw, const int32_t *A32, const int32_t *B32, int n, int L
         return;
     }
     account(c, n, 1, L, L);
+}
+
+/* Limb-plane schoolbook (src/methods.c:94-123): the same exact products as
+ * mm_mfft / conv_mfft, computed as digit-plane GEMMs A_u B_v on the tensor
+ * cores without a transform. */
+static int with_school(mfftgpu_ctx *c, int on)
+{
+    int prev = mfftgpu_get_method(c);
+    mfftgpu_set_method(c, on);
+    return prev;
+}
+
+void mm_limbplane(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, kernel_t k,
+                  uint16_t *out, int RL)
+{
+    (void)k;
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return;
+    mfftgpu_set_profile(c, g_mfft_profile ? 1 : 0);
+    int prev = with_school(c, 1);
+    int rc = mfftgpu_mm_u16(c, Apl, Bpl, n, L, 0, out, RL);
+    with_school(c, prev);
+    if (finish(c, rc, "mm_limbplane")) {
+        memset(out, 0, (size_t)RL * n * n * sizeof(uint16_t));
+        return;
+    }
+    account(c, n, 2, 16 * L, 16 * L);
+}
+
+void mm_limbplane_signed(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, uint16_t *out,
+                         int RL)
+{
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return;
+    mfftgpu_set_profile(c, g_mfft_profile ? 1 : 0);
+    int prev = with_school(c, 1);
+    int rc = mfftgpu_mm_u16(c, Apl, Bpl, n, L, 1, out, RL);
+    with_school(c, prev);
+    if (finish(c, rc, "mm_limbplane_signed")) {
+        memset(out, 0, (size_t)RL * n * n * sizeof(uint16_t));
+        return;
+    }
+    account(c, n, 2, 16 * L, 16 * L);
+}
+
+/* conv_limbplane's unnormalised planes Cw[w] = sum_{u+v=w} A_u B_v depend on
+ * the caller's limb split, so they come from the limb-mode plan (the same
+ * values conv_mfft returns). */
+void conv_limbplane(int64_t *Cw, const int32_t *A32, const int32_t *B32, int n, int L,
+                    kernel_t k)
+{
+    (void)k;
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return;
+    mfftgpu_set_profile(c, g_mfft_profile ? 1 : 0);
+    int rc = mfftgpu_conv_i32(c, A32, B32, n, L, Cw);
+    if (finish(c, rc, "conv_limbplane")) {
+        memset(Cw, 0, (size_t)(2 * L - 1) * n * n * sizeof(int64_t));
+        return;
+    }
+    account(c, n, 1, L, L);
+}
+
+int fpx_gemm_f32_limbplane(const float *A, const float *B, int n, int force_bits, float *C)
+{
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return g_status;
+    int prev = with_school(c, 1);
+    int rc = mfftgpu_fp32(c, A, B, n, force_bits, C);
+    with_school(c, prev);
+    return finish(c, rc, "fpx_gemm_f32_limbplane");
 }
 
 int fpx_gemm_f32(const float *A, const float *B, int n, int force_bits, float *C)

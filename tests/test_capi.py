@@ -111,6 +111,33 @@ def test_plan_exactness_invariants(n, mode, w):
     assert pi["int8_macs"] == pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"] * float(pi["n_int"]) ** 3
 
 
+@pytest.mark.parametrize("n", [1, 16, 100, 1024, 4096, 16384])
+@pytest.mark.parametrize("w", [8, 64, 68, 256, 1024, 8192])
+def test_school_plan_invariants(n, w):
+    """Schoolbook plans: int8 digit planes, every chunk's int32 accumulator
+    bounded by the worst digit product, chunks covering all of A's digits."""
+    pi = m.plan_info(n, 2, w)
+    assert pi["kind"] == 1 and pi["NB"] == 1 and pi["dA"] == pi["dB"] == pi["nW"] == 1
+    b, LbA, LbB, U = pi["b"], pi["LbA"], pi["LbB"], pi["U"]
+    assert 2 <= b <= 7 and LbA * b >= w and LbB * b >= w
+    assert pi["positions"] == LbA + LbB - 1
+    assert pi["K"] % 4 == 0 and pi["K"] >= pi["positions"]
+    assert pi["nchunk"] * U >= LbA > (pi["nchunk"] - 1) * U
+    dmax = (1 << b) - 1
+    worst = min(U, LbA, LbB) * pi["n_int"] * dmax * dmax
+    assert worst == pi["acc_bound"] and worst < 2 ** 31
+    assert pi["int8_macs"] == LbA * LbB * float(pi["n_int"]) ** 3
+    assert pi["njobs"] == pi["K"] * pi["nchunk"]
+
+
+def test_school_plan_fewer_products_at_the_bench_widths():
+    """The comparison the reference's GPU planner makes: at W=64 and W=256
+    schoolbook needs fewer plane products than flat MFFT."""
+    for n, w in ((16384, 64), (1024, 256), (8192, 68)):
+        s, f = m.plan_info(n, 2, w), m.plan_info(n, 0, w)
+        assert s["int8_macs"] < f["int8_macs"] / 2
+
+
 def test_bench_plans_are_single_digit():
     """The bench configurations run with one int8 digit per transformed value."""
     for n, w in ((16384, 64), (1024, 256)):
