@@ -55,6 +55,7 @@ typedef struct {
     int kind;                /* 0 MFFT; 1 limb-plane schoolbook (NB = 1, no transform:
                                 job t of chunk ch sums A_u B_(t-u), u in [ch*U, ch*U+U)) */
     int U;                   /* schoolbook: digit planes of A per contraction chunk */
+    int balanced;            /* 1: balanced digits in [-2^(b-1), 2^(b-1)) (int64 operands) */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -90,8 +91,9 @@ const char *mfftgpu_status_string(int status);
 int mfftgpu_device_count(void);
 
 /* Plan the product (mode 0: value re-radix, 1: limb mode as used by
- * conv_mfft, 2: value re-radix with the limb-plane schoolbook method).
- * wA/wB: magnitude bits (modes 0, 2) or limb counts (mode 1). */
+ * conv_mfft, 2: value re-radix with the limb-plane schoolbook method, 3: the
+ * same for int64 operands, which may use balanced 8-bit digits).
+ * wA/wB: magnitude bits (modes 0, 2, 3) or limb counts (mode 1). */
 int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info *out);
 /* The plan of the last product run on this context (the fp32 plan depends on
  * the exponent window of the data). */

@@ -215,6 +215,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     pb.plane = nn_int;
     pb.transpose = 1;
     pb.err = C->d_err;
+    pb.balanced = P.balanced;
     FwdArgs fb{};
     fb.D = DB;
     fb.dbytes = dbytes;
@@ -376,10 +377,12 @@ int check_rows(int n, int row_begin, int row_end) {
     return (row_begin < 0 || row_end > n || row_begin > row_end) ? MFFTB_ERR_ARG : MFFTB_OK;
 }
 
-int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P) {
+int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P,
+                int balanced_ok = 0) {
     // the schoolbook method covers value-mode products; limb mode (conv)
     // always runs the MFFT plan
-    if (C->method == 1 && mode == PLAN_VALUE && plan_search_school(n, wA, wB, 0, P) == 0)
+    if (C->method == 1 && mode == PLAN_VALUE &&
+        plan_search_school(n, wA, wB, 0, P, balanced_ok) == 0)
         return MFFTB_OK;
     int rc = plan_search(n, mode, wA, wB, 0, 0, P);
     if (rc)
@@ -598,8 +601,8 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o);
 int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o) {
     if (!o) return MFFTB_ERR_ARG;
     Plan P;
-    if (mode == 2) {
-        if (plan_search_school(n, wA, wB, 0, &P)) return MFFTB_ERR_PLAN;
+    if (mode == 2 || mode == 3) {  // 3: int64 operands, balanced digits allowed
+        if (plan_search_school(n, wA, wB, 0, &P, mode == 3)) return MFFTB_ERR_PLAN;
     } else if (plan_search(n, mode, wA, wB, 0, 0, &P)) {
         return MFFTB_ERR_PLAN;
     }
@@ -641,6 +644,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->pw_kernel = 0;
     o->kind = P.kind;
     o->U = P.U;
+    o->balanced = P.balanced;
 }
 
 // --------------------------------------------------------------------- integers
@@ -665,7 +669,7 @@ int mfftgpu_mm_i64_dev(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n
     if (check_rows(n, row_begin, row_end)) return set_err(C, MFFTB_ERR_ARG, "bad row range");
     cudaSetDevice(C->device);
     Plan P;
-    int rc = plan_or_err(C, n, PLAN_VALUE, 64, 64, &P);
+    int rc = plan_or_err(C, n, PLAN_VALUE, 64, 64, &P, 1);
     if (rc) return rc;
     Operand a{PACK_I64, A, n, 4, 64, 1, 0, 0, 0};
     Operand b = a;

@@ -768,8 +768,107 @@ __global__ void __launch_bounds__(SC_THREADS) school_carry_kernel(const InvArgs 
     out[o] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
 }
 
+// Integer output, 4 consecutive elements per thread: 16-byte loads of every
+// job plane (512 contiguous bytes per warp and plane) and 8-byte limb stores.
+constexpr int SC4_UNROLL = 4;
+
+__global__ void __launch_bounds__(SC_THREADS) school_carry4_kernel(const InvArgs a, int vec_out) {
+    const long long e = (blockIdx.x * (long long)SC_THREADS + threadIdx.x) * 4;
+    const long long total = (long long)a.rows * a.lda;
+    if (e >= total) return;
+    const int row = (int)(e / a.lda), col = (int)(e % a.lda);  // lda % 4 == 0: one row
+    if (row >= a.rows || col >= a.cols) return;
+    const int P = a.positions, b = a.b;
+    const uint64_t mask = (1ULL << b) - 1ULL;
+    int64_t carry[4] = {0, 0, 0, 0};
+    uint64_t bits[4] = {0, 0, 0, 0};
+    int nb = 0, w = 0;  // same for the 4 elements
+    uint16_t* out16 = reinterpret_cast<uint16_t*>(a.out);
+    const long long o = (long long)row * a.ldo + col;
+    const bool full = vec_out && col + 3 < a.cols;
+    auto store = [&](int wv, const uint16_t (&h)[4]) {
+        uint16_t* dst = out16 + (long long)wv * a.out_plane + o;
+        if (full) {
+            ushort4 q;
+            q.x = h[0];
+            q.y = h[1];
+            q.z = h[2];
+            q.w = h[3];
+            *reinterpret_cast<ushort4*>(dst) = q;
+        } else {
+            for (int i = 0; i < 4; ++i)
+                if (col + i < a.cols) dst[i] = h[i];
+        }
+    };
+    for (int t0 = 0; t0 < P; t0 += SC4_UNROLL) {
+        int64_t v[SC4_UNROLL][4];
+#pragma unroll
+        for (int u = 0; u < SC4_UNROLL; ++u) {
+            v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0;
+            const int t = t0 + u;
+            if (t < P)
+                for (int ch = 0; ch < a.nchunk; ++ch)
+                    if (school_live(a, t, ch)) {
+                        const int4 r = __ldg(reinterpret_cast<const int4*>(
+                            a.acc + (long long)(t * a.nchunk + ch) * a.acc_plane + e));
+                        v[u][0] += r.x;
+                        v[u][1] += r.y;
+                        v[u][2] += r.z;
+                        v[u][3] += r.w;
+                    }
+        }
+#pragma unroll
+        for (int u = 0; u < SC4_UNROLL; ++u) {
+            if (t0 + u >= P) break;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int64_t x = v[u][i] + carry[i];
+                bits[i] |= ((uint64_t)x & mask) << nb;
+                carry[i] = x >> b;
+            }
+            nb += b;
+            while (nb >= 16) {
+                if (w < a.RL) {
+                    uint16_t h[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) h[i] = (uint16_t)(bits[i] & 0xFFFFu);
+                    store(w, h);
+                }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) bits[i] >>= 16;
+                nb -= 16;
+                ++w;
+            }
+        }
+    }
+    while (w < a.RL) {  // sign-extend from the final carries
+        const int need = 16 - nb;
+        uint16_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            bits[i] |= ((uint64_t)carry[i] & ((1ULL << need) - 1ULL)) << nb;
+            carry[i] >>= need;
+            h[i] = (uint16_t)(bits[i] & 0xFFFFu);
+            bits[i] = 0;
+        }
+        store(w, h);
+        nb = 0;
+        ++w;
+    }
+}
+
 static int school_carry_launch(const InvArgs& a, cudaStream_t stream) {
     if (a.out_kind == INV_I64) return MFFTB_ERR_UNSUPPORTED;
+    if (a.out_kind == INV_U16 && a.lda % 4 == 0 && a.acc_plane % 4 == 0 &&
+        reinterpret_cast<uintptr_t>(a.acc) % 16 == 0 && a.b >= 1 && a.b <= 15 && a.nchunk >= 1 &&
+        a.U >= 1) {
+        const int vec_out = a.ldo % 4 == 0 && a.out_plane % 4 == 0 &&
+                            reinterpret_cast<uintptr_t>(a.out) % 8 == 0;
+        const long long total4 = ((long long)a.rows * a.lda) / 4;
+        const long long blocks = (total4 + SC_THREADS - 1) / SC_THREADS;
+        if (blocks > 0) school_carry4_kernel<<<(unsigned)blocks, SC_THREADS, 0, stream>>>(a, vec_out);
+        return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+    }
     if (a.b < 1 || a.b > 15 || a.nchunk < 1 || a.U < 1) return MFFTB_ERR_ARG;
     if (a.out_kind == INV_F32 && (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
         return MFFTB_ERR_UNSUPPORTED;

@@ -32,6 +32,7 @@ struct PackArgs {
     long long plane;   // elements per output plane
     int transpose;     // 1: output row = source column
     int* err;
+    int balanced;      // PACK_I64 only: balanced digits in [-2^(b-1), 2^(b-1)), b <= 8
 };
 int pack_launch(const PackArgs& a, cudaStream_t stream);
 

@@ -174,6 +174,22 @@ __device__ __forceinline__ int digit_of_i64(int64_t x, int p, int b, int W) {
     return (int)(((uint64_t)x >> p) & ((1u << b) - 1u));
 }
 
+// Balanced digits: with H = sum_{i < Lb} 2^(b*i + b-1), the value
+// z = x + H is non-negative and below 2^(b*Lb) (Lb >= ceil((64+1)/b)), and
+// digit m = field m of z minus 2^(b-1) -- so x = sum_m digit_m 2^(b*m) with
+// every digit in [-2^(b-1), 2^(b-1)), still a local bit-field extraction.
+__device__ __forceinline__ unsigned __int128 balanced_offset(int b, int Lb) {
+    unsigned __int128 h = 0;
+    for (int i = 0; i < Lb; ++i) h |= (unsigned __int128)1 << (b * i + b - 1);
+    return h;
+}
+__device__ __forceinline__ int digit_balanced(unsigned __int128 z, int p, int b) {
+    return (int)((unsigned)(z >> p) & ((1u << b) - 1u)) - (1 << (b - 1));
+}
+__device__ __forceinline__ unsigned __int128 balanced_z(int64_t x, unsigned __int128 H) {
+    return (unsigned __int128)(__int128)x + H;
+}
+
 __device__ __forceinline__ uint32_t pack4(int d0, int d1, int d2, int d3) {
     return (uint32_t)(d0 & 0xFF) | ((uint32_t)(d1 & 0xFF) << 8) | ((uint32_t)(d2 & 0xFF) << 16) |
            ((uint32_t)(d3 & 0xFF) << 24);
@@ -191,6 +207,19 @@ __global__ void __launch_bounds__(256) pack_i64_straight_kernel(const PackArgs a
     for (int q = 0; q < 4; ++q)
         x[q] = (i < a.n && c0 + q < a.n) ? __ldg(src + (long long)i * a.n + c0 + q) : 0;
     uint8_t* out = reinterpret_cast<uint8_t*>(a.dst) + (long long)r * a.ld + c0;
+    if (a.balanced) {
+        const unsigned __int128 H = balanced_offset(a.b, a.Lb);
+        unsigned __int128 z[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) z[q] = balanced_z(x[q], H);
+        for (int m = 0; m < a.Lb; ++m) {
+            const int p = m * a.b;
+            *reinterpret_cast<uint32_t*>(out + (long long)m * a.plane) =
+                pack4(digit_balanced(z[0], p, a.b), digit_balanced(z[1], p, a.b),
+                      digit_balanced(z[2], p, a.b), digit_balanced(z[3], p, a.b));
+        }
+        return;
+    }
     for (int m = 0; m < a.Lb; ++m) {
         const int p = m * a.b;
         *reinterpret_cast<uint32_t*>(out + (long long)m * a.plane) =
@@ -217,6 +246,18 @@ __global__ void __launch_bounds__(256) pack_i64_transposed_kernel(const PackArgs
         const int64_t x0 = tile[kq][jj], x1 = tile[kq + 1][jj], x2 = tile[kq + 2][jj],
                       x3 = tile[kq + 3][jj];
         uint8_t* o = out + (long long)r * a.ld + c;
+        if (a.balanced) {
+            const unsigned __int128 H = balanced_offset(a.b, a.Lb);
+            const unsigned __int128 z0 = balanced_z(x0, H), z1 = balanced_z(x1, H),
+                                    z2 = balanced_z(x2, H), z3 = balanced_z(x3, H);
+            for (int m = 0; m < a.Lb; ++m) {
+                const int p = m * a.b;
+                *reinterpret_cast<uint32_t*>(o + (long long)m * a.plane) =
+                    pack4(digit_balanced(z0, p, a.b), digit_balanced(z1, p, a.b),
+                          digit_balanced(z2, p, a.b), digit_balanced(z3, p, a.b));
+            }
+            continue;
+        }
         for (int m = 0; m < a.Lb; ++m) {
             const int p = m * a.b;
             *reinterpret_cast<uint32_t*>(o + (long long)m * a.plane) =
@@ -230,7 +271,10 @@ int pack_launch(const PackArgs& a, cudaStream_t stream) {
     if (a.ld % 16 || a.rows <= 0 || a.Lb <= 0 || a.b < 1 || (a.b > 15 && a.fmt != PACK_I32LIMB))
         return MFFTB_ERR_ARG;
     dim3 block(256);
-    if (a.fmt == PACK_I64 && a.b <= 7 && a.plane % 4 == 0) {
+    if (a.balanced && (a.fmt != PACK_I64 || a.b > 8 || a.plane % 4 || a.W != 64 ||
+                       a.b * a.Lb < 65 || a.b * a.Lb > 120))
+        return MFFTB_ERR_ARG;
+    if (a.fmt == PACK_I64 && (a.b <= 7 || a.balanced) && a.plane % 4 == 0) {
         if (a.transpose) {
             dim3 grid((a.ld + 63) / 64, (a.rows + 63) / 64);
             pack_i64_transposed_kernel<<<grid, block, 0, stream>>>(a);

@@ -129,14 +129,20 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
     return 0;
 }
 
-int plan_search_school(int n, int wA, int wB, int force_b, Plan* out) {
+int plan_search_school(int n, int wA, int wB, int force_b, Plan* out, int balanced_ok) {
     if (n <= 0 || wA <= 0 || wB <= 0 || !out) return 1;
-    if (force_b > 7) return 1;
+    if (force_b > 8 || (force_b == 8 && !balanced_ok)) return 1;
     Plan best;
     double best_cost = 0;
     bool have = false;
     const long long lim = 2147483647LL;
-    for (int b = force_b > 0 ? force_b : 2; b <= (force_b > 0 ? force_b : 7); ++b) {
+    const int b_lo = force_b > 0 ? force_b : 2;
+    const int b_hi = force_b > 0 ? force_b : (balanced_ok ? 8 : 7);
+    for (int cand = 0; cand < 2 * (b_hi - b_lo + 1); ++cand) {
+        const int b = b_lo + cand / 2;
+        const int bal = cand & 1;
+        if (bal && !balanced_ok) continue;
+        if (!bal && b > 7) continue;
         Plan p;
         std::memset(&p, 0, sizeof p);
         p.kind = KIND_SCHOOL;
@@ -144,8 +150,10 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* out) {
         p.n_int = (n + 15) / 16 * 16;
         p.mode = PLAN_VALUE;
         p.b = b;
-        p.LbA = (wA + b - 1) / b;
-        p.LbB = (wB + b - 1) / b;
+        p.balanced = bal;
+        // balanced digits of a W-bit two's complement value: ceil((W+1)/b)
+        p.LbA = bal ? (wA + b) / b : (wA + b - 1) / b;
+        p.LbB = bal ? (wB + b) / b : (wB + b - 1) / b;
         p.positions = p.LbA + p.LbB - 1;
         p.NB = 1;
         p.K = (p.positions + 3) / 4 * 4;
@@ -154,7 +162,7 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* out) {
         p.ncA = p.LbA;
         p.ncB = p.LbB;
         p.dA = p.dB = p.nW = 1;
-        const long long dmax = (1LL << b) - 1;
+        const long long dmax = bal ? (1LL << (b - 1)) : (1LL << b) - 1;
         p.boundA[0] = p.boundB[0] = (int)dmax;
         const long long seg = (long long)p.n_int * dmax * dmax;  // one plane product
         long long U = lim / seg;

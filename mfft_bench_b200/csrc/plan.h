@@ -48,19 +48,27 @@ struct Plan {
     // sums A_u * B_(t-u) over u in [ch*U, ch*U+U) with 0 <= t-u < LbB;
     // NB = 1, dA = dB = nW = 1, njobs = K * nchunk.
     int U;
+    // balanced digits (int64 entries only): digit m of x is byte m of
+    // x + sum_i 2^(b*i + b-1), minus 2^(b-1), so digits lie in
+    // [-2^(b-1), 2^(b-1)) and b = 8 still fits int8
+    int balanced;
 };
 
 // Returns 0 and fills *p on success.  wA / wB: magnitude bits per entry in
 // PLAN_VALUE, limb counts in PLAN_LIMB.  force_b > 0 pins the digit width
 // (PLAN_VALUE only); force_S > 0 pins the block size.
 // Bytes per element of the digit planes the pack kernel writes.
-inline int plan_digit_bytes(const Plan& p) { return p.mode == PLAN_LIMB ? 4 : (p.b <= 7 ? 1 : 2); }
+inline int plan_digit_bytes(const Plan& p) {
+    return p.mode == PLAN_LIMB ? 4 : ((p.b <= 7 || p.balanced) ? 1 : 2);
+}
 int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan* p);
 // Schoolbook limb-plane plan (PLAN_VALUE only): digit width b in [2, 7] so
 // the digit planes are the int8 tensor-core operands themselves; the
 // contraction over u is chunked so every int32 accumulator stays < 2^31.
 // Minimises plane products plus the job-plane traffic.  force_b > 0 pins b.
-int plan_search_school(int n, int wA, int wB, int force_b, Plan* p);
+// balanced_ok: the operands are two's complement int64 entries, which may use
+// balanced 8-bit digits (ceil((W+1)/8) of them).
+int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced_ok = 0);
 // Whether job (t, ch) of a schoolbook plan has any term.
 inline bool school_job_live(const Plan& p, int t, int ch) {
     const int lo = t - (p.LbB - 1) > ch * p.U ? t - (p.LbB - 1) : ch * p.U;

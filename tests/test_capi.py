@@ -112,22 +112,40 @@ def test_plan_exactness_invariants(n, mode, w):
 
 
 @pytest.mark.parametrize("n", [1, 16, 100, 1024, 4096, 16384])
-@pytest.mark.parametrize("w", [8, 64, 68, 256, 1024, 8192])
-def test_school_plan_invariants(n, w):
+@pytest.mark.parametrize("mode,w", [(2, 8), (2, 64), (2, 68), (2, 256), (2, 1024), (2, 8192),
+                                    (3, 64)])
+def test_school_plan_invariants(n, mode, w):
     """Schoolbook plans: int8 digit planes, every chunk's int32 accumulator
     bounded by the worst digit product, chunks covering all of A's digits."""
-    pi = m.plan_info(n, 2, w)
+    pi = m.plan_info(n, mode, w)
     assert pi["kind"] == 1 and pi["NB"] == 1 and pi["dA"] == pi["dB"] == pi["nW"] == 1
     b, LbA, LbB, U = pi["b"], pi["LbA"], pi["LbB"], pi["U"]
-    assert 2 <= b <= 7 and LbA * b >= w and LbB * b >= w
+    bal = pi["balanced"]
+    assert bal in (0, 1) and (mode == 3 or not bal)
+    assert 2 <= b <= (8 if bal else 7) and LbA * b >= w + bal and LbB * b >= w + bal
     assert pi["positions"] == LbA + LbB - 1
     assert pi["K"] % 4 == 0 and pi["K"] >= pi["positions"]
     assert pi["nchunk"] * U >= LbA > (pi["nchunk"] - 1) * U
-    dmax = (1 << b) - 1
+    dmax = (1 << (b - 1)) if bal else (1 << b) - 1
     worst = min(U, LbA, LbB) * pi["n_int"] * dmax * dmax
     assert worst == pi["acc_bound"] and worst < 2 ** 31
     assert pi["int8_macs"] == LbA * LbB * float(pi["n_int"]) ** 3
     assert pi["njobs"] == pi["K"] * pi["nchunk"]
+
+
+def test_balanced_digits_restate_the_value():
+    """The balanced digit rule of the int64 pack kernel, restated: byte m of
+    x + sum 2^(8i+7), minus 128, over 9 digits gives back x exactly."""
+    H = sum(1 << (8 * i + 7) for i in range(9))
+    for x in (0, 1, -1, 2**63 - 1, -2**63, 0x7F7F7F7F7F7F7F7F, -0x8080808080808080, 12345678901234):
+        z = x + H
+        assert 0 <= z < 1 << 72
+        d = [((z >> (8 * i)) & 255) - 128 for i in range(9)]
+        assert all(-128 <= v <= 127 for v in d)
+        assert sum(v << (8 * i) for i, v in enumerate(d)) == x
+    pi = m.plan_info(16384, 3, 64)
+    assert pi["balanced"] == 1 and pi["b"] == 8 and pi["LbA"] == 9
+    assert pi["int8_macs"] == 81 * 16384.0 ** 3
 
 
 def test_school_plan_fewer_products_at_the_bench_widths():
