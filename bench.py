@@ -46,6 +46,7 @@ WORKLOADS = {
     "c5": dict(n=16384, kind="i64", signed=True,
                desc="configs[4]: n=16384, W=64 signed int64"),
 }
+DEFAULT_N = {k: v["n"] for k, v in WORKLOADS.items()}
 # bounded CPU samples of the same workload for the reference arm / baseline:
 # (sample n, what is timed).  Full-size reference runs take hours (c3-c5).
 CPU_SAMPLE_N = {"c1": 64, "c2": 256, "c3": 128, "c4": 256, "c5": 512}
@@ -561,8 +562,8 @@ def main():
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share
     tr = POINTWISE_TRAFFIC.get(args.workload)
-    if ("roofline" in line and tr and world == 1 and n == WORKLOADS[args.workload]["n"]
-            and pi.get("pw_kernel") == 3):
+    if ("roofline" in line and tr and world == 1 and n == DEFAULT_N[args.workload]
+            and pi.get("pw_kernel") == 3 and pi.get("kind") == 0):
         line["roofline"]["traffic"] = tr["bytes_per_launch"]
         line["roofline"]["traffic_note"] = tr["note"]
 
