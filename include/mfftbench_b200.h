@@ -109,6 +109,10 @@ typedef struct {
 int fpx_init(fpx_ctx *c, const float *A, const float *B, int n, int force_bits); /* src/fpfixed.c:96-108 */
 void fpx_encode(fpx_ctx *c, const float *A, const float *B);                    /* src/fpfixed.c:195-204 */
 void fpx_decode_f32(fpx_ctx *c, float *C);                                       /* src/fpfixed.c:269-285 */
+int fpx_init_d(fpx_ctx *c, const double *A, const double *B, int n, int force_bits); /* src/fpfixed.c:130-140 */
+void fpx_encode_d(fpx_ctx *c, const double *A, const double *B);                    /* src/fpfixed.c:162-172 */
+void fpx_decode_f64(fpx_ctx *c, double *C);                                       /* src/fpfixed.c:308-322 */
+void fpx_decode_ld(fpx_ctx *c, long double *C);                                   /* src/fpfixed.c:291-306 */
 void fpx_free(fpx_ctx *c);                                                       /* src/fpfixed.c:324-328 */
 
 /* status of the last drop-in call (MFFTGPU_* codes of mfftgpu.h); no
@@ -124,6 +128,9 @@ void mm_mfft_signed(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, uint
  * fpx_encode + conv_mfft + fpx_decode_f32 in one call (src/mlgemm.c:1107-1175
  * without the host round trip of the limb planes) */
 int fpx_gemm_f32(const float *A, const float *B, int n, int force_bits, float *C);
+/* fp64 counterpart: fpx_init_d + fpx_encode_d + conv_mfft + fpx_decode_f64
+ * fused on the device */
+int fpx_gemm_f64(const double *A, const double *B, int n, int force_bits, double *C);
 
 /* The limb-plane schoolbook method on the same tensor-core kernel: exact,
  * bit-identical to the MFFT entry points, with LbA*LbB digit-plane products
@@ -138,6 +145,7 @@ void conv_limbplane(int64_t *Cw, const int32_t *A32, const int32_t *B32, int n, 
 void mm_limbplane_signed(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, uint16_t *out,
                          int RL);
 int fpx_gemm_f32_limbplane(const float *A, const float *B, int n, int force_bits, float *C);
+int fpx_gemm_f64_limbplane(const double *A, const double *B, int n, int force_bits, double *C);
 
 #ifdef __cplusplus
 }

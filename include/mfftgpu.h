@@ -145,6 +145,15 @@ int mfftgpu_fp32_dev(mfftgpu_ctx *ctx, const float *A, const float *B, int n, in
 int mfftgpu_fp32(mfftgpu_ctx *ctx, const float *A, const float *B, int n, int force_bits,
                  float *C);
 
+/* --- fp64 fixed-point embedding --------------------------------------------
+ * fpx_init_d + fpx_encode_d + conv + fpx_decode_f64 (src/fpfixed.c:109-160,
+ * 308-322) fused on the device: 53-bit significands on the same grid, each
+ * entry touching up to 5 limbs, rounded once to fp64.  Row-major fp64 n x n. */
+int mfftgpu_fp64_dev(mfftgpu_ctx *ctx, const double *A, const double *B, int n, int force_bits,
+                     double *C, int row_begin, int row_end);
+int mfftgpu_fp64(mfftgpu_ctx *ctx, const double *A, const double *B, int n, int force_bits,
+                 double *C);
+
 /* Exact product of signed 64-bit row-major matrices, like mfftgpu_mm_i64_dev,
  * but with no device allocation at all: for callers that may not call
  * cudaMalloc (a framework that owns all device memory through its own pool,
@@ -194,8 +203,14 @@ int mfftgpu_selftest_school(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int 
  * context stays usable afterwards. */
 int mfftgpu_selftest_timeout(mfftgpu_ctx *ctx, unsigned long long timeout_ns);
 
-/* host self-test of the device fp32 rounding rule (no GPU needed) */
+/* host self-tests of the device fp32 / fp64 rounding rules (no GPU needed) */
 float mfftgpu_decode_words_f32(uint32_t *words, int nwords, int bit_off, int S);
+double mfftgpu_decode_words_f64(uint32_t *words, int nwords, int bit_off, int S);
+/* the shared front half of those rules (extract + round_to of
+ * src/fpfixed.c:212-265) for any significand width `bits` <= 63: returns 0
+ * for zero, else the sign, with value = sig * 2^shift on the grid */
+int mfftgpu_decode_words_round(uint32_t *words, int nwords, int bit_off, int bits, uint64_t *sig,
+                               int *shift);
 
 #ifdef __cplusplus
 }

@@ -8,7 +8,8 @@ contraction, fused fold/carry/round).  Python only binds it.
 """
 from .api import (KERNEL_PACKED, KERNEL_SM100, PLAN_LIMB, PLAN_VALUE, Context, Fpx,  # noqa: F401
                   MfftError, bigmat_rand, conv_mfft, decode_words_f32, device_count,
-                  conv_limbplane, fpx_gemm_f32, fpx_gemm_f32_limbplane, gen_normal_f32,
+                  Fpx64, conv_limbplane, decode_words_f64, decode_words_round, fpx_gemm_f32,
+                  fpx_gemm_f32_limbplane, fpx_gemm_f64, fpx_gemm_f64_limbplane, gen_normal_f32,
                   mfft_plan_init, mm_limbplane, mm_limbplane_signed, mm_mfft, mm_mfft_signed,
                   normalize_planes, plan_info)
 from ._lib import LIB_PATH  # noqa: F401

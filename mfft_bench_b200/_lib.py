@@ -87,12 +87,17 @@ _sig("mfftgpu_conv_i32_dev", i32, vp, vp, vp, i32, i32, vp)
 _sig("mfftgpu_conv_i32", i32, vp, vp, vp, i32, i32, vp)
 _sig("mfftgpu_fp32_dev", i32, vp, vp, vp, i32, i32, vp, i32, i32)
 _sig("mfftgpu_fp32", i32, vp, vp, vp, i32, i32, vp)
+_sig("mfftgpu_fp64_dev", i32, vp, vp, vp, i32, i32, vp, i32, i32)
+_sig("mfftgpu_fp64", i32, vp, vp, vp, i32, i32, vp)
 _sig("mfftgpu_gen_bigmat_dev", i32, vp, vp, i32, i32, u64)
 _sig("mfftgpu_gen_int64_dev", i32, vp, vp, sz, u64)
 _sig("mfftgpu_selftest_timeout", i32, vp, C.c_ulonglong)
 _sig("mfftgpu_gen_normal_f32", None, vp, vp, sz, u64)
 _sig("mfftgpu_mm_i64_noalloc", i32, vp, vp, i32, vp, i32, vp)
 _sig("mfftgpu_decode_words_f32", C.c_float, vp, i32, i32, i32)
+_sig("mfftgpu_decode_words_f64", C.c_double, vp, i32, i32, i32)
+_sig("mfftgpu_decode_words_round", i32, vp, i32, i32, i32, C.POINTER(C.c_uint64),
+     C.POINTER(C.c_int))
 _sig("mfftgpu_selftest_pointwise", i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
      C.POINTER(C.c_longlong))
 _sig("mfftgpu_selftest_school", i32, vp, i32, i32, i32, i32, i32, i32, C.POINTER(C.c_longlong))
@@ -114,6 +119,12 @@ _sig("fpx_encode", None, C.POINTER(FpxCtx), vp, vp)
 _sig("fpx_decode_f32", None, C.POINTER(FpxCtx), vp)
 _sig("fpx_free", None, C.POINTER(FpxCtx))
 _sig("fpx_gemm_f32", i32, vp, vp, i32, i32, vp)
+_sig("fpx_init_d", i32, C.POINTER(FpxCtx), vp, vp, i32, i32)
+_sig("fpx_encode_d", None, C.POINTER(FpxCtx), vp, vp)
+_sig("fpx_decode_f64", None, C.POINTER(FpxCtx), vp)
+_sig("fpx_decode_ld", None, C.POINTER(FpxCtx), vp)
+_sig("fpx_gemm_f64", i32, vp, vp, i32, i32, vp)
+_sig("fpx_gemm_f64_limbplane", i32, vp, vp, i32, i32, vp)
 _sig("mm_limbplane", None, vp, vp, i32, i32, i32, vp, i32)
 _sig("mm_limbplane_signed", None, vp, vp, i32, i32, vp, i32)
 _sig("conv_limbplane", None, vp, vp, vp, i32, i32, i32)

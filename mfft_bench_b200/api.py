@@ -199,6 +199,21 @@ class Context:
                     "fp32")
         return out
 
+    def fp64(self, A, B, n, force_bits=512, out=None, rows=None):
+        """fp64 GEMM through the exact fixed-point embedding (fpx_*_d)."""
+        if _is_cuda(A):
+            import torch
+            r0, r1 = rows or (0, n)
+            if out is None:
+                out = torch.empty((r1 - r0) * n, dtype=torch.float64, device=A.device)
+            self._check(lib.mfftgpu_fp64_dev(self._h, _ptr(A), _ptr(B), n, force_bits,
+                                             _ptr(out), r0, r1), "fp64_dev")
+            return out
+        out = np.empty(n * n, np.float64) if out is None else out
+        self._check(lib.mfftgpu_fp64(self._h, _ptr(A), _ptr(B), n, force_bits, _ptr(out)),
+                    "fp64")
+        return out
+
     def gen_bigmat(self, m, n, L, seed):
         """bigmat_rand on the device into the uint16 CUDA tensor m."""
         self._check(lib.mfftgpu_gen_bigmat_dev(self._h, _ptr(m), n, L, seed), "gen_bigmat")
@@ -314,6 +329,51 @@ class Fpx:
         lib.fpx_free(C.byref(self.c))
 
 
+class Fpx64(Fpx):
+    """fpx_init_d / fpx_encode_d / conv_mfft / fpx_decode_f64 / fpx_decode_ld
+    (src/fpfixed.c:109-172, 291-322)."""
+
+    def __init__(self, A, B, n, force_bits=512):
+        self.c = FpxCtx()
+        self.n = n
+        self.A, self.B = np.ascontiguousarray(A, np.float64), np.ascontiguousarray(B, np.float64)
+        if lib.fpx_init_d(C.byref(self.c), _ptr(self.A), _ptr(self.B), n, force_bits) != 0:
+            raise MfftError(1, "fpx_init_d")
+
+    def encode(self):
+        lib.fpx_encode_d(C.byref(self.c), _ptr(self.A), _ptr(self.B))
+
+    def decode_f64(self):
+        out = np.empty(self.n * self.n, np.float64)
+        lib.fpx_decode_f64(C.byref(self.c), _ptr(out))
+        return out
+
+    def decode_ld(self):
+        out = np.empty(self.n * self.n, np.longdouble)
+        lib.fpx_decode_ld(C.byref(self.c), _ptr(out))
+        return out
+
+
+def fpx_gemm_f64(A, B, n, force_bits=512):
+    out = np.empty(n * n, np.float64)
+    A = np.ascontiguousarray(A, np.float64)
+    B = np.ascontiguousarray(B, np.float64)
+    rc = lib.fpx_gemm_f64(_ptr(A), _ptr(B), n, force_bits, _ptr(out))
+    if rc:
+        raise MfftError(rc, "fpx_gemm_f64")
+    return out
+
+
+def fpx_gemm_f64_limbplane(A, B, n, force_bits=512):
+    out = np.empty(n * n, np.float64)
+    A = np.ascontiguousarray(A, np.float64)
+    B = np.ascontiguousarray(B, np.float64)
+    rc = lib.fpx_gemm_f64_limbplane(_ptr(A), _ptr(B), n, force_bits, _ptr(out))
+    if rc:
+        raise MfftError(rc, "fpx_gemm_f64_limbplane")
+    return out
+
+
 def fpx_gemm_f32(A, B, n, force_bits=512):
     out = np.empty(n * n, np.float32)
     A = np.ascontiguousarray(A, np.float32)
@@ -366,6 +426,21 @@ def gen_normal_f32(n, seed):
     B = np.empty(n * n, np.float32)
     lib.mfftgpu_gen_normal_f32(_ptr(A), _ptr(B), n * n, C.c_uint64(seed))
     return A, B
+
+
+def decode_words_f64(words, bit_off, S):
+    """Host run of the device fp64 rounding rule (self-test)."""
+    w = np.array(words, dtype=np.uint32)
+    return float(lib.mfftgpu_decode_words_f64(_ptr(w), w.size, bit_off, S))
+
+
+def decode_words_round(words, bit_off, bits):
+    """(sign, sig, shift) of the shared extract + round_to rule."""
+    w = np.array(words, dtype=np.uint32)
+    sig, shift = C.c_uint64(0), C.c_int(0)
+    sgn = lib.mfftgpu_decode_words_round(_ptr(w), w.size, bit_off, bits, C.byref(sig),
+                                         C.byref(shift))
+    return sgn, sig.value, shift.value
 
 
 def decode_words_f32(words, bit_off, S):

@@ -1,5 +1,5 @@
-// decode.cuh -- exact big-integer -> fp32 rounding of the fp32 embedding,
-// shared by the GPU kernel and the host self-test entry point.
+// decode.cuh -- exact big-integer -> fp32 / fp64 rounding of the fixed-point
+// embeddings, shared by the GPU kernels and the host self-test entry points.
 //
 // Semantics follow fpx_decode_f32 (src/fpfixed.c:212-285): the exact product
 // is carried into 16-bit limbs (two's complement), negated if negative, the
@@ -72,6 +72,97 @@ MFFTB_HD bool any_bits_below(const uint32_t* w, int nw, int lim) {
     int rem = lim & 31;
     if (rem && full < nw && (w[full] & ((1u << rem) - 1u))) return true;
     return false;
+}
+
+// sig * 2^e rounded to the nearest fp64 (ties to even), sig < 2^53; the
+// IEEE-754 binary64 counterpart of scale_to_f32_bits (ldexp of fpx_decode_f64,
+// src/fpfixed.c:308-322).
+MFFTB_HD uint64_t scale_to_f64_bits(uint64_t sig, int e) {
+    if (sig == 0) return 0ull;
+    const int nb = bitlen64(sig);
+    const int E = e + nb - 1;  // value in [2^E, 2^(E+1))
+    if (E > 1023) return 0x7FF0000000000000ull;
+    if (E >= -1022) {
+        uint64_t mant = sig << (53 - nb);
+        return ((uint64_t)(E + 1023) << 52) | (mant & 0xFFFFFFFFFFFFFull);
+    }
+    // subnormal: units of 2^-1074
+    const int sh = e + 1074;
+    if (sh >= 0) return sig << sh;  // exact, < 2^52
+    const int r = -sh;
+    if (r >= 64) return 0ull;
+    uint64_t q = sig >> r;
+    uint64_t rem = sig & ((1ull << r) - 1ull);
+    uint64_t half = 1ull << (r - 1);
+    if (rem > half || (rem == half && (q & 1ull))) ++q;
+    return q;
+}
+
+// Shared front half of the decode (extract + round_to of src/fpfixed.c:
+// 212-265): negate a negative value in place, locate its top 16-bit limb on
+// the grid, gather at most four limbs as `top`, round to `bits` significant
+// bits half-to-even with the sticky bit breaking ties.  Returns 0 for an
+// exact zero, else -1 / +1 with *sig and *shift set (value = sig * 2^shift).
+MFFTB_HD int decode_words_round(uint32_t* w, int nw, int bit_off, int bits, uint64_t* sig_out,
+                                int* shift_out) {
+    const bool neg = (w[nw - 1] >> 31) & 1u;
+    if (neg) {
+        uint32_t c = 1;
+        for (int i = 0; i < nw; ++i) {
+            uint64_t t = (uint64_t)(~w[i]) + c;
+            w[i] = (uint32_t)t;
+            c = (uint32_t)(t >> 32);
+        }
+    }
+    int top_word = -1;
+    for (int i = nw - 1; i >= 0; --i)
+        if (w[i]) {
+            top_word = i;
+            break;
+        }
+    if (top_word < 0) return 0;
+    const int bitlen_int = 32 * top_word + bitlen64(w[top_word]);
+    const int bitlen = bitlen_int + bit_off;
+    const int h = (bitlen - 1) >> 4;
+    const int k = h + 1 < 4 ? h + 1 : 4;
+    const int base = 16 * (h - k + 1);
+    const int tb = bitlen - base;
+    const uint64_t top = get_bits(w, nw, base - bit_off, tb);
+    const bool sticky = any_bits_below(w, nw, base - bit_off);
+    int shift = base;
+    uint64_t sig = top;
+    if (tb > bits) {
+        int drop = tb - bits;
+        uint64_t q = top >> drop;
+        uint64_t rem = top & ((1ULL << drop) - 1);
+        uint64_t half = 1ULL << (drop - 1);
+        int up = rem > half ? 1 : (rem < half ? 0 : (sticky ? 1 : (int)(q & 1)));
+        q += up;
+        if (q >> bits) {
+            q >>= 1;
+            ++drop;
+        }
+        shift += drop;
+        sig = q;
+    }
+    *sig_out = sig;
+    *shift_out = shift;
+    return neg ? -1 : 1;
+}
+
+// fpx_decode_f64's rule on the same word array (53-bit significand).
+MFFTB_HD double decode_words_f64(uint32_t* w, int nw, int bit_off, int S) {
+    uint64_t sig;
+    int shift;
+    const int sgn = decode_words_round(w, nw, bit_off, 53, &sig, &shift);
+    uint64_t bits = sgn ? scale_to_f64_bits(sig, shift - S) : 0ull;
+    if (sgn < 0) bits |= 0x8000000000000000ull;
+    union {
+        uint64_t u;
+        double d;
+    } cv;
+    cv.u = bits;
+    return cv.d;
 }
 
 // w: the exact product as nw 32-bit words of two's complement (little

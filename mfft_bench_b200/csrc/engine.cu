@@ -18,6 +18,7 @@
 #include <new>
 
 #include "../../include/mfftgpu.h"
+#include "decode.cuh"
 #include "kernels.h"
 #include "plan.h"
 #include "runtime.h"
@@ -692,23 +693,36 @@ int mfftgpu_conv_i32_dev(mfftgpu_ctx* C, const int32_t* A32, const int32_t* B32,
     return run_product(C, P, a, b, 0, n, o);
 }
 
-// --------------------------------------------------------------------- fp32
-int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int force_bits,
-                     float* Cout, int row_begin, int row_end) {
+// --------------------------------------------------------------------- fp32 / fp64
+// The fixed-point embeddings of src/fpfixed.c: fp32 (sig 24, an entry touches
+// wr = 3 limbs) and fp64 (sig 53, wr = 5), same grid rules, same product,
+// decode rounded once to the output precision.
+static int fp_dev(mfftgpu_ctx* C, const void* A, const void* B, int n, int force_bits, void* Cout,
+                  int row_begin, int row_end, bool is64) {
     if (!C || !A || !B || !Cout || n <= 0 || force_bits < 0) return MFFTB_ERR_ARG;
     if (check_rows(n, row_begin, row_end)) return set_err(C, MFFTB_ERR_ARG, "bad row range");
     cudaSetDevice(C->device);
     cudaStream_t st = C->stream;
     const long long nn = (long long)n * n;
+    const int sig = is64 ? 53 : 24, wr = is64 ? 5 : 3;
     int rc;
-    if ((rc = scan_f32_launch(A, nn, C->d_scan, st))) return set_err(C, rc, "scan(A) failed");
-    if ((rc = scan_f32_launch(B, nn, C->d_scan + 3, st))) return set_err(C, rc, "scan(B) failed");
+    if (is64) {
+        if ((rc = scan_f64_launch(static_cast<const double*>(A), nn, C->d_scan, st)))
+            return set_err(C, rc, "scan(A) failed");
+        if ((rc = scan_f64_launch(static_cast<const double*>(B), nn, C->d_scan + 3, st)))
+            return set_err(C, rc, "scan(B) failed");
+    } else {
+        if ((rc = scan_f32_launch(static_cast<const float*>(A), nn, C->d_scan, st)))
+            return set_err(C, rc, "scan(A) failed");
+        if ((rc = scan_f32_launch(static_cast<const float*>(B), nn, C->d_scan + 3, st)))
+            return set_err(C, rc, "scan(B) failed");
+    }
     int h[6];
     CUDA_OK(cudaMemcpyAsync(h, C->d_scan, sizeof h, cudaMemcpyDeviceToHost, st));
     CUDA_OK(cudaStreamSynchronize(st));
     const int loA = h[2] ? h[0] : 0, hiA = h[2] ? h[1] : 0, anyA = h[2];
     const int loB = h[5] ? h[3] : 0, hiB = h[5] ? h[4] : 0, anyB = h[5];
-    // grid sizing of fpx_size (src/fpfixed.c:59-78) with sig = 24, wr = 3
+    // grid sizing of fpx_size (src/fpfixed.c:59-78)
     int SA, SB, L;
     const int spreadA = anyA ? hiA - loA : 0, spreadB = anyB ? hiB - loB : 0;
     if (force_bits > 0) {
@@ -717,9 +731,9 @@ int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int 
     } else {
         SA = -loA;
         SB = -loB;
-        int bits = std::max(24 + spreadA + 1, 24 + spreadB + 1);
+        int bits = std::max(sig + spreadA + 1, sig + spreadB + 1);
         int spread = std::max(spreadA, spreadB);
-        int need = (bits + 15) / 16, need2 = spread / 16 + 3;
+        int need = (bits + 15) / 16, need2 = spread / 16 + wr;
         L = next_pow2i(std::max(need, need2));
         if (L < 2) L = 2;
     }
@@ -731,7 +745,7 @@ int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int 
         lo_bit = 0;
         width = 1;
         if (!any) return;
-        int l = std::max(0, lo + S), t = std::min(16 * L, hi + S + 24);
+        int l = std::max(0, lo + S), t = std::min(16 * L, hi + S + sig);
         if (t <= l) return;
         lo_bit = l;
         width = t - l;
@@ -741,10 +755,21 @@ int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int 
     window(anyB, loB, hiB, SB, loBitB, wB);
     Plan P;
     if ((rc = plan_or_err(C, n, PLAN_VALUE, wA, wB, &P))) return rc;
-    Operand a{PACK_F32, A, n, 0, wA, 1, SA, loBitA, 16 * L - loBitA};
-    Operand b{PACK_F32, B, n, 0, wB, 1, SB, loBitB, 16 * L - loBitB};
-    OutSpec o{INV_F32, Cout, 0, n, 0, loBitA + loBitB, SA + SB, 4};
+    const int fmt = is64 ? PACK_F64 : PACK_F32;
+    Operand a{fmt, A, n, 0, wA, 1, SA, loBitA, 16 * L - loBitA};
+    Operand b{fmt, B, n, 0, wB, 1, SB, loBitB, 16 * L - loBitB};
+    OutSpec o{is64 ? INV_F64 : INV_F32, Cout, 0, n, 0, loBitA + loBitB, SA + SB, is64 ? 8 : 4};
     return run_product(C, P, a, b, row_begin, row_end, o);
+}
+
+int mfftgpu_fp32_dev(mfftgpu_ctx* C, const float* A, const float* B, int n, int force_bits,
+                     float* Cout, int row_begin, int row_end) {
+    return fp_dev(C, A, B, n, force_bits, Cout, row_begin, row_end, false);
+}
+
+int mfftgpu_fp64_dev(mfftgpu_ctx* C, const double* A, const double* B, int n, int force_bits,
+                     double* Cout, int row_begin, int row_end) {
+    return fp_dev(C, A, B, n, force_bits, Cout, row_begin, row_end, true);
 }
 
 // --------------------------------------------------------------------- host-pointer variants
@@ -804,6 +829,22 @@ int mfftgpu_conv_i32(mfftgpu_ctx* C, const int32_t* A32, const int32_t* B32, int
     rc = mfftgpu_conv_i32_dev(C, (int32_t*)dA, (int32_t*)dB, n, L, (int64_t*)dO);
     if (rc) return rc;
     CUDA_OK(cudaMemcpyAsync(Cw, dO, ob, cudaMemcpyDeviceToHost, C->stream));
+    return mfftgpu_sync(C);
+}
+
+int mfftgpu_fp64(mfftgpu_ctx* C, const double* A, const double* B, int n, int force_bits,
+                 double* Cout) {
+    if (!C || !A || !B || !Cout || n <= 0) return MFFTB_ERR_ARG;
+    cudaSetDevice(C->device);
+    const size_t in = (size_t)n * n * 8;
+    char *dA, *dB, *dO;
+    int rc = stage(C, in, in, in, &dA, &dB, &dO);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
+    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
+    rc = mfftgpu_fp64_dev(C, (double*)dA, (double*)dB, n, force_bits, (double*)dO, 0, n);
+    if (rc) return rc;
+    CUDA_OK(cudaMemcpyAsync(Cout, dO, in, cudaMemcpyDeviceToHost, C->stream));
     return mfftgpu_sync(C);
 }
 
@@ -988,6 +1029,16 @@ int mfftgpu_selftest_timeout(mfftgpu_ctx* C, unsigned long long timeout_ns) {
 
 float mfftgpu_decode_words_f32(uint32_t* w, int nw, int bit_off, int S) {
     return decode_words_host(w, nw, bit_off, S);
+}
+
+double mfftgpu_decode_words_f64(uint32_t* w, int nw, int bit_off, int S) {
+    return decode_words_host_f64(w, nw, bit_off, S);
+}
+
+int mfftgpu_decode_words_round(uint32_t* w, int nw, int bit_off, int bits, uint64_t* sig,
+                               int* shift) {
+    if (!w || nw <= 0 || bits < 1 || bits > 63 || !sig || !shift) return 0;
+    return decode_words_round(w, nw, bit_off, bits, sig, shift);
 }
 
 }  // extern "C"

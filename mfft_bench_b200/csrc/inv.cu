@@ -10,8 +10,8 @@
 //   * INV_U16: carry into 16-bit two's complement limbs, normalize_planes
 //     (src/bigmat.c:48-60);
 //   * INV_I64: the unnormalised int64 planes conv_mfft returns (limb mode);
-//   * INV_F32: extract + round_to + ldexpf of fpx_decode_f32
-//     (src/fpfixed.c:212-285), see decode.cuh.
+//   * INV_F32 / INV_F64: extract + round_to + ldexpf / ldexp of
+//     fpx_decode_f32 / fpx_decode_f64 (src/fpfixed.c:212-322), see decode.cuh.
 //
 // A CTA owns E consecutive elements (E <= 32) and keeps their NB*K int64
 // transformed values in shared memory; 256 threads cooperate on the loads
@@ -25,6 +25,14 @@
 #include "runtime.h"
 
 namespace mfftb {
+
+// fp output of one element from its exact product words
+__device__ __forceinline__ void store_float(const InvArgs& a, long long o, uint32_t* words, int nw) {
+    if (a.out_kind == INV_F64)
+        reinterpret_cast<double*>(a.out)[o] = decode_words_f64(words, nw, a.bit_off, a.S_scale);
+    else
+        reinterpret_cast<float*>(a.out)[o] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
+}
 
 constexpr int INV_THREADS = 256;
 constexpr int INV_VPT = 16;     // inverse-DFT outputs per thread (registers)
@@ -170,8 +178,7 @@ __global__ void __launch_bounds__(INV_THREADS) inverse_kernel(const InvArgs a) {
         bits = 0;
         nb = 0;
     }
-    float* out = reinterpret_cast<float*>(a.out);
-    out[(long long)row * a.ldo + col] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
+    store_float(a, (long long)row * a.ldo + col, words, nw);
 }
 
 // ---------------------------------------------------------------- register variant
@@ -337,8 +344,7 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
         bits = 0;
         nb = 0;
     }
-    float* out = reinterpret_cast<float*>(a.out);
-    out[(long long)row * a.ldo + col] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
+    store_float(a, (long long)row * a.ldo + col, words, nw);
 }
 
 // ---------------------------------------------------------------- lane variant
@@ -644,7 +650,8 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if ((1 << a.log2NB) != a.NB || (1 << a.lgS) != a.S || (1 << a.lgK) != a.K ||
         (1 << a.lgE) != a.elems)
         return MFFTB_ERR_ARG;
-    if (a.out_kind == INV_F32 && (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
+    if ((a.out_kind == INV_F32 || a.out_kind == INV_F64) &&
+        (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
         return MFFTB_ERR_UNSUPPORTED;
     if (a.positions <= (a.NB + 1) * a.S) {
         if (a.NB == 8 && a.K == 8) return launch_reg<8, 8>(a, stream);
@@ -764,8 +771,7 @@ __global__ void __launch_bounds__(SC_THREADS) school_carry_kernel(const InvArgs 
         bits = 0;
         nb = 0;
     }
-    float* out = reinterpret_cast<float*>(a.out);
-    out[o] = decode_words_f32(words, nw, a.bit_off, a.S_scale);
+    store_float(a, o, words, nw);
 }
 
 // Integer output, 4 consecutive elements per thread: 16-byte loads of every
@@ -870,7 +876,8 @@ static int school_carry_launch(const InvArgs& a, cudaStream_t stream) {
         return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
     }
     if (a.b < 1 || a.b > 15 || a.nchunk < 1 || a.U < 1) return MFFTB_ERR_ARG;
-    if (a.out_kind == INV_F32 && (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
+    if ((a.out_kind == INV_F32 || a.out_kind == INV_F64) &&
+        (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
         return MFFTB_ERR_UNSUPPORTED;
     const long long total = (long long)a.rows * a.lda;
     const long long blocks = (total + SC_THREADS - 1) / SC_THREADS;
@@ -879,15 +886,25 @@ static int school_carry_launch(const InvArgs& a, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------- fp32 exponent scan
-__global__ void scan_f32_kernel(const float* X, long long count, int* out3) {
+__device__ __forceinline__ int frexp_e(float x) {
+    int e;
+    frexpf(x, &e);
+    return e;
+}
+__device__ __forceinline__ int frexp_e(double x) {
+    int e;
+    frexp(x, &e);
+    return e;
+}
+
+template <typename T, int SIG>
+__global__ void scan_fp_kernel(const T* X, long long count, int* out3) {
     int lo = 1 << 30, hi = -(1 << 30), any = 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count;
          i += (long long)gridDim.x * blockDim.x) {
-        float x = __ldg(X + i);
-        if (x == 0.0f || !isfinite(x)) continue;
-        int e;
-        frexpf(x, &e);
-        int e2 = e - 24;
+        T x = __ldg(X + i);
+        if (x == (T)0 || !isfinite(x)) continue;
+        int e2 = frexp_e(x) - SIG;
         lo = min(lo, e2);
         hi = max(hi, e2);
         any = 1;
@@ -904,19 +921,30 @@ __global__ void scan_f32_kernel(const float* X, long long count, int* out3) {
     }
 }
 
-int scan_f32_launch(const float* X, long long count, int* out3, cudaStream_t stream) {
+template <typename T, int SIG>
+static int scan_launch(const T* X, long long count, int* out3, cudaStream_t stream) {
     int init[3] = {1 << 30, -(1 << 30), 0};
     if (cudaMemcpyAsync(out3, init, sizeof init, cudaMemcpyHostToDevice, stream) != cudaSuccess)
         return MFFTB_ERR_CUDA;
     long long blocks = (count + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
     if (blocks < 1) blocks = 1;
-    scan_f32_kernel<<<(unsigned)blocks, 256, 0, stream>>>(X, count, out3);
+    scan_fp_kernel<T, SIG><<<(unsigned)blocks, 256, 0, stream>>>(X, count, out3);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+int scan_f32_launch(const float* X, long long count, int* out3, cudaStream_t stream) {
+    return scan_launch<float, 24>(X, count, out3, stream);
+}
+int scan_f64_launch(const double* X, long long count, int* out3, cudaStream_t stream) {
+    return scan_launch<double, 53>(X, count, out3, stream);
 }
 
 float decode_words_host(uint32_t* w, int nw, int bit_off, int S) {
     return decode_words_f32(w, nw, bit_off, S);
+}
+double decode_words_host_f64(uint32_t* w, int nw, int bit_off, int S) {
+    return decode_words_f64(w, nw, bit_off, S);
 }
 
 }  // namespace mfftb

@@ -12,6 +12,7 @@ enum PackFmt {
     PACK_I64 = 1,      // int64 row-major [n][n]
     PACK_F32 = 2,      // fp32 row-major [n][n] on a fixed-point grid
     PACK_I32LIMB = 3,  // int32 limb planes [L][n][n], limbs are the digits (conv_mfft)
+    PACK_F64 = 4,      // fp64 row-major [n][n] on a fixed-point grid (53-bit significand)
 };
 
 struct PackArgs {
@@ -55,6 +56,7 @@ enum InvOut {
     INV_U16 = 0,   // normalised two's complement 16-bit limb planes [RL][rows][ldo]
     INV_I64 = 1,   // unnormalised int64 limb-convolution planes [P][rows][ldo] (limb mode)
     INV_F32 = 2,   // fp32 [rows][ldo], rounded once (fpx_decode_f32 semantics)
+    INV_F64 = 3,   // fp64 [rows][ldo], rounded once (fpx_decode_f64 semantics)
 };
 
 struct InvArgs {
@@ -71,8 +73,8 @@ struct InvArgs {
     long long out_plane;  // elements between output planes
     int ldo;
     int RL;               // INV_U16: limbs to emit; INV_I64: planes to emit
-    int bit_off;          // INV_F32: true grid position of internal bit 0
-    int S_scale;          // INV_F32: SA + SB
+    int bit_off;          // INV_F32 / INV_F64: true grid position of internal bit 0
+    int S_scale;          // INV_F32 / INV_F64: SA + SB
     int elems;            // elements per CTA (power of two, <= 32)
     int* err;
     int variant;          // 0 auto, 1 the generic shared-memory kernel only
@@ -86,8 +88,11 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream);
 // fp32 exponent scan of src/fpfixed.c:40-54: out[0] = min e2, out[1] = max e2,
 // out[2] = any finite non-zero (e2 = frexp exponent - 24).
 int scan_f32_launch(const float* X, long long count, int* out3, cudaStream_t stream);
+// fp64 counterpart (src/fpfixed.c:115-128, e2 = frexp exponent - 53)
+int scan_f64_launch(const double* X, long long count, int* out3, cudaStream_t stream);
 
-// test-only host entry: the device decode rule run on the CPU
+// test-only host entries: the device decode rules run on the CPU
 float decode_words_host(uint32_t* w, int nw, int bit_off, int S);
+double decode_words_host_f64(uint32_t* w, int nw, int bit_off, int S);
 
 }  // namespace mfftb

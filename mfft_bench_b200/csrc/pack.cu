@@ -66,6 +66,34 @@ __device__ __forceinline__ int digit_f32(float x, int m, int b, int S_grid, int 
     return x < 0.0f ? -d : d;
 }
 
+// fp64 on the same grid (encode_one_d, src/fpfixed.c:141-160): the 53-bit
+// significand mi = |m| * 2^53 placed at bit off = e - 53 + S, bits at or above
+// the grid top dropped, digit m of the window starting at lo_bit.
+__device__ __forceinline__ int digit_f64(double x, int m, int b, int S_grid, int lo_bit,
+                                         int trunc_rel) {
+    if (x == 0.0 || !isfinite(x)) return 0;
+    int e;
+    double mf = frexp(x, &e);
+    const uint64_t mi = (uint64_t)(fabs(mf) * 9007199254740992.0);  // 2^53, exact
+    const int off = e - 53 + S_grid;
+    if (off < 0) return 0;                // below the grid (src/fpfixed.c:149)
+    const int rel = off - lo_bit;
+    const int p = m * b;
+    const int lim = trunc_rel - p;
+    if (lim <= 0) return 0;
+    uint64_t field;
+    if (p >= rel) {
+        const int s = p - rel;
+        field = s >= 53 ? 0 : (mi >> s);
+    } else {
+        const int s = rel - p;            // only the low b - s bits of mi reach the field
+        field = s >= b ? 0 : ((mi & ((1ull << (b - s)) - 1ull)) << s);
+    }
+    const uint64_t mask = lim >= b ? ((1ull << b) - 1ull) : ((1ull << lim) - 1ull);
+    const int d = (int)(field & mask);
+    return x < 0.0 ? -d : d;
+}
+
 template <int FMT>
 __device__ __forceinline__ int entry_digit(const PackArgs& a, int i, int j, int m) {
     if (i < 0 || i >= a.n || j >= a.n) return 0;
@@ -82,6 +110,9 @@ __device__ __forceinline__ int entry_digit(const PackArgs& a, int i, int j, int 
             return (int)(t >> p);
         }
         return (int)(((uint64_t)x >> p) & ((1u << a.b) - 1u));
+    } else if (FMT == PACK_F64) {
+        double x = __ldg(reinterpret_cast<const double*>(a.src) + idx);
+        return digit_f64(x, m, a.b, a.S_grid, a.lo_bit, a.trunc_rel);
     } else {
         float x = __ldg(reinterpret_cast<const float*>(a.src) + idx);
         return digit_f32(x, m, a.b, a.S_grid, a.lo_bit, a.trunc_rel);
@@ -304,6 +335,8 @@ int pack_launch(const PackArgs& a, cudaStream_t stream) {
             MFFTB_PACK(PACK_I64)
         } else if (a.fmt == PACK_F32) {
             MFFTB_PACK(PACK_F32)
+        } else if (a.fmt == PACK_F64) {
+            MFFTB_PACK(PACK_F64)
         } else {
             return MFFTB_ERR_ARG;
         }

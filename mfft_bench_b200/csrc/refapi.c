@@ -387,6 +387,26 @@ static int next_pow2(int x)
     return r;
 }
 
+/* exponent range of finite non-zero fp64 entries, e2 = frexp exponent - 53
+ * (src/fpfixed.c:115-128) */
+static void dscan(const double *X, size_t nn, int *lo, int *hi, int *any)
+{
+    int l = 1 << 30, h = -(1 << 30), seen = 0;
+    for (size_t i = 0; i < nn; i++) {
+        double x = X[i];
+        if (x == 0.0 || !isfinite(x)) continue;
+        int e;
+        frexp(x, &e);
+        if (e - 53 < l) l = e - 53;
+        if (e - 53 > h) h = e - 53;
+        seen = 1;
+    }
+    if (!seen) l = h = 0;
+    *lo = l;
+    *hi = h;
+    *any = seen;
+}
+
 /* exponent range of finite non-zero entries, e2 = frexp exponent - 24
  * (src/fpfixed.c:40-54) */
 static void fscan(const float *X, size_t nn, int *lo, int *hi, int *any)
@@ -407,15 +427,14 @@ static void fscan(const float *X, size_t nn, int *lo, int *hi, int *any)
     *any = seen;
 }
 
-/* grid sizing and allocation: src/fpfixed.c:59-108 */
-int fpx_init(fpx_ctx *c, const float *A, const float *B, int n, int force_bits)
+/* grid sizing and allocation shared by both precisions (src/fpfixed.c:59-94):
+ * sig = significand bits, wr = limbs one shifted significand can touch */
+static int fpx_setup(fpx_ctx *c, int n, int force_bits, int sig, int wr, int loA, int hiA,
+                     int anyA, int loB, int hiB, int anyB)
 {
     size_t nn = (size_t)n * n;
-    int loA, hiA, loB, hiB, anyA, anyB;
-    fscan(A, nn, &loA, &hiA, &anyA);
-    fscan(B, nn, &loB, &hiB, &anyB);
     memset(c, 0, sizeof *c);
-    c->sig = 24;
+    c->sig = sig;
     c->spreadA = anyA ? hiA - loA : 0;
     c->spreadB = anyB ? hiB - loB : 0;
     int L;
@@ -425,10 +444,10 @@ int fpx_init(fpx_ctx *c, const float *A, const float *B, int n, int force_bits)
     } else {
         c->SA = -loA;
         c->SB = -loB;
-        int bitsA = 24 + c->spreadA + 1, bitsB = 24 + c->spreadB + 1;
+        int bitsA = sig + c->spreadA + 1, bitsB = sig + c->spreadB + 1;
         int bits = bitsA > bitsB ? bitsA : bitsB;
         int spread = c->spreadA > c->spreadB ? c->spreadA : c->spreadB;
-        int need = (bits + LIMB_BITS - 1) / LIMB_BITS, need2 = spread / LIMB_BITS + 3;
+        int need = (bits + LIMB_BITS - 1) / LIMB_BITS, need2 = spread / LIMB_BITS + wr;
         L = next_pow2(need > need2 ? need : need2);
         if (L < 2) L = 2;
     }
@@ -448,6 +467,27 @@ int fpx_init(fpx_ctx *c, const float *A, const float *B, int n, int force_bits)
     return 0;
 }
 
+/* src/fpfixed.c:96-108 */
+int fpx_init(fpx_ctx *c, const float *A, const float *B, int n, int force_bits)
+{
+    size_t nn = (size_t)n * n;
+    int loA, hiA, loB, hiB, anyA, anyB;
+    fscan(A, nn, &loA, &hiA, &anyA);
+    fscan(B, nn, &loB, &hiB, &anyB);
+    return fpx_setup(c, n, force_bits, 24, 3, loA, hiA, anyA, loB, hiB, anyB);
+}
+
+/* src/fpfixed.c:130-140: a 53-bit significand shifted by up to 15 touches
+ * five limbs */
+int fpx_init_d(fpx_ctx *c, const double *A, const double *B, int n, int force_bits)
+{
+    size_t nn = (size_t)n * n;
+    int loA, hiA, loB, hiB, anyA, anyB;
+    dscan(A, nn, &loA, &hiA, &anyA);
+    dscan(B, nn, &loB, &hiB, &anyB);
+    return fpx_setup(c, n, force_bits, 53, 5, loA, hiA, anyA, loB, hiB, anyB);
+}
+
 /* significand shifted onto the grid, up to three signed 16-bit limbs
  * (src/fpfixed.c:175-193) */
 static void encode_entry(int32_t *plane, size_t nn, size_t idx, float x, int L, int S)
@@ -463,6 +503,34 @@ static void encode_entry(int32_t *plane, size_t nn, size_t idx, float x, int L, 
     int32_t sgn = x < 0.0f ? -1 : 1;
     for (int t = 0; t < 3 && lo + t < L; t++)
         plane[(size_t)(lo + t) * nn + idx] = sgn * (int32_t)((v >> (16 * t)) & 0xFFFFu);
+}
+
+/* fp64 significand on the grid through 128-bit staging, up to five signed
+ * 16-bit limbs (src/fpfixed.c:141-160) */
+static void encode_entry_d(int32_t *plane, size_t nn, size_t idx, double x, int L, int S)
+{
+    if (x == 0.0 || !isfinite(x)) return;
+    int e;
+    double m = frexp(x, &e);
+    uint64_t mi = (uint64_t)(fabs(m) * 9007199254740992.0);
+    int off = e - 53 + S;
+    if (off < 0) return;
+    int lo = off >> 4;
+    unsigned __int128 v = (unsigned __int128)mi << (off & 15);
+    int32_t sgn = x < 0.0 ? -1 : 1;
+    for (int t = 0; t < 5 && lo + t < L; t++)
+        plane[(size_t)(lo + t) * nn + idx] = sgn * (int32_t)((uint64_t)(v >> (16 * t)) & 0xFFFFu);
+}
+
+void fpx_encode_d(fpx_ctx *c, const double *A, const double *B)
+{
+    size_t nn = (size_t)c->n * c->n;
+    double t0 = now_sec();
+    memset(c->A32, 0, (size_t)c->L * nn * sizeof(int32_t));
+    memset(c->B32, 0, (size_t)c->L * nn * sizeof(int32_t));
+    for (size_t i = 0; i < nn; i++) encode_entry_d(c->A32, nn, i, A[i], c->L, c->SA);
+    for (size_t i = 0; i < nn; i++) encode_entry_d(c->B32, nn, i, B[i], c->L, c->SB);
+    c->enc_secs = now_sec() - t0;
 }
 
 void fpx_encode(fpx_ctx *c, const float *A, const float *B)
@@ -503,6 +571,77 @@ void fpx_decode_f32(fpx_ctx *c, float *C)
         free(w);
     }
     c->dec_secs = now_sec() - t0;
+}
+
+/* the exact value of entry i as 32-bit two's complement words */
+static void entry_words(const fpx_ctx *c, size_t nn, long long i, uint32_t *w, int nw)
+{
+    int P = 2 * c->L - 1;
+    int64_t carry = 0;
+    memset(w, 0, (size_t)nw * sizeof(uint32_t));
+    for (int k = 0; k < 2 * nw; k++) {
+        int64_t v = (k < P ? c->Cw[(size_t)k * nn + i] : 0) + carry;
+        w[k >> 1] |= (uint32_t)(v & 0xFFFF) << (16 * (k & 1));
+        carry = v >> 16;
+    }
+}
+
+/* src/fpfixed.c:308-322: round once to 53 bits */
+void fpx_decode_f64(fpx_ctx *c, double *C)
+{
+    size_t nn = (size_t)c->n * c->n;
+    int RL = 2 * c->L + 2;
+    int nw = (RL + 1) / 2 + 1;
+    int S = c->SA + c->SB;
+    double t0 = now_sec();
+#pragma omp parallel
+    {
+        uint32_t *w = malloc((size_t)nw * sizeof(uint32_t));
+#pragma omp for schedule(static)
+        for (long long i = 0; i < (long long)nn; i++) {
+            entry_words(c, nn, i, w, nw);
+            C[i] = mfftgpu_decode_words_f64(w, nw, 0, S);
+        }
+        free(w);
+    }
+    c->dec_secs = now_sec() - t0;
+}
+
+/* src/fpfixed.c:291-306: the reference-precision decode, rounded to the
+ * 64-bit significand of x86 long double (ldexpl of the host libm) */
+void fpx_decode_ld(fpx_ctx *c, long double *C)
+{
+    size_t nn = (size_t)c->n * c->n;
+    int RL = 2 * c->L + 2;
+    int nw = (RL + 1) / 2 + 1;
+    int S = c->SA + c->SB;
+    uint32_t *w = malloc((size_t)nw * sizeof(uint32_t));
+    if (!w) return;
+    for (long long i = 0; i < (long long)nn; i++) {
+        entry_words(c, nn, i, w, nw);
+        uint64_t sig;
+        int shift;
+        int sgn = mfftgpu_decode_words_round(w, nw, 0, 63, &sig, &shift);
+        C[i] = sgn ? (long double)sgn * ldexpl((long double)sig, shift - S) : 0.0L;
+    }
+    free(w);
+}
+
+int fpx_gemm_f64(const double *A, const double *B, int n, int force_bits, double *C)
+{
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return g_status;
+    return finish(c, mfftgpu_fp64(c, A, B, n, force_bits, C), "fpx_gemm_f64");
+}
+
+int fpx_gemm_f64_limbplane(const double *A, const double *B, int n, int force_bits, double *C)
+{
+    mfftgpu_ctx *c = default_ctx();
+    if (!c) return g_status;
+    int prev = with_school(c, 1);
+    int rc = mfftgpu_fp64(c, A, B, n, force_bits, C);
+    with_school(c, prev);
+    return finish(c, rc, "fpx_gemm_f64_limbplane");
 }
 
 void fpx_free(fpx_ctx *c)

@@ -523,6 +523,143 @@ void orc_fpx_entries(const float *A, const float *B, int n, int force_bits, int 
 }
 
 /* ------------------------------------------------------------------ *
+ * fp64 on the same grid (src/fpfixed.c:109-172, 308-322): 53-bit
+ * significand, up to five limbs per entry through 128-bit staging, round once
+ * to 53 bits, ldexp.
+ * ------------------------------------------------------------------ */
+/* src/fpfixed.c:115-128 */
+static void dscan(const double *X, size_t nn, int *lo, int *hi, int *any)
+{
+    int l = 1 << 30, h = -(1 << 30), seen = 0;
+    for (size_t i = 0; i < nn; i++) {
+        double x = X[i];
+        if (x == 0.0 || !isfinite(x)) continue;
+        int e;
+        frexp(x, &e);
+        int e2 = e - 53;
+        if (e2 < l) l = e2;
+        if (e2 > h) h = e2;
+        seen = 1;
+    }
+    if (!seen) { l = 0; h = 0; }
+    *lo = l; *hi = h; *any = seen;
+}
+
+/* src/fpfixed.c:141-160 */
+static void encode_one_d(int32_t *plane, size_t nn, size_t idx, double x, int L, int S)
+{
+    if (x == 0.0 || !isfinite(x)) return;
+    int e;
+    double m = frexp(x, &e);
+    int64_t mi = (int64_t)(fabs(m) * 9007199254740992.0);
+    int off = e - 53 + S;
+    if (off < 0) return;
+    int lo = off >> 4, sh = off & 15;
+    unsigned __int128 v = (unsigned __int128)mi << sh;
+    int sgn = x < 0.0 ? -1 : 1;
+    for (int t = 0; t < 5; t++) {
+        int w = lo + t;
+        if (w >= L) break;
+        uint64_t chunk = (uint64_t)(v >> (16 * t));
+        plane[(size_t)w * nn + idx] = sgn * (int32_t)(chunk & 0xFFFFu);
+    }
+}
+
+/* extract + round_to(53) + ldexp for one entry (src/fpfixed.c:214-265,
+ * 308-322) */
+double orc_decode_f64_entry(const int64_t *cw, int L, int S)
+{
+    int RL = 2 * L + 2, P = 2 * L - 1;
+    int32_t *limb = malloc((size_t)RL * 4);
+    int64_t carry = 0;
+    for (int w = 0; w < RL; w++) {
+        int64_t t = (w < P ? cw[w] : 0) + carry;
+        limb[w] = (int32_t)(t & 0xFFFF);
+        carry = t >> 16;
+    }
+    int neg = carry < 0;
+    if (neg) {
+        int32_t borrow = 1;
+        for (int w = 0; w < RL; w++) {
+            int32_t t = (~limb[w] & 0xFFFF) + borrow;
+            limb[w] = t & 0xFFFF;
+            borrow = t >> 16;
+        }
+    }
+    int h = -1;
+    for (int w = RL - 1; w >= 0; w--) if (limb[w]) { h = w; break; }
+    if (h < 0) { free(limb); return 0.0; }
+    int bl = 0;
+    { int32_t v = limb[h]; while (v) { bl++; v >>= 1; } }
+    int bitlen = 16 * h + bl;
+    int k = h + 1 < 4 ? h + 1 : 4;
+    uint64_t top = 0;
+    for (int w = h; w > h - k; w--) top = (top << 16) | (uint64_t)limb[w];
+    int base = 16 * (h - k + 1);
+    int sticky = 0;
+    for (int w = h - k; w >= 0; w--) if (limb[w]) { sticky = 1; break; }
+    int tb = bitlen - base, shift = base;
+    uint64_t sig = top;
+    if (tb > 53) {
+        int drop = tb - 53;
+        uint64_t q = top >> drop, rem = top & ((1ULL << drop) - 1), half = 1ULL << (drop - 1);
+        int up = rem > half ? 1 : rem < half ? 0 : (sticky ? 1 : (int)(q & 1));
+        q += up;
+        if (q >> 53) { q >>= 1; drop++; }
+        shift += drop;
+        sig = q;
+    }
+    free(limb);
+    return (double)(neg ? -1 : 1) * ldexp((double)sig, shift - S);
+}
+
+/* Sampled entries of the fp64 path (grid sizing of src/fpfixed.c:59-78 with
+ * sig 53, five limbs touched) */
+void orc_fpx64_entries(const double *A, const double *B, int n, int force_bits, int nsamp,
+                       const int *rows, const int *cols, double *out)
+{
+    size_t nn = (size_t)n * n;
+    int loA, hiA, loB, hiB, anyA, anyB, SA, SB, L;
+    dscan(A, nn, &loA, &hiA, &anyA);
+    dscan(B, nn, &loB, &hiB, &anyB);
+    if (force_bits > 0) {
+        SA = SB = force_bits / 2;
+        L = next_pow2(force_bits / 16);
+    } else {
+        int spreadA = anyA ? hiA - loA : 0, spreadB = anyB ? hiB - loB : 0;
+        SA = -loA; SB = -loB;
+        int bitsA = 53 + spreadA + 1, bitsB = 53 + spreadB + 1;
+        int bits = bitsA > bitsB ? bitsA : bitsB;
+        int spread = spreadA > spreadB ? spreadA : spreadB;
+        int need = (bits + 15) / 16, need2 = spread / 16 + 5;
+        L = next_pow2(need > need2 ? need : need2);
+        if (L < 2) L = 2;
+    }
+    int P = 2 * L - 1;
+#pragma omp parallel
+    {
+        int32_t *a = calloc((size_t)L, 4), *b = calloc((size_t)L, 4);
+        int64_t *cw = malloc((size_t)P * 8);
+#pragma omp for schedule(dynamic)
+        for (int s = 0; s < nsamp; s++) {
+            memset(cw, 0, (size_t)P * 8);
+            for (int k = 0; k < n; k++) {
+                memset(a, 0, (size_t)L * 4);
+                memset(b, 0, (size_t)L * 4);
+                encode_one_d(a, 1, 0, A[(size_t)rows[s] * n + k], L, SA);
+                encode_one_d(b, 1, 0, B[(size_t)k * n + cols[s]], L, SB);
+                for (int u = 0; u < L; u++) {
+                    if (!a[u]) continue;
+                    for (int v = 0; v < L; v++) cw[u + v] += (int64_t)a[u] * b[v];
+                }
+            }
+            out[s] = orc_decode_f64_entry(cw, L, SA + SB);
+        }
+        free(a); free(b); free(cw);
+    }
+}
+
+/* ------------------------------------------------------------------ *
  * Size-independent property for full-size runs: every row and column sum
  * of C = A*B must match the matrix-vector products A*(B*1) and (1^T A)*B,
  * all taken modulo the Mersenne prime M = 2^61 - 1.  Entries of A, B, C

@@ -44,6 +44,9 @@ void orc_fpx_free(orc_fpx *c);
 void orc_fpx_entries(const float *A, const float *B, int n, int force_bits, int nsamp,
                      const int *rows, const int *cols, float *out);
 float orc_decode_f32_entry(const int64_t *cw, int L, int S);
+double orc_decode_f64_entry(const int64_t *cw, int L, int S);
+void orc_fpx64_entries(const double *A, const double *B, int n, int force_bits, int nsamp,
+                       const int *rows, const int *cols, double *out);
 long long orc_checksum_modp(const void *A, const void *B, int fmt, int n, int L, int is_signed,
                             const uint16_t *C, int RL);
 

@@ -81,6 +81,10 @@ class Oracle:
                                       _f32p]
         L.orc_decode_f32_entry.argtypes = [_i64p, C.c_int, C.c_int]
         L.orc_decode_f32_entry.restype = C.c_float
+        L.orc_fpx64_entries.argtypes = [_f64p, _f64p, C.c_int, C.c_int, C.c_int, _i32p, _i32p,
+                                        _f64p]
+        L.orc_decode_f64_entry.argtypes = [_i64p, C.c_int, C.c_int]
+        L.orc_decode_f64_entry.restype = C.c_double
         L.orc_checksum_modp.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                         C.c_int, _u16p, C.c_int]
         L.orc_checksum_modp.restype = C.c_longlong
@@ -186,6 +190,18 @@ class Oracle:
     def decode_f32_entry(self, cw, L, S):
         return float(self.lib.orc_decode_f32_entry(np.ascontiguousarray(cw, np.int64), L, S))
 
+    def decode_f64_entry(self, cw, L, S):
+        return float(self.lib.orc_decode_f64_entry(np.ascontiguousarray(cw, np.int64), L, S))
+
+    def fpx64_entries(self, A, B, n, force_bits, rows, cols):
+        rows = np.ascontiguousarray(rows, np.int32)
+        cols = np.ascontiguousarray(cols, np.int32)
+        out = np.empty(rows.size, np.float64)
+        self.lib.orc_fpx64_entries(np.ascontiguousarray(A, np.float64),
+                                   np.ascontiguousarray(B, np.float64), n, force_bits, rows.size,
+                                   rows, cols, out)
+        return out
+
 
 def _host_has_avx512():
     try:
@@ -223,6 +239,9 @@ class RefLib:
         L.fpx_init.argtypes = [C.POINTER(RefFpx), _f32p, _f32p, C.c_int, C.c_int]
         L.fpx_encode.argtypes = [C.POINTER(RefFpx), _f32p, _f32p]
         L.fpx_decode_f32.argtypes = [C.POINTER(RefFpx), _f32p]
+        L.fpx_init_d.argtypes = [C.POINTER(RefFpx), _f64p, _f64p, C.c_int, C.c_int]
+        L.fpx_encode_d.argtypes = [C.POINTER(RefFpx), _f64p, _f64p]
+        L.fpx_decode_f64.argtypes = [C.POINTER(RefFpx), _f64p]
         L.fpx_free.argtypes = [C.POINTER(RefFpx)]
         L.roots_selftest.argtypes = [C.c_int, C.c_int]
         L.roots_build_H.argtypes = [C.c_int]
@@ -277,6 +296,28 @@ class RefLib:
                                c.L, C.byref(plan), kernel)
             out = np.empty(nn, np.float32)
             self.lib.fpx_decode_f32(C.byref(c), out)
+            return out, (c.L, c.SA, c.SB)
+        finally:
+            self.lib.fpx_free(C.byref(c))
+
+    def fp64_gemm(self, A, B, n, force_bits, kernel=KERNEL_PACKED):
+        """fpx_init_d -> fpx_encode_d -> conv_mfft (flat plan) -> fpx_decode_f64."""
+        c = RefFpx()
+        A = np.ascontiguousarray(A, np.float64)
+        B = np.ascontiguousarray(B, np.float64)
+        if self.lib.fpx_init_d(C.byref(c), A, B, n, force_bits) != 0:
+            raise RuntimeError("fpx_init_d failed")
+        try:
+            self.lib.fpx_encode_d(C.byref(c), A, B)
+            nn = n * n
+            A32 = np.ctypeslib.as_array(c.A32, shape=(c.L * nn,))
+            B32 = np.ctypeslib.as_array(c.B32, shape=(c.L * nn,))
+            cw = np.ctypeslib.as_array(c.Cw, shape=((2 * c.L - 1) * nn,))
+            plan = self.plan(c.L)
+            self.lib.conv_mfft(cw, np.ascontiguousarray(A32), np.ascontiguousarray(B32), n,
+                               c.L, C.byref(plan), kernel)
+            out = np.empty(nn, np.float64)
+            self.lib.fpx_decode_f64(C.byref(c), out)
             return out, (c.L, c.SA, c.SB)
         finally:
             self.lib.fpx_free(C.byref(c))

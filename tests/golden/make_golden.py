@@ -4,9 +4,10 @@ Every output here comes from the reference's own C (hadilq/mfft-bench
 ``src/*.c``) compiled from source into ``oracle/_ref`` by ``oracle/Makefile``
 and called with its own signatures (``src/mfftbench.h``): ``bigmat_rand``,
 ``mm_mfft``, ``conv_mfft``, ``normalize_planes``, ``fpx_init`` /
-``fpx_encode`` / ``fpx_decode_f32``.  Inputs that the reference has no
-generator for (signed integers, N(0,1)*2^k floats) come from the oracle's
-generators and are stored in the fixture next to the outputs.
+``fpx_encode`` / ``fpx_decode_f32`` and ``fpx_init_d`` / ``fpx_encode_d`` /
+``fpx_decode_f64``.  Inputs that the reference has no generator for (signed
+integers, N(0,1)*2^k floats and doubles) come from the oracle's generators or
+a seeded numpy generator and are stored in the fixture next to the outputs.
 
 Run from the repository root:  python tests/golden/make_golden.py [--big]
 (--big adds the n=1024 W=256 unsigned digest, ~100 s of reference CPU time).
@@ -64,6 +65,21 @@ def fp32_case(r, o, n, force_bits):
             "digest_f32": f"{o.digest(C.view(np.uint16)):016x}"}
 
 
+def fp64_case(r, o, n, force_bits, tag, lo_k, hi_k, seed):
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal(n * n) * np.exp2(rng.integers(lo_k, hi_k + 1, n * n))
+    B = rng.standard_normal(n * n) * np.exp2(rng.integers(lo_k, hi_k + 1, n * n))
+    A[::13] = 0.0
+    B[5::17] = -0.0
+    A[7] = np.inf
+    B[11] = np.nan
+    C, (L, SA, SB) = r.fp64_gemm(A, B, n, force_bits)
+    np.savez_compressed(os.path.join(OUT, f"fp64_n{n}_w{force_bits}{tag}.npz"), A=A, B=B, C=C,
+                        L=L, SA=SA, SB=SB)
+    return {"n": n, "force_bits": force_bits, "tag": tag, "L": L, "SA": SA, "SB": SB,
+            "digest_f64": f"{o.digest(C.view(np.uint16)):016x}"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--big", action="store_true")
@@ -71,7 +87,7 @@ def main():
     r, o = RefLib(), Oracle()
     meta = {"generator": "tests/golden/make_golden.py", "reference_lib": os.path.basename(r.path),
             "seeds": [SEED_A, SEED_B], "digest": "FNV-1a over uint16 words, plane-major",
-            "unsigned": [], "signed": [], "fp32": []}
+            "unsigned": [], "signed": [], "fp32": [], "fp64": []}
     for n, L, full in ((8, 8, True), (16, 64, True), (48, 16, True), (64, 512, False)):
         meta["unsigned"].append(unsigned_case(r, o, n, L, full))
     if args.big:
@@ -80,6 +96,11 @@ def main():
         meta["signed"].append(signed_case(r, o, n, L, kind))
     for n, fb in ((64, 512), (64, 0), (96, 512)):
         meta["fp32"].append(fp32_case(r, o, n, fb))
+    # fp64: the 512-bit grid, the adaptive grid, and an adaptive case whose
+    # products fall into the subnormal range of binary64
+    for n, fb, tag, lo_k, hi_k, seed in ((64, 512, "", -8, 8, 1), (64, 0, "", -30, 30, 2),
+                                         (48, 0, "_tiny", -560, -530, 3)):
+        meta["fp64"].append(fp64_case(r, o, n, fb, tag, lo_k, hi_k, seed))
     old = {}
     path = os.path.join(OUT, "golden.json")
     if os.path.exists(path):

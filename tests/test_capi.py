@@ -201,6 +201,34 @@ def test_decode_rule_matches_oracle(oracle):
         assert want.view(np.uint32) == got.view(np.uint32), (cw.nonzero(), S, want, got)
 
 
+def test_decode_rule_f64_matches_oracle(oracle):
+    """The fp64 rule (53-bit round, binary64 ldexp incl. subnormals and
+    overflow) vs the oracle's restatement of fpx_decode_f64."""
+    rng = np.random.default_rng(13)
+    L = 32
+    cases = []
+    for _ in range(3000):
+        cw = np.zeros(2 * L - 1, np.int64)
+        for p in rng.integers(0, 2 * L - 1, rng.integers(1, 6)):
+            cw[p] += int(rng.integers(-(1 << 45), 1 << 45))
+        cases.append((cw, int(rng.integers(0, 2300))))  # reaches subnormal results
+    for top in ((1 << 53) + 1, (1 << 53) + 3, (1 << 54) - 1, (1 << 60) - 8, (1 << 54) + 1):
+        for lowbits in (0, 1, 0x8000, 0x4000):
+            cw = np.zeros(2 * L - 1, np.int64)
+            cw[3] = top
+            cw[2] = lowbits
+            for S in (100, 0, 1100, 2100, 2150, 20):
+                cases.append((cw.copy(), S))
+                cases.append((-cw, S))
+    big = np.zeros(2 * L - 1, np.int64)
+    big[2 * L - 2] = 1 << 40  # ~2^1032 on the grid: overflows binary64 at S = 0
+    cases += [(big, 0), (-big, 0), (np.zeros(2 * L - 1, np.int64), 512)]
+    for cw, S in cases:
+        want = np.float64(oracle.decode_f64_entry(cw, L, S))
+        got = np.float64(m.decode_words_f64(_words_from_cw(cw, 36), 0, S))
+        assert want.view(np.uint64) == got.view(np.uint64), (cw.nonzero(), S, want, got)
+
+
 def test_decode_rule_bit_offset_equivalence():
     """Shifting the integer by 2^k and passing bit_off = k is the same number."""
     rng = np.random.default_rng(5)
@@ -244,6 +272,46 @@ def test_fpx_host_decode_matches_reference(reflib):
         lib.fpx_decode_f32(C.byref(ours), o1.ctypes.data)
         reflib.lib.fpx_decode_f32(C.byref(ref), o2)
         assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+        lib.fpx_free(C.byref(ours))
+        reflib.lib.fpx_free(C.byref(ref))
+
+
+def test_fpx64_host_matches_reference(reflib):
+    """Drop-in fpx_init_d / fpx_encode_d / fpx_decode_f64 / fpx_decode_ld
+    (host side) vs the reference's own."""
+    from mfft_bench_b200._lib import FpxCtx, lib
+    from oracle.oracle import RefFpx
+    rng = np.random.default_rng(3)
+    n = 20
+    A = rng.standard_normal(n * n) * np.exp2(rng.integers(-40, 40, n * n))
+    B = rng.standard_normal(n * n) * np.exp2(rng.integers(-600, -560, n * n))
+    A[3] = 0.0
+    B[4] = np.inf
+    ldp = np.ctypeslib.ndpointer(np.longdouble, flags="C_CONTIGUOUS")
+    reflib.lib.fpx_decode_ld.argtypes = [C.POINTER(RefFpx), ldp]
+    for fb in (512, 0):
+        ours, ref = FpxCtx(), RefFpx()
+        assert lib.fpx_init_d(C.byref(ours), A.ctypes.data, B.ctypes.data, n, fb) == 0
+        assert reflib.lib.fpx_init_d(C.byref(ref), A, B, n, fb) == 0
+        assert (ours.L, ours.SA, ours.SB, ours.sig, ours.spreadB) == \
+            (ref.L, ref.SA, ref.SB, ref.sig, ref.spreadB)
+        lib.fpx_encode_d(C.byref(ours), A.ctypes.data, B.ctypes.data)
+        reflib.lib.fpx_encode_d(C.byref(ref), A, B)
+        nn = n * n
+        for x, y in ((ours.A32, ref.A32), (ours.B32, ref.B32)):
+            assert np.array_equal(np.ctypeslib.as_array(x, shape=(ours.L * nn,)),
+                                  np.ctypeslib.as_array(y, shape=(ref.L * nn,)))
+        cw = rng.integers(-(1 << 45), 1 << 45, (2 * ours.L - 1) * nn, dtype=np.int64)
+        np.ctypeslib.as_array(ours.Cw, shape=cw.shape)[:] = cw
+        np.ctypeslib.as_array(ref.Cw, shape=cw.shape)[:] = cw
+        o1, o2 = np.empty(nn, np.float64), np.empty(nn, np.float64)
+        lib.fpx_decode_f64(C.byref(ours), o1.ctypes.data)
+        reflib.lib.fpx_decode_f64(C.byref(ref), o2)
+        assert np.array_equal(o1.view(np.uint64), o2.view(np.uint64))
+        l1, l2 = np.empty(nn, np.longdouble), np.empty(nn, np.longdouble)
+        lib.fpx_decode_ld(C.byref(ours), l1.ctypes.data)
+        reflib.lib.fpx_decode_ld(C.byref(ref), l2)
+        assert np.array_equal(l1, l2)
         lib.fpx_free(C.byref(ours))
         reflib.lib.fpx_free(C.byref(ref))
 

@@ -79,6 +79,19 @@ def test_fp32_fixture(oracle, n, fb):
     assert np.array_equal(C.view(np.uint32), f["C"].view(np.uint32))
 
 
+@pytest.mark.parametrize("name", ["fp64_n64_w512", "fp64_n64_w0", "fp64_n48_w0_tiny"])
+def test_fp64_fixture(oracle, name):
+    """The oracle's fp64 restatement equals the reference's fpx_*_d path on
+    every entry (the _tiny case has ~2000 subnormal results)."""
+    f = load_fixture(name + ".npz")
+    n = int(round(np.sqrt(f["A"].size)))
+    fb = 512 if "w512" in name else 0
+    rows = np.repeat(np.arange(n), n)
+    cols = np.tile(np.arange(n), n)
+    C = oracle.fpx64_entries(f["A"], f["B"], n, fb, rows, cols)
+    assert np.array_equal(C.view(np.uint64), f["C"].view(np.uint64))
+
+
 def test_checksum_detects_single_limb_error(oracle):
     f = load_fixture("signed_n48_L16.npz")
     out = f["out"].copy()
