@@ -45,11 +45,23 @@ WORKLOADS = {
                desc="configs[3]: n=8192 fp32 N(0,1)*2^k on the 512-bit grid"),
     "c5": dict(n=16384, kind="i64", signed=True,
                desc="configs[4]: n=16384, W=64 signed int64"),
+    # not a BASELINE config: the fp64 embedding (fpx_*_d) on c4's shape
+    "f64": dict(n=8192, kind="f64", force_bits=512,
+                desc="fp64 N(0,1)*2^k (k in [-8, 8]) on the 512-bit grid, n=8192"),
 }
 DEFAULT_N = {k: v["n"] for k, v in WORKLOADS.items()}
 # bounded CPU samples of the same workload for the reference arm / baseline:
 # (sample n, what is timed).  Full-size reference runs take hours (c3-c5).
-CPU_SAMPLE_N = {"c1": 64, "c2": 256, "c3": 128, "c4": 256, "c5": 512}
+CPU_SAMPLE_N = {"c1": 64, "c2": 256, "c3": 128, "c4": 256, "c5": 512, "f64": 256}
+
+
+def normal_f64(n, seed):
+    """The f64 workload's inputs: N(0,1) * 2^k, k uniform in [-8, 8]."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal(n * n) * np.exp2(rng.integers(-8, 9, n * n))
+    B = rng.standard_normal(n * n) * np.exp2(rng.integers(-8, 9, n * n))
+    return A, B
 
 METRIC = "s per exact n x n W-bit matmul; effective int8 TOPS vs tcgen05 int8 peak"
 SUBBLOCKS = 1
@@ -182,12 +194,17 @@ def _ref_sample(workload, n_s, reps, method="mfft"):
                 r.mm_mfft(A, B, n_s, L)
             best = min(best, time.perf_counter() - t0)
     else:
-        A, B = o.normal_f32(n_s, SEED_A)
         import ctypes as C
         from oracle.oracle import RefFpx
         c = RefFpx()
-        r.lib.fpx_init(C.byref(c), A, B, n_s, w["force_bits"])
-        r.lib.fpx_encode(C.byref(c), A, B)
+        if w["kind"] == "f64":
+            A, B = normal_f64(n_s, SEED_A)
+            r.lib.fpx_init_d(C.byref(c), A, B, n_s, w["force_bits"])
+            r.lib.fpx_encode_d(C.byref(c), A, B)
+        else:
+            A, B = o.normal_f32(n_s, SEED_A)
+            r.lib.fpx_init(C.byref(c), A, B, n_s, w["force_bits"])
+            r.lib.fpx_encode(C.byref(c), A, B)
         nn = n_s * n_s
         A32 = np.ctypeslib.as_array(c.A32, shape=(c.L * nn,))
         B32 = np.ctypeslib.as_array(c.B32, shape=(c.L * nn,))
@@ -276,6 +293,11 @@ class Workload:
             B = torch.empty(L * n * n, dtype=torch.uint16, device=dev)
             ctx.gen_bigmat(A, n, L, SEED_A)
             ctx.gen_bigmat(B, n, L, SEED_B)
+        elif w["kind"] == "f64":
+            self.RL, self.planes, self.bytes_in = 1, 1, 8
+            hA, hB = normal_f64(n, SEED_A)
+            A = torch.from_numpy(hA).to(dev)
+            B = torch.from_numpy(hB).to(dev)
         else:
             from mfft_bench_b200 import gen_normal_f32
             self.RL, self.planes, self.bytes_in = 1, 1, 4
@@ -288,7 +310,7 @@ class Workload:
         P = self.planes
         self.B_local = B.view(P, n, n)[:, self.r0:self.r1, :].contiguous().view(-1) \
             if world > 1 else None
-        odt = torch.float32 if w["kind"] == "f32" else torch.uint16
+        odt = {"f32": torch.float32, "f64": torch.float64}.get(w["kind"], torch.uint16)
         self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=odt, device=dev)
         self.full_out = self.out if world == 1 else (
             torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
@@ -345,6 +367,8 @@ class Workload:
         elif w["kind"] == "u16":
             ctx.mm_u16(self.A, self.B, n, w["L"], signed=w["signed"], RL=self.RL, out=out,
                        rows=rows)
+        elif w["kind"] == "f64":
+            ctx.fp64(self.A, self.B, n, w["force_bits"], out=out, rows=rows)
         else:
             ctx.fp32(self.A, self.B, n, w["force_bits"], out=out, rows=rows)
 
@@ -392,6 +416,8 @@ def e2e_measure(ctx, wl, steps, torch):
             ctx.mm_i64(hA.numpy(), hB.numpy(), n, RL=wl.RL, out=hout.numpy())
         elif w["kind"] == "u16":
             ctx.mm_u16(u16(hA), u16(hB), n, w["L"], signed=w["signed"], RL=wl.RL, out=u16(hout))
+        elif w["kind"] == "f64":
+            ctx.fp64(hA.numpy(), hB.numpy(), n, w["force_bits"], out=hout.numpy())
         else:
             ctx.fp32(hA.numpy(), hB.numpy(), n, w["force_bits"], out=hout.numpy())
 
@@ -402,7 +428,7 @@ def e2e_measure(ctx, wl, steps, torch):
         run()
         ts.append(time.perf_counter() - t0)
     h2d = 2 * n * n * wl.bytes_in
-    d2h = wl.RL * n * n * (4 if w["kind"] == "f32" else 2)
+    d2h = wl.RL * n * n * wl.out.element_size()
     return {"value": statistics.mean(ts), "unit": "s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps}
 
@@ -436,7 +462,7 @@ def e2e_measure_dist(wl, steps, torch, dist, device):
     t = torch.tensor([statistics.mean(ts)], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     h2d = 2 * n * n * wl.bytes_in
-    d2h = wl.RL * n * n * (4 if wl.w["kind"] == "f32" else 2)
+    d2h = wl.RL * n * n * wl.out.element_size()
     return {"value": float(t.item()), "unit": "s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps,
             "note": "each rank uploads its row blocks; rank 0 downloads all of C"}
@@ -537,7 +563,9 @@ def main():
     line = {"metric": METRIC, "value": ms / 1e3, "unit": "s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8", "data": "synthetic (seeded splitmix64, reference generators)",
+            "dtype": "int8",
+            "data": ("synthetic (seeded numpy PCG64 N(0,1)*2^k)" if w["kind"] == "f64" else
+                     "synthetic (seeded splitmix64, reference generators)"),
             "config": {"workload": args.workload, "desc": w["desc"], "n": n, "method": args.method,
                        "parallelism": f"row-blocks x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (no flush needed)"},

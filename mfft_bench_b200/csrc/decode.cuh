@@ -51,17 +51,26 @@ MFFTB_HD uint32_t scale_to_f32_bits(uint32_t sig, int e) {
     return q;  // may carry into the smallest normal, which is the right encoding
 }
 
-// Bits [lo, lo+cnt) (cnt <= 64) of the little-endian word array w[0..nw).
+// Bits [lo, lo+cnt) (cnt <= 64) of the little-endian word array w[0..nw);
+// positions below 0 or past the array read as 0.  Three words are enough:
+// a 64-bit field starting at bit (lo mod 32) ends inside the third.
 MFFTB_HD uint64_t get_bits(const uint32_t* w, int nw, int lo, int cnt) {
-    uint64_t r = 0;
-    for (int i = 0; i < cnt; ++i) {
-        int p = lo + i;
-        if (p < 0) continue;
-        int wi = p >> 5;
-        if (wi >= nw) break;
-        r |= (uint64_t)((w[wi] >> (p & 31)) & 1u) << i;
+    if (cnt <= 0) return 0;
+    int lead = 0;  // zero bits contributed by positions below 0
+    if (lo < 0) {
+        lead = -lo;
+        if (lead >= cnt) return 0;
+        cnt -= lead;
+        lo = 0;
     }
-    return r;
+    const int wi = lo >> 5, sh = lo & 31;
+    const uint64_t x0 = wi < nw ? w[wi] : 0u;
+    const uint64_t x1 = wi + 1 < nw ? w[wi + 1] : 0u;
+    const uint64_t x2 = wi + 2 < nw ? w[wi + 2] : 0u;
+    uint64_t r = ((x1 << 32) | x0) >> sh;
+    if (sh) r |= x2 << (64 - sh);
+    if (cnt < 64) r &= (1ull << cnt) - 1ull;
+    return r << lead;
 }
 
 MFFTB_HD bool any_bits_below(const uint32_t* w, int nw, int lim) {

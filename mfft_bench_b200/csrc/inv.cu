@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(INV_THREADS) inverse_kernel(const InvArgs a) {
 }
 
 // ---------------------------------------------------------------- register variant
-// For plans with NB*K <= 64 (the W=64 and fp32 configurations) one thread
+// For plans with NB*K <= 64 (the W=64, fp32 and fp64 configurations) one thread
 // owns one element and keeps its NB ring elements in registers: a radix-2
 // decimation-in-time inverse FFT whose twiddles y^-e are compile-time signed
 // permutations, then fold, carry and output.  Same semantics as
@@ -417,9 +417,11 @@ __device__ __forceinline__ void lane_dit(int64_t (&x)[NB], int c) {
     }
 }
 
+// RL: 16-bit limbs the carry stage emits per element (a.RL for INV_U16; for
+// fp outputs enough limbs to hold the product plus its sign extension).
 template <int NB, int K>
 __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const InvArgs a, int seg,
-                                                                       int vec_out) {
+                                                                       int vec_out, int RL) {
     constexpr int EPW = 32 / K;                  // elements per warp
     constexpr int E = (INVL_THREADS / 32) * EPW;  // elements per CTA
     constexpr int NK = NB * K;
@@ -538,7 +540,6 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     carry = c == 0 ? 0 : co_prev + delta_prev;
 
     uint16_t* ob = reinterpret_cast<uint16_t*>(sm + (long long)E * PMAX);  // [RL][E]
-    const int RL = a.RL;
     int w = p0 * b / 16;
     uint64_t bits = 0;
     int nb = 0;
@@ -567,6 +568,22 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     }
     __syncthreads();
 
+    if (a.out_kind == INV_F32 || a.out_kind == INV_F64) {
+        // one thread per element: the limbs as 32-bit words, rounded once
+        if (threadIdx.x >= E) return;
+        const long long e = e_base + threadIdx.x;
+        if (e >= total) return;
+        const int row = (int)(e / a.lda), col = (int)(e % a.lda);
+        if (row >= a.rows || col >= a.cols) return;
+        uint32_t words[INV_MAXW];
+        const int nw = RL / 2;
+        for (int k = 0; k < nw; ++k)
+            words[k] = (uint32_t)ob[(2 * k) * E + threadIdx.x] |
+                       ((uint32_t)ob[(2 * k + 1) * E + threadIdx.x] << 16);
+        store_float(a, (long long)row * a.ldo + col, words, nw);
+        return;
+    }
+
     // ---- store the CTA's limbs, plane by plane
     uint16_t* out = reinterpret_cast<uint16_t*>(a.out);
     if (vec_out) {  // element e is output index e: 16-byte stores of 8 elements
@@ -593,8 +610,15 @@ template <int NB, int K>
 static int launch_lane(const InvArgs& a, cudaStream_t stream) {
     constexpr int E = (INVL_THREADS / 32) * (32 / K);
     constexpr int PMAX = (NB + 1) * (K / 2);
+    // fp outputs: the product's limbs plus 64 bits of sign extension, in whole
+    // 32-bit words (the register and generic kernels append the same margin)
+    int RL = a.RL;
+    if (a.out_kind == INV_F32 || a.out_kind == INV_F64) {
+        RL = ((a.positions * a.b + 15) / 16 + 4 + 1) / 2 * 2;
+        if (RL > 2 * INV_MAXW) return MFFTB_ERR_UNSUPPORTED;
+    }
     const size_t stage = (size_t)NB * K * (E + 1) * sizeof(int64_t);
-    const size_t carry = (size_t)E * PMAX * sizeof(int64_t) + (size_t)a.RL * E * sizeof(uint16_t);
+    const size_t carry = (size_t)E * PMAX * sizeof(int64_t) + (size_t)RL * E * sizeof(uint16_t);
     const size_t smem = (stage > carry ? stage : carry + 16);
     if (smem > 200 * 1024) return MFFTB_ERR_UNSUPPORTED;
     static int attr_dev = -1;
@@ -613,13 +637,14 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
                         a.out_plane % 8 == 0 && reinterpret_cast<uintptr_t>(a.out) % 16 == 0;
     const long long blocks = (total + E - 1) / E;
     if (blocks > 0)
-        inverse_lane_kernel<NB, K><<<(unsigned)blocks, INVL_THREADS, smem, stream>>>(a, seg, vec_out);
+        inverse_lane_kernel<NB, K><<<(unsigned)blocks, INVL_THREADS, smem, stream>>>(a, seg, vec_out,
+                                                                                 RL);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
 // MFFTB_ERR_UNSUPPORTED when the lane variant does not cover the plan
 static int try_lane(const InvArgs& a, cudaStream_t stream) {
-    if (a.out_kind != INV_U16) return MFFTB_ERR_UNSUPPORTED;
+    if (a.out_kind == INV_I64) return MFFTB_ERR_UNSUPPORTED;
     if (a.positions > (a.NB + 1) * a.S || a.b < 2 || a.b > 15) return MFFTB_ERR_UNSUPPORTED;
     if (a.lda % 4 || a.acc_plane % 4 || reinterpret_cast<uintptr_t>(a.acc) % 16)
         return MFFTB_ERR_UNSUPPORTED;
@@ -662,6 +687,9 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
         if (a.NB == 2 && a.K == 2) return launch_reg<2, 2>(a, stream);
         if (a.NB == 4 && a.K == 2) return launch_reg<4, 2>(a, stream);
         if (a.NB == 2 && a.K == 8) return launch_reg<2, 8>(a, stream);
+        if (a.NB == 4 && a.K == 16) return launch_reg<4, 16>(a, stream);
+        if (a.NB == 2 && a.K == 16) return launch_reg<2, 16>(a, stream);
+        if (a.NB == 2 && a.K == 32) return launch_reg<2, 32>(a, stream);
     }
     if (a.variant != 1) {
         const int rc = try_lane(a, stream);

@@ -80,3 +80,34 @@ def test_fp64_large_sampled(ctx, oracle):
     mag = (tA.abs() @ tB.abs()).cpu().numpy().ravel()
     err = np.abs(C - ref)
     assert (err <= 2.0 ** -53 * np.abs(ref) * (1 + 2.0 ** -20) + n * 2.0 ** -52 * mag).all()
+
+
+@pytest.mark.parametrize("dtype,fb,lo,hi", [
+    ("f64", 0, -20, 20), ("f64", 0, -45, 45), ("f64", 512, -8, 8), ("f64", 0, -90, 90),
+    ("f32", 0, -45, 45), ("f32", 0, -70, 70), ("f32", 512, -8, 8),
+])
+def test_float_outputs_all_inverse_kernels(ctx, oracle, dtype, fb, lo, hi):
+    """fp32 / fp64 outputs through the lane inverse (NB*K >= 64 plans) and the
+    generic kernel agree bit for bit with each other and with the oracle."""
+    rng = np.random.default_rng(1000 + 7 * abs(lo) + hi)
+    n = 72
+    A = rng.standard_normal(n * n) * np.exp2(rng.integers(lo, hi, n * n))
+    B = rng.standard_normal(n * n) * np.exp2(rng.integers(lo, hi, n * n))
+    rows = np.repeat(np.arange(n), n)
+    cols = np.tile(np.arange(n), n)
+    if dtype == "f32":
+        A, B = A.astype(np.float32), B.astype(np.float32)
+        run, want = ctx.fp32, oracle.fpx_entries(A, B, n, fb, rows, cols)
+        view = np.uint32
+    else:
+        run, want = ctx.fp64, oracle.fpx64_entries(A, B, n, fb, rows, cols)
+        view = np.uint64
+    got = run(A, B, n, fb)
+    plan = ctx.last_plan()
+    ctx.set_kernel_variant("inverse", 1)
+    try:
+        gen = run(A, B, n, fb)
+    finally:
+        ctx.set_kernel_variant("inverse", 0)
+    assert np.array_equal(got.view(view), gen.view(view)), plan
+    assert np.array_equal(got.view(view), want.view(view)), plan
