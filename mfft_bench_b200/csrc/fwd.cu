@@ -61,7 +61,9 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
     if (e0 >= a.nelem) return;
     const int mask2K = 2 * a.K - 1;  // 2K is a power of two
     const int nplanes_j = a.f_stack ? (2 * a.K - 1) : a.K;
-    for (int j = 0; j < a.NB; ++j) {
+    // small operands (few elements, many points) spread the points over
+    // gridDim.y so that every SM gets work
+    for (int j = blockIdx.y; j < a.NB; j += gridDim.y) {
         const int step = (a.g * j) & mask2K;
         for (int c = 0; c < a.K; ++c) {
             int x[4] = {0, 0, 0, 0};
@@ -173,9 +175,13 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
         if (a.NB == 8 && a.K == 4) return launch_simd<8, 4>(a, stream);
         if (a.NB == 4 && a.K == 8) return launch_simd<4, 8>(a, stream);
     }
-    if (a.dbytes == 1) forward_kernel<1><<<(unsigned)blocks, threads, 0, stream>>>(a);
-    else if (a.dbytes == 2) forward_kernel<2><<<(unsigned)blocks, threads, 0, stream>>>(a);
-    else forward_kernel<4><<<(unsigned)blocks, threads, 0, stream>>>(a);
+    long long jsplit = (4 * 148 + blocks - 1) / blocks;  // aim at >= 4 CTAs per SM
+    if (jsplit > a.NB) jsplit = a.NB;
+    if (jsplit < 1) jsplit = 1;
+    const dim3 grid((unsigned)blocks, (unsigned)jsplit);
+    if (a.dbytes == 1) forward_kernel<1><<<grid, threads, 0, stream>>>(a);
+    else if (a.dbytes == 2) forward_kernel<2><<<grid, threads, 0, stream>>>(a);
+    else forward_kernel<4><<<grid, threads, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
