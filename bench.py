@@ -435,37 +435,58 @@ def e2e_measure(ctx, wl, steps, torch):
 
 def e2e_measure_dist(wl, steps, torch, dist, device):
     """N GPUs: every rank copies its own row blocks of A and B from pinned
-    host memory, the step runs (B all-gather, rows of C, gather to rank 0)
-    and rank 0 reads the whole C back.  Time = max over ranks."""
+    host memory, B is all-gathered, the rank computes its rows of C and reads
+    them back into its own pinned host buffer over its own PCIe link (all N
+    links busy at once; C's rows are not funnelled through rank 0).  Also
+    reported: the same step with C gathered to rank 0 on the GPUs and read
+    back by rank 0 alone.  Time = max over ranks of the mean step."""
     n, P = wl.n, wl.planes
     rows = wl.rows
     Av = wl.A.view(P, n, n)
     hA = Av[:, wl.r0:wl.r1, :].contiguous().cpu().pin_memory()
     hB = wl.B_local.cpu().pin_memory()
+    hrows = torch.empty(max(1, wl.RL * rows * n), dtype=wl.out.dtype).pin_memory()
     hout = torch.empty(wl.RL * n * n, dtype=wl.out.dtype).pin_memory() if wl.rank == 0 else None
 
-    def run():
+    def upload():
         Av[:, wl.r0:wl.r1, :].copy_(hA.view(P, rows, n).to(device, non_blocking=True))
         wl.B_local.copy_(hB.to(device, non_blocking=True))
+
+    def run_local():
+        upload()
+        wl.gather_B()
+        wl._compute((wl.r0, wl.r1), wl.out)
+        hrows.copy_(wl.out[:hrows.numel()], non_blocking=True)
+        torch.cuda.synchronize()
+
+    def run_root():
+        upload()
         wl.step()
         if wl.rank == 0:
             hout.copy_(wl.full_out, non_blocking=True)
         torch.cuda.synchronize()
 
-    run()
-    ts = []
-    for _ in range(steps):
-        dist.barrier()
-        t0 = time.perf_counter()
-        run()
-        ts.append(time.perf_counter() - t0)
-    t = torch.tensor([statistics.mean(ts)], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(steps):
+            dist.barrier()
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        t = torch.tensor([statistics.mean(ts)], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    local, root = timed(run_local), timed(run_root)
     h2d = 2 * n * n * wl.bytes_in
     d2h = wl.RL * n * n * wl.out.element_size()
-    return {"value": float(t.item()), "unit": "s", "h2d_bytes_per_step": h2d,
+    return {"value": local, "unit": "s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": steps,
-            "note": "each rank uploads its row blocks; rank 0 downloads all of C"}
+            "note": ("each rank uploads its row blocks of A and B and reads back its own "
+                     "rows of C (plane-major [RL][rows][n]) over its own PCIe link; "
+                     "bytes are totals over all ranks"),
+            "value_gather_to_rank0": root}
 
 
 def main():

@@ -30,6 +30,10 @@ struct mfftgpu_ctx {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
+    cudaStream_t copy_stream = nullptr;  // device->host reads of the host-pointer entry points
+    cudaStream_t up_stream = nullptr;    // host->device uploads of the host-pointer entry points
+    cudaEvent_t chunk_ev[8] = {};
+    cudaEvent_t up_ev[9] = {};
     int* d_err = nullptr;    // device status word
     int* d_scan = nullptr;   // fp32 exponent scan results
     char* ws = nullptr;      // grow-only workspace
@@ -500,6 +504,15 @@ int mfftgpu_destroy(mfftgpu_ctx* C) {
     cudaFree(C->d_err);
     for (auto& e : C->ev)
         if (e) cudaEventDestroy(e);
+    for (cudaStream_t s : {C->copy_stream, C->up_stream})
+        if (s) {
+            cudaStreamSynchronize(s);
+            cudaStreamDestroy(s);
+        }
+    for (auto& e : C->chunk_ev)
+        if (e) cudaEventDestroy(e);
+    for (auto& e : C->up_ev)
+        if (e) cudaEventDestroy(e);
     if (C->own_stream && C->stream) cudaStreamDestroy(C->stream);
     delete C;
     return MFFTB_OK;
@@ -784,6 +797,83 @@ static int stage(mfftgpu_ctx* C, size_t inA, size_t inB, size_t outb, char** dA,
     return MFFTB_OK;
 }
 
+}  // extern "C"
+
+// Host-pointer products: B is uploaded first and A in row chunks on an
+// upload stream; the rows of C are computed chunk by chunk as their rows of
+// A arrive (B packed and transformed once, kept across chunks), and each
+// chunk's rows of every output plane are read back on a third stream while
+// the next chunk computes, so both copies hide behind the tensor-core work.
+// The operands are row-major planes: A and B have a_planes planes of
+// a_esize-byte elements ([planes][n][n]); compute(r0, r1, dst) writes rows
+// [r0, r1) of C as [planes][r1-r0][n] at dst; host out is [planes][n][n]
+// with elements of esize bytes.  whole_a: every chunk reads all of A (the
+// fp embeddings scan A's exponent range first), so chunk 0 waits for the
+// last upload.
+template <typename F>
+static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB, char* dA,
+                          char* dB, int a_planes, size_t a_esize, int planes, size_t esize,
+                          char* dO, void* out, bool whole_a, F compute) {
+    const int nchunks = n >= 4096 ? 4 : 1;
+    const size_t in = (size_t)a_planes * n * n * a_esize;
+    if (nchunks == 1) {
+        CUDA_OK(cudaMemcpyAsync(dA, hA, in, cudaMemcpyHostToDevice, C->stream));
+        CUDA_OK(cudaMemcpyAsync(dB, hB, in, cudaMemcpyHostToDevice, C->stream));
+    } else {
+        if (!C->copy_stream) {
+            CUDA_OK(cudaStreamCreateWithFlags(&C->copy_stream, cudaStreamNonBlocking));
+            CUDA_OK(cudaStreamCreateWithFlags(&C->up_stream, cudaStreamNonBlocking));
+            for (auto& e : C->chunk_ev) CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            for (auto& e : C->up_ev) CUDA_OK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        }
+        // earlier work on the context stream may still read the staging buffers
+        CUDA_OK(cudaEventRecord(C->up_ev[8], C->stream));
+        CUDA_OK(cudaStreamWaitEvent(C->up_stream, C->up_ev[8], 0));
+        CUDA_OK(cudaMemcpyAsync(dB, hB, in, cudaMemcpyHostToDevice, C->up_stream));
+        for (int c = 0; c < nchunks; ++c) {
+            const int r0 = (int)((long long)n * c / nchunks), r1 = (int)((long long)n * (c + 1) / nchunks);
+            const size_t w = (size_t)(r1 - r0) * n * a_esize, off = (size_t)r0 * n * a_esize;
+            CUDA_OK(cudaMemcpy2DAsync(dA + off, (size_t)n * n * a_esize,
+                                      static_cast<const char*>(hA) + off, (size_t)n * n * a_esize,
+                                      w, a_planes, cudaMemcpyHostToDevice, C->up_stream));
+            CUDA_OK(cudaEventRecord(C->up_ev[c], C->up_stream));
+        }
+    }
+    const bool keep = C->reuse_b;
+    int rc = MFFTB_OK;
+    C->b_valid = false;
+    for (int c = 0; c < nchunks && !rc; ++c) {
+        const int r0 = (int)((long long)n * c / nchunks), r1 = (int)((long long)n * (c + 1) / nchunks);
+        if (r1 <= r0) continue;
+        if (nchunks > 1)
+            CUDA_OK(cudaStreamWaitEvent(C->stream, C->up_ev[whole_a ? nchunks - 1 : c], 0));
+        char* dst = dO + (size_t)planes * r0 * n * esize;
+        C->reuse_b = c > 0;  // same B buffer for every chunk
+        rc = compute(r0, r1, dst);
+        if (rc) break;
+        const size_t w = (size_t)(r1 - r0) * n * esize;
+        if (nchunks == 1) {
+            CUDA_OK(cudaMemcpyAsync(out, dst, (size_t)planes * w, cudaMemcpyDeviceToHost, C->stream));
+            continue;
+        }
+        CUDA_OK(cudaEventRecord(C->chunk_ev[c], C->stream));
+        CUDA_OK(cudaStreamWaitEvent(C->copy_stream, C->chunk_ev[c], 0));
+        CUDA_OK(cudaMemcpy2DAsync(static_cast<char*>(out) + (size_t)r0 * n * esize,
+                                  (size_t)n * n * esize, dst, w, w, planes, cudaMemcpyDeviceToHost,
+                                  C->copy_stream));
+    }
+    C->reuse_b = keep;
+    C->b_valid = false;
+    if (nchunks > 1) {
+        cudaError_t e = cudaStreamSynchronize(C->copy_stream);
+        if (!rc && e != cudaSuccess) rc = set_err(C, MFFTB_ERR_CUDA, "%s", cudaGetErrorString(e));
+    }
+    int rs = mfftgpu_sync(C);
+    return rc ? rc : rs;
+}
+
+extern "C" {
+
 int mfftgpu_mm_u16(mfftgpu_ctx* C, const uint16_t* A, const uint16_t* B, int n, int L,
                    int is_signed, uint16_t* out, int RL) {
     if (!C || !A || !B || !out || n <= 0 || L <= 0 || RL <= 0) return MFFTB_ERR_ARG;
@@ -792,12 +882,10 @@ int mfftgpu_mm_u16(mfftgpu_ctx* C, const uint16_t* A, const uint16_t* B, int n, 
     char *dA, *dB, *dO;
     int rc = stage(C, in, in, ob, &dA, &dB, &dO);
     if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
-    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
-    rc = mfftgpu_mm_u16_dev(C, (uint16_t*)dA, (uint16_t*)dB, n, L, is_signed, (uint16_t*)dO, RL, 0, n);
-    if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(out, dO, ob, cudaMemcpyDeviceToHost, C->stream));
-    return mfftgpu_sync(C);
+    return rows_pipelined(C, n, A, B, dA, dB, L, 2, RL, 2, dO, out, false, [&](int r0, int r1, char* dst) {
+        return mfftgpu_mm_u16_dev(C, (uint16_t*)dA, (uint16_t*)dB, n, L, is_signed,
+                                  (uint16_t*)dst, RL, r0, r1);
+    });
 }
 
 int mfftgpu_mm_i64(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n, uint16_t* out,
@@ -808,12 +896,9 @@ int mfftgpu_mm_i64(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n, ui
     char *dA, *dB, *dO;
     int rc = stage(C, in, in, ob, &dA, &dB, &dO);
     if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
-    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
-    rc = mfftgpu_mm_i64_dev(C, (int64_t*)dA, (int64_t*)dB, n, (uint16_t*)dO, RL, 0, n);
-    if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(out, dO, ob, cudaMemcpyDeviceToHost, C->stream));
-    return mfftgpu_sync(C);
+    return rows_pipelined(C, n, A, B, dA, dB, 1, 8, RL, 2, dO, out, false, [&](int r0, int r1, char* dst) {
+        return mfftgpu_mm_i64_dev(C, (int64_t*)dA, (int64_t*)dB, n, (uint16_t*)dst, RL, r0, r1);
+    });
 }
 
 int mfftgpu_conv_i32(mfftgpu_ctx* C, const int32_t* A32, const int32_t* B32, int n, int L,
@@ -840,12 +925,9 @@ int mfftgpu_fp64(mfftgpu_ctx* C, const double* A, const double* B, int n, int fo
     char *dA, *dB, *dO;
     int rc = stage(C, in, in, in, &dA, &dB, &dO);
     if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
-    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
-    rc = mfftgpu_fp64_dev(C, (double*)dA, (double*)dB, n, force_bits, (double*)dO, 0, n);
-    if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(Cout, dO, in, cudaMemcpyDeviceToHost, C->stream));
-    return mfftgpu_sync(C);
+    return rows_pipelined(C, n, A, B, dA, dB, 1, 8, 1, 8, dO, Cout, true, [&](int r0, int r1, char* dst) {
+        return mfftgpu_fp64_dev(C, (double*)dA, (double*)dB, n, force_bits, (double*)dst, r0, r1);
+    });
 }
 
 int mfftgpu_fp32(mfftgpu_ctx* C, const float* A, const float* B, int n, int force_bits,
@@ -856,12 +938,9 @@ int mfftgpu_fp32(mfftgpu_ctx* C, const float* A, const float* B, int n, int forc
     char *dA, *dB, *dO;
     int rc = stage(C, in, in, in, &dA, &dB, &dO);
     if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(dA, A, in, cudaMemcpyHostToDevice, C->stream));
-    CUDA_OK(cudaMemcpyAsync(dB, B, in, cudaMemcpyHostToDevice, C->stream));
-    rc = mfftgpu_fp32_dev(C, (float*)dA, (float*)dB, n, force_bits, (float*)dO, 0, n);
-    if (rc) return rc;
-    CUDA_OK(cudaMemcpyAsync(Cout, dO, in, cudaMemcpyDeviceToHost, C->stream));
-    return mfftgpu_sync(C);
+    return rows_pipelined(C, n, A, B, dA, dB, 1, 4, 1, 4, dO, Cout, true, [&](int r0, int r1, char* dst) {
+        return mfftgpu_fp32_dev(C, (float*)dA, (float*)dB, n, force_bits, (float*)dst, r0, r1);
+    });
 }
 
 // --------------------------------------------------------------------- generators

@@ -245,3 +245,29 @@ def test_device_generators_match_host(ctx):
     ctx.sync()
     assert np.array_equal(dm.view(torch.int16).cpu().numpy().view(np.uint16),
                           m.bigmat_rand(n, L, 12345))
+
+
+def test_host_entry_points_chunked_readback(ctx):
+    """n >= 4096: the host-pointer calls compute C in row chunks and read each
+    chunk back while the next computes; the result equals the one-shot
+    device-pointer product."""
+    import torch
+    n = 4096
+    dA = torch.empty(n * n, dtype=torch.int64, device="cuda")
+    dB = torch.empty_like(dA)
+    ctx.gen_int64(dA, 101)
+    ctx.gen_int64(dB, 202)
+    want = ctx.mm_i64(dA, dB, n, RL=9)
+    ctx.sync()
+    got = ctx.mm_i64(dA.cpu().numpy(), dB.cpu().numpy(), n, RL=9)
+    assert np.array_equal(got, want.view(torch.int16).cpu().numpy().view(np.uint16))
+    L = 3
+    uA = torch.empty(L * n * n, dtype=torch.uint16, device="cuda")
+    uB = torch.empty_like(uA)
+    ctx.gen_bigmat(uA, n, L, 7)
+    ctx.gen_bigmat(uB, n, L, 8)
+    want = ctx.mm_u16(uA, uB, n, L, signed=True, RL=5)
+    ctx.sync()
+    h = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
+    got = ctx.mm_u16(h(uA), h(uB), n, L, signed=True, RL=5)
+    assert np.array_equal(got, h(want))
