@@ -585,27 +585,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             if (p.jobs.school) {
                 int ulo;
                 const int npairs_u = pw3_school_pairs(p.jobs, t0, w, ulo);
+                int rlo[PW3_TG], rhi[PW3_TG];
+#pragma unroll
+                for (int tt = 0; tt < PW3_TG; ++tt) pw_school_range(p.jobs, t0 + tt, w, rlo[tt], rhi[tt]);
                 for (int cp = 0; cp < npairs_u; ++cp) {
                     const int c = ulo + 2 * cp;
+                    // only the planes some valid (t, u) slot of this stage reads are
+                    // loaded (the MMA thread applies the same validity test)
+                    uint32_t needA = 0, needF = 0;
+#pragma unroll
+                    for (int cc = 0; cc < PW3_CPS; ++cc)
+#pragma unroll
+                        for (int tt = 0; tt < PW3_TG; ++tt)
+                            if (c + cc >= rlo[tt] && c + cc <= rhi[tt]) {
+                                needA |= 1u << cc;
+                                needF |= 1u << (PW3_TG - 1 - tt + cc);
+                            }
+                    const uint32_t stage_tx =
+                        2u * ((uint32_t)__popc(needA) * PW3_A_BYTES + (uint32_t)__popc(needF) * PW3_F_BYTES);
                     for (int kb = 0; kb < p.kblocks; ++kb) {
                         if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
                                                global_timer_ns() + tmo))
                             goto producer_done;
                         const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
-                        if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                        if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
                         uint8_t* st = smem + stage * PW3_STAGE_BYTES;
                         // A planes c, c+1; B planes t0+3-c-f in slot f (out-of-range
                         // plane coordinates load zeros)
 #pragma unroll
                         for (int cc = 0; cc < PW3_CPS; ++cc)
-                            tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
-                                             kb * PW_BK, mt * 256 + (int)rank * 128, c + cc);
+                            if (needA & (1u << cc))
+                                tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
+                                                 kb * PW_BK, mt * 256 + (int)rank * 128, c + cc);
 #pragma unroll
                         for (int f = 0; f < PW3_NF; ++f)
-                            tma_load_3d_pair(
-                                smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
-                                full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
-                                t0 + PW3_TG - 1 - c - f);
+                            if (needF & (1u << f))
+                                tma_load_3d_pair(
+                                    smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
+                                    full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
+                                    t0 + PW3_TG - 1 - c - f);
                         issued_parity[stage] = (int)phase;
                         if (++stage == PW3_STAGES) {
                             stage = 0;
