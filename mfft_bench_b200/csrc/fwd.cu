@@ -117,16 +117,18 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
 // Single-digit plans (every transformed coefficient fits int8, so every
 // partial sum does too) with int8 digit planes: 4 elements per thread as
 // packed bytes, byte-wise SIMD adds, all twiddle indices resolved at compile
-// time.  Same outputs as forward_kernel.
-template <int NB, int K>
+// time.  Same outputs as forward_kernel.  NBLK: blocks that may be non-zero
+// (NB, or NB/2 when nc <= NB/2, which NB = next_pow2(ncA + ncB) gives for
+// operands of equal width -- half the digit registers).
+template <int NB, int K, int NBLK = NB>
 __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
     constexpr int S = K / 2, G = 2 * K / NB, TWO_K = 2 * K;
     const long long e0 = 4 * (blockIdx.x * 256LL + threadIdx.x);
     if (e0 >= a.nelem) return;
     const int8_t* D = reinterpret_cast<const int8_t*>(a.D);
-    uint32_t dg[NB * S];
+    uint32_t dg[NBLK * S];
 #pragma unroll
-    for (int m = 0; m < NB * S; ++m)
+    for (int m = 0; m < NBLK * S; ++m)
         dg[m] = (m < a.Lb && m / S < a.nc)
                     ? __ldg(reinterpret_cast<const uint32_t*>(D + (long long)m * a.dplane + e0))
                     : 0u;
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
         for (int c = 0; c < K; ++c) {
             uint32_t x = 0;
 #pragma unroll
-            for (int beta = 0; beta < NB; ++beta) {
+            for (int beta = 0; beta < NBLK; ++beta) {
                 const int e = (G * j * beta) % TWO_K;
                 int r = ((c - e) % TWO_K + TWO_K) % TWO_K;
                 const bool neg = r >= K;
@@ -159,7 +161,16 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
 template <int NB, int K>
 static int launch_simd(const FwdArgs& a, cudaStream_t stream) {
     long long blocks = (a.nelem / 4 + 255) / 256;
-    if (blocks > 0) forward_simd_kernel<NB, K><<<(unsigned)blocks, 256, 0, stream>>>(a);
+    if (blocks <= 0) return MFFTB_OK;
+    if (a.nc <= NB / 2) {
+        forward_simd_kernel<NB, K, NB / 2><<<(unsigned)blocks, 256, 0, stream>>>(a);
+    } else {
+        // all NB blocks in registers only while they fit (NB*S <= 64 words)
+        if constexpr (NB * K / 2 <= 64)
+            forward_simd_kernel<NB, K><<<(unsigned)blocks, 256, 0, stream>>>(a);
+        else
+            return MFFTB_ERR_UNSUPPORTED;
+    }
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
@@ -170,10 +181,15 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     if (blocks <= 0) return MFFTB_OK;
     if ((1 << a.lgS) != a.S || (1 << a.lgK) != a.K) return MFFTB_ERR_ARG;
     if (a.d == 1 && a.dbytes == 1 && 2 * a.S == a.K) {
-        if (a.NB == 8 && a.K == 8) return launch_simd<8, 8>(a, stream);
-        if (a.NB == 4 && a.K == 4) return launch_simd<4, 4>(a, stream);
-        if (a.NB == 8 && a.K == 4) return launch_simd<8, 4>(a, stream);
-        if (a.NB == 4 && a.K == 8) return launch_simd<4, 8>(a, stream);
+        int rc = MFFTB_ERR_UNSUPPORTED;
+        if (a.NB == 8 && a.K == 8) rc = launch_simd<8, 8>(a, stream);
+        else if (a.NB == 4 && a.K == 4) rc = launch_simd<4, 4>(a, stream);
+        else if (a.NB == 8 && a.K == 4) rc = launch_simd<8, 4>(a, stream);
+        else if (a.NB == 4 && a.K == 8) rc = launch_simd<4, 8>(a, stream);
+        else if (a.NB == 16 && a.K == 16) rc = launch_simd<16, 16>(a, stream);
+        else if (a.NB == 16 && a.K == 8) rc = launch_simd<16, 8>(a, stream);
+        else if (a.NB == 8 && a.K == 16) rc = launch_simd<8, 16>(a, stream);
+        if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
     }
     long long jsplit = (4 * 148 + blocks - 1) / blocks;  // aim at >= 4 CTAs per SM
     if (jsplit > a.NB) jsplit = a.NB;
