@@ -5,12 +5,12 @@
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
     python bench.py --impl reference ...                      (reference CPU arm)
 
-Metric: "s per exact n x n W-bit matmul; effective int8 TOPS
-vs tcgen05 int8 peak".  One step = one exact product of the workload's two
-matrices (inputs resident in HBM, device-timed with CUDA events on the
-launching stream, max over ranks).  The default workload is BASELINE
-configs[4] (n=16384, W=64 signed, the north star's target configuration); the
-others are selectable with --workload c1..c5 (configs[0..4]).
+Metric: "s per exact n x n W-bit matmul; effective int8 TOPS vs tcgen05 int8
+peak".  One step = one exact product of the workload's two matrices (inputs
+resident in HBM, device-timed with CUDA events on the launching stream, max
+over ranks).  The default workload is c5 (n=16384, W=64 signed, the headline
+configuration); the other benchmark configurations are selectable with
+--workload c1..c4, plus f64 (the fp64 embedding on c4's shape).
 
 Also reported on the same JSON line: the live roofline of the dominant kernel
 (the tcgen05 pointwise contraction), an end-to-end number through the C ABI
@@ -45,7 +45,8 @@ WORKLOADS = {
                desc="configs[3]: n=8192 fp32 N(0,1)*2^k on the 512-bit grid"),
     "c5": dict(n=16384, kind="i64", signed=True,
                desc="configs[4]: n=16384, W=64 signed int64"),
-    # not a BASELINE config: the fp64 embedding (fpx_*_d) on c4's shape
+    # not one of the benchmark configurations c1-c5: the fp64 embedding
+    # (fpx_*_d) on c4's shape
     "f64": dict(n=8192, kind="f64", force_bits=512,
                 desc="fp64 N(0,1)*2^k (k in [-8, 8]) on the 512-bit grid, n=8192"),
 }

@@ -1,4 +1,4 @@
-"""Parity at the BASELINE configurations' full sizes (bit-exact).
+"""Parity at the full sizes of the benchmark configurations c2-c5 (bit-exact).
 
 Full CPU runs of the reference are infeasible beyond n = 1024 (hours), so
 full-size parity uses size-independent properties and sampled entries:
@@ -100,7 +100,7 @@ def test_c4_fp32_512bit_grid(ctx, oracle):
 
 
 def test_c5_signed_64bit(ctx, oracle):
-    """n=16384, W=64 signed (the north star configuration)."""
+    """c5: n=16384, W=64 signed (the headline configuration)."""
     import torch
     n = 16384
     dA = torch.empty(n * n, dtype=torch.int64, device="cuda")

@@ -2,7 +2,7 @@
 mm_limbplane / conv_limbplane and limb-*-exact comparator rows) on the same
 tcgen05 kernel: its job table against a CUDA-core evaluation, its products
 against the oracle and the reference's fixtures, and bit-identity with the
-MFFT path at the BASELINE configurations' full sizes.
+MFFT path at the full sizes of the benchmark configurations c3-c5.
 """
 import numpy as np
 import pytest

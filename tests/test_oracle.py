@@ -26,7 +26,7 @@ def test_unsigned_fixture(oracle, golden, n, L):
 
 
 def test_c1_digest(oracle, golden):
-    """BASELINE config 1 (n=64, W=8192): the oracle's restated MFFT reproduces
+    """Benchmark configuration c1 (n=64, W=8192): the oracle's restated MFFT reproduces
     the digest of the reference's own mm_mfft output."""
     n, L = 64, 512
     out = oracle.mm_mfft(oracle.bigmat_rand(n, L, SA), oracle.bigmat_rand(n, L, SB), n, L)
