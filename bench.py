@@ -504,11 +504,15 @@ def main():
     ap.add_argument("--subblocks", type=int, default=1,
                     help="row sub-blocks per rank whose gathers overlap the next block's compute")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sample-n", type=int, default=0,
+                    help="matrix size of the reference CPU samples (default: per workload)")
     ap.add_argument("--method", default="mfft", choices=["mfft", "schoolbook"],
                     help="mfft: the MFFT hot path (the headline); schoolbook: the limb-plane "
                          "comparator on the same tensor-core kernel")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.sample_n > 0:
+        CPU_SAMPLE_N[args.workload] = args.sample_n
     global SUBBLOCKS
     SUBBLOCKS = max(1, args.subblocks)
     if args.n > 0:
