@@ -1,12 +1,18 @@
-// pointwise.cu -- persistent, warp-specialised tcgen05 (kind::i8) kernel for
-// the MFFT pointwise step; see pointwise.cuh for the job semantics.
+// pointwise.cu -- persistent, warp-specialised tcgen05 (kind::i8) kernels for
+// the plane products (MFFT pointwise step and schoolbook digit-plane
+// products); see pointwise.cuh for the job semantics.
 //
-// One CTA per SM.  Warp 0 streams K-major int8 tiles of Ahat and F into a
-// 4-stage shared-memory ring with TMA (128-byte swizzle, no multicast).  One
-// thread of warp 1 issues tcgen05.mma (M=128, N=block_n, K=32 per
-// instruction) into one of two 256-column int32 TMEM accumulators.  Warps 2-5
-// drain the other accumulator (tcgen05.ld) and store int32 rows to HBM while
-// the next tile accumulates.
+// All three kernels: warp 0 streams K-major int8 tiles into a shared-memory
+// ring with TMA (128-byte swizzle, no multicast), one thread of warp 1 issues
+// tcgen05.mma (K = 32 per instruction) into int32 TMEM accumulators, warps
+// 2-5 drain them (tcgen05.ld) and store int32 job planes; every wait is
+// bounded.  pointwise_launch picks:
+//   * pointwise_i8_kernel: one CTA per SM, M = 128, N = block_n, two
+//     256-column accumulators (the epilogue overlaps the next tile) -- small n;
+//   * pointwise2_i8_kernel: CTA pairs (cta_group::2), 256 x 256 tiles;
+//   * pointwise3_i8_kernel: CTA pairs, 256 x 128 tiles of 4 jobs that share
+//     their A planes and overlapping F windows, wave-aligned tile order -- the
+//     default for one-chunk MFFT plans and the only one for schoolbook plans.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
