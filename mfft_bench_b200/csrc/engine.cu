@@ -6,7 +6,10 @@
 // fold + carry straight into the caller's output rows.  Row blocks bound the
 // device workspace (the reference mallocs NB*K full planes per call,
 // src/mfft.c:310-316; here only F is kept whole) and are also the unit of
-// multi-GPU sharding: a rank computes rows [row_begin, row_end).
+// multi-GPU sharding: a rank computes rows [row_begin, row_end).  Schoolbook
+// plans skip both transforms (the digit planes are the tensor-core operands)
+// and finish with the streaming carry.  The host-pointer entry points
+// overlap their uploads and read-backs with the compute of row chunks.
 #include <cuda_runtime.h>
 
 #include <algorithm>

@@ -10,10 +10,13 @@
 //     Xhat_j[c] = sum_beta  s * X[beta*S + c'],   c' = (c - g j beta) mod 2K
 //                                                 (s = -1 when c' lands in [K, 2K))
 //
-// The kernel evaluates these sums directly for 4 consecutive elements per
-// thread (the digit planes of a CTA's 1024 elements stay in L1) and writes
-// each value as d signed int8 digits.  For B it writes the F stack the
-// pointwise kernel expects: F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
+// Both kernels evaluate these sums directly for 4 consecutive elements per
+// thread and write each value as d signed int8 digits; forward_simd_kernel
+// (one-digit plans, int8 digit planes) keeps the digits in registers as
+// packed bytes with compile-time twiddles, forward_kernel (the rest) reads
+// them through L1 and spreads the evaluation points over gridDim.y when the
+// operand is small.  For B they write the F stack the pointwise kernel
+// expects: F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
 #include <cuda_runtime.h>
 
 #include <cstdint>

@@ -13,9 +13,12 @@
 //   * INV_F32 / INV_F64: extract + round_to + ldexpf / ldexp of
 //     fpx_decode_f32 / fpx_decode_f64 (src/fpfixed.c:212-322), see decode.cuh.
 //
-// A CTA owns E consecutive elements (E <= 32) and keeps their NB*K int64
-// transformed values in shared memory; 256 threads cooperate on the loads
-// and on the inverse DFT, then E threads fold and carry one element each.
+// Kernels: inverse_kernel (below; any plan) -- a CTA owns E consecutive
+// elements (E <= 32) and keeps their NB*K int64 transformed values in shared
+// memory; 256 threads cooperate on the loads and on the inverse DFT, then E
+// threads fold and carry one element each.  inverse_reg_kernel (NB*K <= 64)
+// and inverse_lane_kernel (K in {8,16,32}, NB <= 32) are the fast paths for
+// the common plans; school_carry*_kernel finish schoolbook plans.
 #include <cuda_runtime.h>
 
 #include <cstdint>
