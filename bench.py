@@ -66,6 +66,7 @@ def normal_f64(n, seed):
 
 METRIC = "s per exact n x n W-bit matmul; effective int8 TOPS vs tcgen05 int8 peak"
 SUBBLOCKS = 1
+C_GATHER = "peer"
 
 
 # ---------------------------------------------------------------------------- helpers
@@ -313,8 +314,17 @@ class Workload:
             if world > 1 else None
         odt = {"f32": torch.float32, "f64": torch.float64}.get(w["kind"], torch.uint16)
         self.out = torch.empty(max(1, self.RL * self.rows * n), dtype=odt, device=dev)
-        self.full_out = self.out if world == 1 else (
-            torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
+        # C's rows reach rank 0 either through a CUDA IPC mapping of its
+        # output buffer, written by every rank's final kernel (the default:
+        # compute and gather in one step), or by NCCL point-to-point transfers
+        self.peer = None
+        if world > 1 and C_GATHER == "peer" and SUBBLOCKS == 1:
+            self.peer = D.PeerOutput(self.RL * n * n, str(odt).replace("torch.", ""))
+            self.full_out = self.peer.tensor
+            self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        else:
+            self.full_out = self.out if world == 1 else (
+                torch.empty(self.RL * n * n, dtype=odt, device=dev) if rank == 0 else None)
         # optionally (--subblocks > 1) a rank computes its rows in sub-blocks
         # and ships each one to rank 0 while the next computes (B is transformed
         # once per step).  Off by default: NCCL's copy kernels then share the
@@ -350,6 +360,17 @@ class Workload:
             self._compute((self.r0, self.r1), self.out)
             return
         self.gather_B()
+        if self.peer is not None:
+            # this rank's rows of every plane straight into rank 0's buffer
+            ctx.set_reuse_b(False)
+            self._compute((self.r0, self.r1), self.peer.ptr + self.r0 * n * self.out.element_size(),
+                          plane_stride=n * n)
+            # the stores are complete once this rank's stream is; rank 0's
+            # stream continues only after every rank's all-reduce, i.e. after
+            # every rank's final kernel
+            self.torch.cuda.current_stream().synchronize()
+            self.torch.distributed.all_reduce(self.flag)
+            return
         works = []
         for si in range(self.nsub):
             a, b = self.subs[self.rank][si]
@@ -361,8 +382,9 @@ class Workload:
         for wk in works:
             wk.wait()
 
-    def _compute(self, rows, out):
+    def _compute(self, rows, out, plane_stride=0):
         w, ctx, n = self.w, self.ctx, self.n
+        ctx.set_output_plane_stride(plane_stride)
         if w["kind"] == "i64":
             ctx.mm_i64(self.A, self.B, n, RL=self.RL, out=out, rows=rows)
         elif w["kind"] == "u16":
@@ -504,6 +526,10 @@ def main():
     ap.add_argument("--subblocks", type=int, default=1,
                     help="row sub-blocks per rank whose gathers overlap the next block's compute")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--c-gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: C's rows reach rank 0 through stores of every rank's final "
+                         "kernel into an IPC mapping of rank 0's buffer (peer) or through NCCL "
+                         "point-to-point transfers after the compute (nccl)")
     ap.add_argument("--sample-n", type=int, default=0,
                     help="matrix size of the reference CPU samples (default: per workload)")
     ap.add_argument("--method", default="mfft", choices=["mfft", "schoolbook"],
@@ -513,8 +539,9 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.sample_n > 0:
         CPU_SAMPLE_N[args.workload] = args.sample_n
-    global SUBBLOCKS
+    global SUBBLOCKS, C_GATHER
     SUBBLOCKS = max(1, args.subblocks)
+    C_GATHER = args.c_gather
     if args.n > 0:
         WORKLOADS[args.workload] = dict(WORKLOADS[args.workload], n=args.n)
 
@@ -593,7 +620,10 @@ def main():
             "data": ("synthetic (seeded numpy PCG64 N(0,1)*2^k)" if w["kind"] == "f64" else
                      "synthetic (seeded splitmix64, reference generators)"),
             "config": {"workload": args.workload, "desc": w["desc"], "n": n, "method": args.method,
-                       "parallelism": f"row-blocks x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"row-blocks x{world}, C rows to rank 0 by "
+                                       + ("stores of the final kernel into a peer mapping"
+                                          if wl.peer is not None else "NCCL point-to-point"))
+                                      if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (no flush needed)"},
             "gpu_launches": (launches_per_step or 0) * args.steps,
             "clocks": clk}
@@ -647,6 +677,8 @@ def main():
                                     "sample": f"unavailable: {e}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if wl.peer is not None:
+        wl.peer.close()
     ctx.close()
     if world > 1:
         dist.barrier()

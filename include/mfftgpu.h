@@ -81,6 +81,24 @@ int mfftgpu_set_reuse_b(mfftgpu_ctx *ctx, int on);
  * bit-identical either way. */
 int mfftgpu_set_method(mfftgpu_ctx *ctx, int method);
 int mfftgpu_get_method(mfftgpu_ctx *ctx);
+/* Layout of the integer outputs of the _dev entry points: 0 (default) writes
+ * the computed rows compactly, [RL][row_end-row_begin][n]; a non-zero stride
+ * puts plane w of those rows at out + w * stride (e.g. stride n*n with out at
+ * row row_begin of a full [RL][n][n] array -- possibly another GPU's memory
+ * mapped with mfftgpu_ipc_open, so the final kernel of a sharded product
+ * stores its rows straight into the rank that assembles C).  The host-pointer
+ * entry points are not affected. */
+int mfftgpu_set_output_plane_stride(mfftgpu_ctx *ctx, long long elems);
+
+/* Device buffers shared between the processes of one node (CUDA IPC):
+ * mfftgpu_ipc_alloc allocates `bytes` on the current device and writes its
+ * 64-byte handle; another process maps it with mfftgpu_ipc_open (peer access
+ * over NVLink) and unmaps it with mfftgpu_ipc_close; the owner frees it with
+ * mfftgpu_ipc_free after every mapping is closed. */
+int mfftgpu_ipc_alloc(size_t bytes, void **ptr, void *handle);
+int mfftgpu_ipc_open(const void *handle, void **ptr);
+int mfftgpu_ipc_close(void *ptr);
+int mfftgpu_ipc_free(void *ptr);
 /* Kernel choice per stage, for comparisons; results are identical.
  * stage 2 (plane products): 0 auto, 1 one CTA per tile, 2 CTA pairs,
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);

@@ -70,6 +70,11 @@ _sig("mfftgpu_sync", i32, vp)
 _sig("mfftgpu_set_reuse_b", i32, vp, i32)
 _sig("mfftgpu_set_kernel_variant", i32, vp, i32, i32)
 _sig("mfftgpu_set_method", i32, vp, i32)
+_sig("mfftgpu_set_output_plane_stride", i32, vp, C.c_longlong)
+_sig("mfftgpu_ipc_alloc", i32, C.c_size_t, C.POINTER(C.c_void_p), vp)
+_sig("mfftgpu_ipc_open", i32, vp, C.POINTER(C.c_void_p))
+_sig("mfftgpu_ipc_close", i32, vp)
+_sig("mfftgpu_ipc_free", i32, vp)
 _sig("mfftgpu_get_method", i32, vp)
 _sig("mfftgpu_last_error", C.c_char_p, vp)
 _sig("mfftgpu_status_string", C.c_char_p, i32)

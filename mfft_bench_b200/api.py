@@ -30,6 +30,8 @@ class MfftError(RuntimeError):
 
 
 def _ptr(x):
+    if isinstance(x, int):  # a raw device address (e.g. a peer mapping)
+        return C.c_void_p(x)
     if isinstance(x, np.ndarray):
         if not x.flags["C_CONTIGUOUS"]:
             raise ValueError("arrays must be C-contiguous")
@@ -111,6 +113,12 @@ class Context:
         same tensor-core kernel) for value-mode products; identical results."""
         mid = {"mfft": 0, "schoolbook": 1}[method]
         self._check(lib.mfftgpu_set_method(self._h, mid), "set_method")
+
+    def set_output_plane_stride(self, elems):
+        """Integer outputs of the device-pointer calls: plane w of the computed
+        rows at out + w * elems (0: compact [RL][rows][n])."""
+        self._check(lib.mfftgpu_set_output_plane_stride(self._h, int(elems)),
+                    "set_output_plane_stride")
 
     def set_kernel_variant(self, stage, variant):
         """Pick the kernel of a stage ('pointwise' or 'inverse'; 0 = auto).

@@ -60,6 +60,7 @@ struct mfftgpu_ctx {
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
     int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
+    long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
     bool b_valid = false;
@@ -381,6 +382,12 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     return MFFTB_OK;
 }
 
+// plane stride of a _dev integer output: compact [RL][rows][n] unless the
+// caller asked for another layout (e.g. its rows of a full [RL][n][n] array)
+long long out_plane(const mfftgpu_ctx* C, int n, int row_begin, int row_end) {
+    return C->out_plane_stride ? C->out_plane_stride : (long long)(row_end - row_begin) * n;
+}
+
 int check_rows(int n, int row_begin, int row_end) {
     return (row_begin < 0 || row_end > n || row_begin > row_end) ? MFFTB_ERR_ARG : MFFTB_OK;
 }
@@ -556,6 +563,44 @@ int mfftgpu_set_method(mfftgpu_ctx* C, int method) {
 
 int mfftgpu_get_method(mfftgpu_ctx* C) { return C ? C->method : -1; }
 
+int mfftgpu_set_output_plane_stride(mfftgpu_ctx* C, long long elems) {
+    if (!C || elems < 0) return MFFTB_ERR_ARG;
+    C->out_plane_stride = elems;
+    return MFFTB_OK;
+}
+
+// --------------------------------------------------------------------- peer buffers (CUDA IPC)
+int mfftgpu_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+    if (!ptr || !handle || bytes == 0) return MFFTB_ERR_ARG;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return MFFTB_ERR_NOMEM;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return MFFTB_ERR_CUDA;
+    }
+    std::memcpy(handle, &h, sizeof h);
+    *ptr = p;
+    return MFFTB_OK;
+}
+
+int mfftgpu_ipc_open(const void* handle, void** ptr) {
+    if (!ptr || !handle) return MFFTB_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess
+               ? MFFTB_OK
+               : MFFTB_ERR_CUDA;
+}
+
+int mfftgpu_ipc_close(void* ptr) {
+    return ptr && cudaIpcCloseMemHandle(ptr) == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+int mfftgpu_ipc_free(void* ptr) {
+    return ptr && cudaFree(ptr) == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
 int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
     if (!C) return MFFTB_ERR_ARG;
     if (stage == 2 && variant >= 0 && variant <= 3) {
@@ -676,7 +721,7 @@ int mfftgpu_mm_u16_dev(mfftgpu_ctx* C, const uint16_t* A, const uint16_t* B, int
     Operand a{PACK_U16PL, A, n, L, 16 * L, is_signed ? 1 : 0, 0, 0, 0};
     Operand b = a;
     b.p = B;
-    OutSpec o{INV_U16, out, (long long)(row_end - row_begin) * n, n, RL, 0, 0, 2};
+    OutSpec o{INV_U16, out, out_plane(C, n, row_begin, row_end), n, RL, 0, 0, 2};
     return run_product(C, P, a, b, row_begin, row_end, o);
 }
 
@@ -691,7 +736,7 @@ int mfftgpu_mm_i64_dev(mfftgpu_ctx* C, const int64_t* A, const int64_t* B, int n
     Operand a{PACK_I64, A, n, 4, 64, 1, 0, 0, 0};
     Operand b = a;
     b.p = B;
-    OutSpec o{INV_U16, out, (long long)(row_end - row_begin) * n, n, RL, 0, 0, 2};
+    OutSpec o{INV_U16, out, out_plane(C, n, row_begin, row_end), n, RL, 0, 0, 2};
     return run_product(C, P, a, b, row_begin, row_end, o);
 }
 
@@ -843,6 +888,8 @@ static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB,
         }
     }
     const bool keep = C->reuse_b;
+    const long long keep_stride = C->out_plane_stride;
+    C->out_plane_stride = 0;  // the chunks below are compact
     int rc = MFFTB_OK;
     C->b_valid = false;
     for (int c = 0; c < nchunks && !rc; ++c) {
@@ -866,6 +913,7 @@ static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB,
                                   C->copy_stream));
     }
     C->reuse_b = keep;
+    C->out_plane_stride = keep_stride;
     C->b_valid = false;
     if (nchunks > 1) {
         cudaError_t e = cudaStreamSynchronize(C->copy_stream);

@@ -8,9 +8,10 @@ rows [r0, r1) of A and C.  The exchange steps are the only collectives:
    takes anywhere on the path -- its int8 digit planes are 16 B/entry and the
    transformed F stack 120 B/entry), then every rank packs and transforms B
    locally;
-2. C's row blocks are gathered to rank 0 plane by plane with grouped
-   point-to-point transfers, straight into the plane-major [RL][n][n]
-   layout of the reference (no gather primitive, no re-layout pass).
+2. C's rows reach rank 0 in the plane-major [RL][n][n] layout of the
+   reference: by default each rank's final kernel stores them straight into
+   rank 0's buffer through a CUDA IPC mapping (PeerOutput); or with grouped
+   point-to-point NCCL transfers plane by plane (gather_planes_to_root).
 
 The helpers work on any torch.distributed backend (NCCL on GPUs, gloo on
 CPU tensors in the tests).
@@ -92,6 +93,71 @@ def gather_planes_to_root(local, full, n: int, RL: int, ranges, group=None, root
         for req in dist.batch_isend_irecv(ops):
             req.wait()
     return full
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ of a raw device buffer (for torch.as_tensor)."""
+
+    def __init__(self, ptr, count, typestr):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3}
+
+
+class PeerOutput:
+    """A device buffer owned by rank `root` and mapped into every other rank
+    of the node with CUDA IPC.  Each rank's final kernel (inverse + carry)
+    stores its rows of C straight into it over NVLink -- the compute and the
+    gather of C are one step, with no separate collective.  `ptr` is this
+    rank's device address of the buffer; on the root, `tensor` views it.
+    close() is collective: mappings are closed before the root frees."""
+
+    _TYPESTR = {"uint16": "<u2", "float32": "<f4", "float64": "<f8"}
+
+    def __init__(self, count: int, dtype: str, group=None, root: int = 0):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from ._lib import lib
+        self.group, self.root = group, root
+        self.rank = dist.get_rank(group)
+        esize = {"uint16": 2, "float32": 4, "float64": 8}[dtype]
+        ptr = C.c_void_p()
+        handle = (C.c_char * 64)()
+        payload = [None]
+        if self.rank == root:
+            rc = lib.mfftgpu_ipc_alloc(count * esize, C.byref(ptr), handle)
+            if rc:
+                raise RuntimeError(f"mfftgpu_ipc_alloc failed ({rc})")
+            payload = [bytes(handle)]
+        dist.broadcast_object_list(payload, src=root, group=group)
+        if self.rank != root:
+            buf = (C.c_char * 64).from_buffer_copy(payload[0])
+            rc = lib.mfftgpu_ipc_open(buf, C.byref(ptr))
+            if rc:
+                raise RuntimeError(f"mfftgpu_ipc_open failed ({rc})")
+        self.ptr = ptr.value
+        self.esize = esize
+        self.tensor = None
+        if self.rank == root:
+            self.tensor = torch.as_tensor(_DeviceArray(self.ptr, count, self._TYPESTR[dtype]),
+                                          device="cuda")
+
+    def close(self):
+        import torch.distributed as dist
+
+        from ._lib import lib
+        if self.ptr is None:
+            return
+        self.tensor = None
+        dist.barrier(group=self.group)
+        if self.rank != self.root:
+            lib.mfftgpu_ipc_close(self.ptr)
+        dist.barrier(group=self.group)
+        if self.rank == self.root:
+            lib.mfftgpu_ipc_free(self.ptr)
+        self.ptr = None
 
 
 def sub_ranges(r0: int, r1: int, nsub: int, align: int = 256):

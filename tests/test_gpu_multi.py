@@ -2,9 +2,11 @@
 is visible; skipped otherwise.
 
 Every rank computes its rows of C for a W=64 signed product, B is
-all-gathered from the ranks' row blocks and C's rows are gathered to rank 0,
-which compares the assembled product with a one-GPU product of the same
-inputs, bit for bit.  NVLS is switched off for this test.
+all-gathered from the ranks' row blocks and C's rows reach rank 0 -- by NCCL
+point-to-point transfers, and again by the final kernel of every rank storing
+into rank 0's buffer through a CUDA IPC mapping -- and rank 0 compares each
+assembled product with a one-GPU product of the same inputs, bit for bit.
+NVLS is switched off for this test.
 """
 import os
 import socket
@@ -51,10 +53,25 @@ def _rank(rank, world, port, n, errq):
         full = torch.empty(9 * n * n, dtype=torch.uint16, device=dev) if rank == 0 else None
         ctx.sync()
         D.gather_planes_to_root(out, full, n, 9, ranges)
+        want = None
         if rank == 0:
             want = ctx.mm_i64(A, Bfull, n, RL=9)
             ctx.sync()
             assert torch.equal(full.view(torch.int16), want.view(torch.int16)), "sharded != 1 GPU"
+        # the same product with every rank's final kernel storing its rows
+        # straight into rank 0's buffer through a CUDA IPC mapping
+        peer = D.PeerOutput(9 * n * n, "uint16")
+        ctx.set_output_plane_stride(n * n)
+        ctx.mm_i64(A, B, n, RL=9, out=peer.ptr + r0 * n * 2, rows=(r0, r1))
+        ctx.set_output_plane_stride(0)
+        ctx.sync()
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.all_reduce(flag)
+        torch.cuda.synchronize()
+        if rank == 0:
+            assert torch.equal(peer.tensor.view(torch.int16), want.view(torch.int16)), \
+                "peer-stored rows != 1 GPU"
+        peer.close()
         dist.barrier()
         ctx.close()
         dist.destroy_process_group()
