@@ -641,7 +641,8 @@ def main():
                 "ops_per_step": 2 * macs_rank, "pointwise_ms_per_step": pw_ms}
             line["int8_tops_issued"] = 2 * macs / (ms * 1e-3) / 1e12
             line["schoolbook_equiv_tops"] = 2 * pi["schoolbook_macs"] / (ms * 1e-3) / 1e12
-            line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs")}
+            line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs",
+                                               "half_points")}
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share

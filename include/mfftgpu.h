@@ -56,6 +56,8 @@ typedef struct {
                                 job t of chunk ch sums A_u B_(t-u), u in [ch*U, ch*U+U)) */
     int U;                   /* schoolbook: digit planes of A per contraction chunk */
     int balanced;            /* 1: balanced digits in [-2^(b-1), 2^(b-1)) (int64 operands) */
+    int half_points;         /* 1: the last product skipped the zero plane products of the
+                                points 0 and NB/2 (int8_macs counts the issued ones) */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -104,6 +106,11 @@ int mfftgpu_ipc_free(void *ptr);
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
  * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel. */
 int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
+/* At the evaluation points 0 and NB/2 the transformed blocks keep only their
+ * low K/2 coefficients, so three quarters of those points' plane products
+ * are zero; on = 1 (the default, or $MFFTGPU_HALF_POINTS) lets the t-grouped
+ * plane-product kernel skip them, 0 computes them.  Results are identical. */
+int mfftgpu_set_half_points(mfftgpu_ctx *ctx, int on);
 const char *mfftgpu_last_error(mfftgpu_ctx *ctx);
 const char *mfftgpu_status_string(int status);
 int mfftgpu_device_count(void);

@@ -120,6 +120,11 @@ class Context:
         self._check(lib.mfftgpu_set_output_plane_stride(self._h, int(elems)),
                     "set_output_plane_stride")
 
+    def set_half_points(self, on):
+        """Skip (True, the default) or compute the plane products that are zero
+        at the evaluation points 0 and NB/2; identical results."""
+        self._check(lib.mfftgpu_set_half_points(self._h, int(bool(on))), "set_half_points")
+
     def set_kernel_variant(self, stage, variant):
         """Pick the kernel of a stage ('pointwise' or 'inverse'; 0 = auto).
         Every variant computes the same bits; this is for comparisons."""

@@ -58,6 +58,7 @@ struct mfftgpu_ctx {
     int raster = 0, group_m = 0;  // pointwise tile order (tuning)
     int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs, 3 grouped
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
+    int half_points = 1;          // skip the zero terms of points 0 and NB/2 (t-grouped kernel)
     int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
@@ -70,6 +71,7 @@ struct mfftgpu_ctx {
     Plan last_plan{};
     bool have_plan = false;
     int last_pw_kernel = 0;
+    int last_half = 0;  // the last product's plane-product kernel skipped the half-point terms
     char msg[512] = {};
 };
 
@@ -322,7 +324,8 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.rows = rb;
         L.cols = n_int;
         L.kdim = n_int;
-        L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs, school ? 1 : 0, P.LbA, P.LbB, P.U};
+        L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs, school ? 1 : 0, P.LbA, P.LbB, P.U,
+                        P.NB, (!school && C->half_points && P.K == 2 * P.S) ? P.S : 0};
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
         L.out = acc;
         L.out_plane = R * n_int;
@@ -337,6 +340,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.chosen = &C->last_pw_kernel;
         tick(2);
         if ((rc = pointwise_launch(L, st))) return set_err(C, rc, "pointwise launch failed");
+        C->last_half = L.jobs.zpS > 0 && C->last_pw_kernel == 3;
         ++C->launches;
         tock();
 
@@ -498,6 +502,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_GROUP_M")) C->group_m = atoi(s);
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
+    if (const char* s = getenv("MFFTGPU_HALF_POINTS")) C->half_points = atoi(s) != 0;
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
     cudaMemset(C->d_err, 0, 256);
@@ -601,6 +606,12 @@ int mfftgpu_ipc_free(void* ptr) {
     return ptr && cudaFree(ptr) == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
+int mfftgpu_set_half_points(mfftgpu_ctx* C, int on) {
+    if (!C || on < 0 || on > 1) return MFFTB_ERR_ARG;
+    C->half_points = on;
+    return MFFTB_OK;
+}
+
 int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
     if (!C) return MFFTB_ERR_ARG;
     if (stage == 2 && variant >= 0 && variant <= 3) {
@@ -676,6 +687,12 @@ int mfftgpu_last_plan(mfftgpu_ctx* C, mfftgpu_plan_info* o) {
     if (!C || !o || !C->have_plan) return MFFTB_ERR_ARG;
     fill_info(C->last_plan, o);
     o->pw_kernel = C->last_pw_kernel;
+    const Plan& P = C->last_plan;
+    if (C->last_half && P.kind == KIND_MFFT && P.NB >= 2) {
+        // points 0 and NB/2 issue S^2 of their K^2 plane products
+        o->half_points = 1;
+        o->int8_macs *= ((double)(P.NB - 2) * P.K * P.K + 2.0 * P.S * P.S) / ((double)P.NB * P.K * P.K);
+    }
     return MFFTB_OK;
 }
 
@@ -707,6 +724,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->kind = P.kind;
     o->U = P.U;
     o->balanced = P.balanced;
+    o->half_points = 0;
 }
 
 // --------------------------------------------------------------------- integers
@@ -1020,6 +1038,10 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     cudaSetDevice(C->device);
     const int ld = (kdim + 15) / 16 * 16;
     PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
+    if (C->half_points && K % 2 == 0) {
+        J.NB = NB;
+        J.zpS = K / 2;
+    }
     const int apl = NB * dA * K, fpl = NB * dB * (2 * K - 1);
     const size_t szA = align256((size_t)apl * rows * ld), szF = align256((size_t)fpl * cols * ld);
     const size_t szO = align256((size_t)J.njobs * rows * cols * 4);
@@ -1035,6 +1057,23 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     gen_u16_kernel<<<C->num_sms * 4, 256, 0, C->stream>>>(reinterpret_cast<uint16_t*>(A),
                                                           (long long)(szA + szF) / 2, 0x5EEDull);
     CUDA_OK(cudaGetLastError());
+    if (J.zpS > 0) {
+        // operands as a forward transform leaves them: at j = 0 and j = NB/2
+        // Ahat[c] = Bhat[c] = 0 for c >= K/2, i.e. F planes [0, K/2) and
+        // [K, K + K/2) of every digit (the checker then sums those zeros)
+        for (int j = 0; j < NB; ++j) {
+            if (!pw_half_point(J, j)) continue;
+            for (int da = 0; da < dA; ++da)
+                CUDA_OK(cudaMemsetAsync(A + ((long long)(j * dA + da) * K + K / 2) * rows * ld, 0,
+                                        (size_t)(K / 2) * rows * ld, C->stream));
+            for (int db = 0; db < dB; ++db) {
+                int8_t* f0 = F + (long long)(j * dB + db) * (2 * K - 1) * cols * ld;
+                CUDA_OK(cudaMemsetAsync(f0, 0, (size_t)(K / 2) * cols * ld, C->stream));
+                CUDA_OK(cudaMemsetAsync(f0 + (long long)K * cols * ld, 0, (size_t)(K / 2) * cols * ld,
+                                        C->stream));
+            }
+        }
+    }
     CUDA_OK(cudaMemsetAsync(C->d_err, 0, 64, C->stream));
     PwLaunch L{};
     L.A = A;

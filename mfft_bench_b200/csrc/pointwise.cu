@@ -516,6 +516,32 @@ __device__ __forceinline__ int pw3_school_pairs(const PwJobs& J, int t0, int ch,
     return hi >= lo ? (hi - lo + 2) / 2 : 0;
 }
 
+// Which planes stage c (c1 = c, c+1) of a tile must load: bit cc of needA for
+// A plane c + cc, bit f of needF for F slot f, from the slots (tt, cc) whose
+// term can be non-zero (c + cc in [lo[tt], hi[tt]]).  The MMA thread applies
+// the same test slot by slot; a stage with needA == 0 is skipped by both.
+__device__ __forceinline__ void pw3_stage_need(const int (&lo)[PW3_TG], const int (&hi)[PW3_TG],
+                                               int c, uint32_t& needA, uint32_t& needF) {
+    needA = 0;
+    needF = 0;
+#pragma unroll
+    for (int cc = 0; cc < PW3_CPS; ++cc)
+#pragma unroll
+        for (int tt = 0; tt < PW3_TG; ++tt)
+            if (c + cc >= lo[tt] && c + cc <= hi[tt]) {
+                needA |= 1u << cc;
+                needF |= 1u << (PW3_TG - 1 - tt + cc);
+            }
+}
+
+// MFFT tile (j, t0..t0+3): the c1 range of each job (everything at an
+// ordinary point, the triangle of possibly non-zero terms at a half point)
+__device__ __forceinline__ void pw3_point_ranges(const PwJobs& J, int j, int t0,
+                                                 int (&lo)[PW3_TG], int (&hi)[PW3_TG]) {
+#pragma unroll
+    for (int tt = 0; tt < PW3_TG; ++tt) pw_point_range(J, j, t0 + tt, lo[tt], hi[tt]);
+}
+
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
     pointwise3_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmF, const PwParams p) {
@@ -569,7 +595,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         uint32_t phase = 0;
         int issued_parity[PW3_STAGES];
         for (int s = 0; s < PW3_STAGES; ++s) issued_parity[s] = -1;
-        const uint32_t tx_bytes = 2 * PW3_STAGE_BYTES;
         const long long first_tile = p.stall_producer ? p.num_tiles : pair;
         bool align = p.wave_counter != nullptr;
         long long wave = 0;
@@ -639,6 +664,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                 }
                 continue;
             }
+            int plo[PW3_TG], phi[PW3_TG];
+            pw3_point_ranges(p.jobs, j, t0, plo, phi);
             const int npr = pw_class_pairs(p.jobs, w);
             for (int pi = 0; pi < npr; ++pi) {
             const int da = pw_class_first_da(p.jobs, w) + pi, db = w - da;
@@ -647,23 +674,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             for (int cp = 0; cp < cps_per_kb; ++cp) {
                 const int c = cp * PW3_CPS;
                 const int p_lo = K - PW3_TG - t0 + c;
+                uint32_t needA, needF;  // all planes at an ordinary point
+                pw3_stage_need(plo, phi, c, needA, needF);
+                if (needA == 0) continue;  // every term of the stage is zero (half point)
+                const uint32_t stage_tx =
+                    2u * ((uint32_t)__popc(needA) * PW3_A_BYTES + (uint32_t)__popc(needF) * PW3_F_BYTES);
                 for (int kb = 0; kb < p.kblocks; ++kb) {
                     if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
                                            global_timer_ns() + tmo))
                         goto producer_done;
                     const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
-                    if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, tx_bytes);
+                    if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
                     uint8_t* st = smem + stage * PW3_STAGE_BYTES;
 #pragma unroll
                     for (int cc = 0; cc < PW3_CPS; ++cc)
-                        tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
-                                         kb * PW_BK, mt * 256 + (int)rank * 128, a_base + c + cc);
+                        if (needA & (1u << cc))
+                            tma_load_3d_pair(smem_u32(st + cc * PW3_A_BYTES), &tmA, full_leader,
+                                             kb * PW_BK, mt * 256 + (int)rank * 128, a_base + c + cc);
 #pragma unroll
                     for (int f = 0; f < PW3_NF; ++f)
-                        tma_load_3d_pair(
-                            smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
-                            full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
-                            f_base + p_lo + f);
+                        if (needF & (1u << f))
+                            tma_load_3d_pair(
+                                smem_u32(st + PW3_CPS * PW3_A_BYTES + f * PW3_F_BYTES), &tmF,
+                                full_leader, kb * PW_BK, nt * PW3_BN + (int)rank * (PW3_BN / 2),
+                                f_base + p_lo + f);
                     issued_parity[stage] = (int)phase;
                     if (++stage == PW3_STAGES) {
                         stage = 0;
@@ -689,10 +723,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             int j, w, t0, mt, nt;
             pw3_tile_decode(p, tile, j, w, t0, mt, nt);
             int ulo = 0;
-            const int steps_per_tile =
-                p.jobs.school ? pw3_school_pairs(p.jobs, t0, w, ulo) * p.kblocks
-                              : pw_class_pairs(p.jobs, w) * cps_per_kb * p.kblocks;
-            if (steps_per_tile == 0) continue;  // schoolbook tile without terms
+            int plo[PW3_TG], phi[PW3_TG];
+            int steps_per_tile;
+            if (p.jobs.school) {
+                steps_per_tile = pw3_school_pairs(p.jobs, t0, w, ulo) * p.kblocks;
+            } else {
+                pw3_point_ranges(p.jobs, j, t0, plo, phi);
+                int live = 0;
+                for (int cp = 0; cp < cps_per_kb; ++cp) {
+                    uint32_t needA, needF;
+                    pw3_stage_need(plo, phi, cp * PW3_CPS, needA, needF);
+                    live += needA != 0;
+                }
+                steps_per_tile = pw_class_pairs(p.jobs, w) * live * p.kblocks;
+            }
+            if (steps_per_tile == 0) continue;  // tile without terms
             if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
@@ -737,32 +782,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                 acc_phase ^= 1;
                 continue;
             }
-            for (int it = 0; it < steps_per_tile; ++it) {
-                if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
-                                       global_timer_ns() + tmo))
-                    goto mma_done;
-                tc_fence_after();
-                const uint32_t st = smem_u32(smem + stage * PW3_STAGE_BYTES);
+            {
+            // same stage walk as the producer: class pairs, c1 pairs with a
+            // possibly non-zero term, contraction blocks
+            const int npr = pw_class_pairs(p.jobs, w);
+            uint32_t started = 0;
+            for (int pi = 0; pi < npr; ++pi)
+            for (int cp = 0; cp < cps_per_kb; ++cp) {
+                const int c = cp * PW3_CPS;
+                uint32_t needA, needF;
+                pw3_stage_need(plo, phi, c, needA, needF);
+                if (needA == 0) continue;
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                           global_timer_ns() + tmo))
+                        goto mma_done;
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + stage * PW3_STAGE_BYTES);
 #pragma unroll
-                for (int cc = 0; cc < PW3_CPS; ++cc) {
+                    for (int cc = 0; cc < PW3_CPS; ++cc) {
 #pragma unroll
-                    for (int tt = 0; tt < PW3_TG; ++tt) {
-                        const int fi = PW3_TG - 1 - tt + cc;  // F plane K-1-(t0+tt)+(c+cc) - p_lo
-                        const uint32_t a0 = st + cc * PW3_A_BYTES;
-                        const uint32_t b0 = st + PW3_CPS * PW3_A_BYTES + fi * PW3_F_BYTES;
+                        for (int tt = 0; tt < PW3_TG; ++tt) {
+                            if (c + cc < plo[tt] || c + cc > phi[tt]) continue;  // zero term
+                            const int fi = PW3_TG - 1 - tt + cc;  // F plane K-1-(t0+tt)+(c+cc) - p_lo
+                            const uint32_t a0 = st + cc * PW3_A_BYTES;
+                            const uint32_t b0 = st + PW3_CPS * PW3_A_BYTES + fi * PW3_F_BYTES;
+                            const uint32_t acc_on = (started >> tt) & 1u;
 #pragma unroll
-                        for (int kk = 0; kk < PW_BK / 32; ++kk)
-                            mma_i8_pair(tmem_base + (uint32_t)(tt * PW3_BN),
-                                        sdesc_kmajor_sw128(a0 + kk * 32),
-                                        sdesc_kmajor_sw128(b0 + kk * 32), idesc,
-                                        (it | cc | kk) != 0 ? 1u : 0u);
+                            for (int kk = 0; kk < PW_BK / 32; ++kk)
+                                mma_i8_pair(tmem_base + (uint32_t)(tt * PW3_BN),
+                                            sdesc_kmajor_sw128(a0 + kk * 32),
+                                            sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                            (acc_on | (uint32_t)kk) != 0 ? 1u : 0u);
+                            started |= 1u << tt;
+                        }
+                    }
+                    mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                    if (++stage == PW3_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
                     }
                 }
-                mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
-                if (++stage == PW3_STAGES) {
-                    stage = 0;
-                    phase ^= 1;
-                }
+            }
             }
             mma_commit_pair_mc(bar_tfull, 0x3);
             acc_phase ^= 1;
@@ -777,13 +838,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
             int j, w, t0, mt, nt;
             pw3_tile_decode(p, tile, j, w, t0, mt, nt);
+            int plo[PW3_TG], phi[PW3_TG];
+            bool any = true;  // the MMA thread accumulated something for this tile
             if (p.jobs.school) {
                 int ulo;
                 if (pw3_school_pairs(p.jobs, t0, w, ulo) == 0) continue;
+            } else {
+                pw3_point_ranges(p.jobs, j, t0, plo, phi);
+                any = false;
+#pragma unroll
+                for (int tt = 0; tt < PW3_TG; ++tt) any |= plo[tt] <= phi[tt];
             }
-            if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
-                break;
-            tc_fence_after();
+            if (any) {
+                if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
+                    break;
+                tc_fence_after();
+            }
             const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
             const int col0 = nt * PW3_BN;
             const int colmax = p.cols - col0;
@@ -795,13 +865,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                     if (lo > hi) continue;  // no term: the plane is never read
                     q = (t0 + tt) * p.jobs.nchunk + w;
                 }
+                // an MFFT job without terms (t > K - 2 at a half point) is a zero plane
+                const bool zero = !p.jobs.school && plo[tt] > phi[tt];
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
                 for (int c = 0; c < PW3_BN / 32; ++c) {
                     uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                                           (uint32_t)(tt * PW3_BN + c * 32),
-                                       v);
-                    tmem_ld_wait();
+                    if (zero) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = 0u;
+                    } else {
+                        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                               (uint32_t)(tt * PW3_BN + c * 32),
+                                           v);
+                        tmem_ld_wait();
+                    }
                     if (row < p.rows) {
 #pragma unroll
                         for (int e = 0; e < 32; e += 4) {
@@ -818,9 +895,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
                     }
                 }
             }
-            tc_fence_before();
-            mbar_arrive_cluster(mapa_shared(bar_tempty, 0));
-            acc_phase ^= 1;
+            if (any) {
+                tc_fence_before();
+                mbar_arrive_cluster(mapa_shared(bar_tempty, 0));
+                acc_phase ^= 1;
+            }
         }
     }
 

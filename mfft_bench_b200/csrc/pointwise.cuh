@@ -52,7 +52,32 @@ struct PwJobs {
     // multiple of 4), dA = dB = nW = 1.
     int school;
     int LbA, LbB, U;
+    // Half points (MFFT mode): the points j = 0 and j = NB/2 evaluate the
+    // blocks at y^0 and y^K = -1, which moves no coefficient, so there
+    // Ahat_j and Bhat_j vanish above coefficient zpS - 1 (zpS = S = K/2, the
+    // coefficients one block holds).  zpS > 0 tells the t-grouped kernel it
+    // may skip the terms that are zero for that reason; 0 = no skipping.
+    int NB;
+    int zpS;
 };
+
+__host__ __device__ inline bool pw_half_point(const PwJobs& J, int j) {
+    return !J.school && J.zpS > 0 && (j == 0 || 2 * j == J.NB);
+}
+
+// c1 range [lo, hi] of the terms of job (j, t) that can be non-zero: every c1
+// at an ordinary point; at a half point only c1 < zpS with 0 <= t - c1 < zpS
+// (no wrap, since t - c1 + K >= zpS); empty when lo > hi (t > 2 zpS - 2).
+__host__ __device__ inline void pw_point_range(const PwJobs& J, int j, int t, int& lo, int& hi) {
+    if (!pw_half_point(J, j)) {
+        lo = 0;
+        hi = J.K - 1;
+        return;
+    }
+    lo = t - (J.zpS - 1);
+    if (lo < 0) lo = 0;
+    hi = t < J.zpS - 1 ? t : J.zpS - 1;
+}
 
 // u range [lo, hi] of schoolbook job (t, ch); empty when lo > hi
 __host__ __device__ inline void pw_school_range(const PwJobs& J, int t, int ch, int& lo, int& hi) {

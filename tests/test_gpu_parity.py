@@ -56,6 +56,54 @@ def test_pointwise_grouped_kernel_vs_cuda_cores(ctx, rows, cols, kdim, NB, K, dA
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, 1, 256, variant=3) == 0
 
 
+@pytest.mark.parametrize("half", [0, 1])
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,dA,dB", [
+    (256, 256, 256, 8, 8, 1, 1),
+    (512, 384, 256, 16, 16, 1, 1),
+    (300, 272, 144, 4, 4, 3, 2),
+    (512, 256, 384, 32, 16, 2, 2),
+])
+def test_pointwise_grouped_half_points(ctx, half, rows, cols, kdim, NB, K, dA, dB):
+    """Points 0 and NB/2 with operands that vanish above coefficient K/2 (as
+    the forward transform leaves them): the t-grouped kernel skipping their
+    zero terms (half=1) and computing them (half=0) both match the CUDA-core
+    sum over every term."""
+    ctx.set_half_points(half)
+    try:
+        assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, dA, dB, 1, 256, variant=3) == 0
+    finally:
+        ctx.set_half_points(1)
+
+
+@pytest.mark.parametrize("n,L,signed", [
+    (256, 16, True),    # b4 NB16 K16
+    (300, 4, True),     # b4 NB8 K8 (the W=64 plan), ragged n
+    (256, 64, False),   # b8 NB32 K16, 3 digit classes
+    (512, 8, False),    # b4 NB16 K8
+])
+def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
+    """Whole products with the half-point terms skipped and computed are the
+    same bits, and match the oracle's exact entries."""
+    gen = oracle.signed_planes if signed else oracle.bigmat_rand
+    A, B = gen(n, L, 71 + n), gen(n, L, 73 + L)
+    ctx.set_half_points(0)
+    try:
+        dense = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
+        pd = ctx.last_plan()
+    finally:
+        ctx.set_half_points(1)
+    got = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
+    ph = ctx.last_plan()
+    assert ph["pw_kernel"] == 3 and ph["half_points"] == 1 and pd["half_points"] == 0
+    NB, K, S = ph["NB"], ph["K"], ph["S"]
+    assert ph["int8_macs"] == pytest.approx(pd["int8_macs"] * ((NB - 2) * K * K + 2 * S * S)
+                                            / (NB * K * K))
+    assert np.array_equal(got, dense)
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 3000)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 3000)]
+    assert np.array_equal(got[:, rows, cols], oracle.entries(A, B, n, L, signed, rows, cols))
+
+
 # ---------------------------------------------------------------- the inverse kernels
 @pytest.mark.parametrize("n,L,signed", [
     (256, 16, True),    # b4 NB16 K16
