@@ -81,10 +81,11 @@ def env_int(k, d):
 # capture of dram__bytes_read.sum / dram__bytes_write.sum on the full
 # workload (profiles/pointwise3_i8_c5_dram.md).
 POINTWISE_TRAFFIC = {
-    "c5": {"bytes_per_launch": 1.02e12 + 52.27e9,
-           "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows): "
-                    "1.02 TB read + 52.3 GB written; algorithmic operand bytes of that "
-                    "launch 43.9 GB read + 46.7 GB of int32 job planes written")},
+    "c5": {"bytes_per_launch": 848.51e9 + 52.15e9,
+           "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows), "
+                    "half-point terms skipped: 848.5 GB read + 52.2 GB written; "
+                    "algorithmic operand bytes of that launch 43.9 GB read + 46.7 GB "
+                    "of int32 job planes written")},
 }
 
 PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
