@@ -13,6 +13,9 @@
 //   * pointwise3_i8_kernel: CTA pairs, 256 x 128 tiles of 4 jobs that share
 //     their A planes and overlapping F windows, wave-aligned tile order -- the
 //     default for one-chunk MFFT plans and the only one for schoolbook plans.
+//     It issues only the terms that can be non-zero: at the MFFT points 0 and
+//     NB/2 the triangle c1 < K/2, t - c1 < K/2 (pw_point_range), in
+//     schoolbook mode the planes that exist (pw_school_range).
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -468,7 +471,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
 // planes of A (2 x 16 KB per CTA) and the 5 F planes those 8 (c1, t) pairs
 // need (5 x 8 KB): 72 KB per stage feed 32 pair MMAs (256 x 128 x 32), so
 // every operand byte loaded into shared memory is used 3.2 times on average
-// instead of once.
+// instead of once.  At the half points (pw_half_point) a stage whose eight
+// (c1, t) slots all hold zero terms is skipped, the other stages load and
+// multiply only the planes of their possibly non-zero terms, and the
+// epilogue writes a job without terms (t = K-1) as zeros.
 constexpr int PW3_STAGES = 3;
 constexpr int PW3_TG = 4;             // jobs per tile group
 constexpr int PW3_CPS = 2;            // c1 planes per stage
