@@ -102,6 +102,7 @@ int mfftgpu_ipc_open(const void *handle, void **ptr);
 int mfftgpu_ipc_close(void *ptr);
 int mfftgpu_ipc_free(void *ptr);
 /* Kernel choice per stage, for comparisons; results are identical.
+ * stage 1 (forward transform): 0 auto, 1 the generic kernel;
  * stage 2 (plane products): 0 auto, 1 one CTA per tile, 2 CTA pairs,
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
  * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel. */

@@ -126,9 +126,9 @@ class Context:
         self._check(lib.mfftgpu_set_half_points(self._h, int(bool(on))), "set_half_points")
 
     def set_kernel_variant(self, stage, variant):
-        """Pick the kernel of a stage ('pointwise' or 'inverse'; 0 = auto).
+        """Pick the kernel of a stage ('forward', 'pointwise' or 'inverse'; 0 = auto).
         Every variant computes the same bits; this is for comparisons."""
-        sid = {"pointwise": 2, "inverse": 3}[stage]
+        sid = {"forward": 1, "pointwise": 2, "inverse": 3}[stage]
         self._check(lib.mfftgpu_set_kernel_variant(self._h, sid, int(variant)),
                     "set_kernel_variant")
 

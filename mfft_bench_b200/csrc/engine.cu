@@ -60,6 +60,7 @@ struct mfftgpu_ctx {
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
     int half_points = 1;          // skip the zero terms of points 0 and NB/2 (t-grouped kernel)
     int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
+    int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
@@ -245,6 +246,8 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     fb.out = F;
     fb.oplane = nn_int;
     fb.err = C->d_err;
+    fb.b = P.b;
+    fb.variant = C->fwd_variant;
     if (!b_cached) {
         C->b_valid = false;
         tick(0);
@@ -504,6 +507,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
     if (const char* s = getenv("MFFTGPU_HALF_POINTS")) C->half_points = atoi(s) != 0;
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
+    if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
     cudaMemset(C->d_err, 0, 256);
     *out = C;
@@ -620,6 +624,10 @@ int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
     }
     if (stage == 3 && variant >= 0 && variant <= 1) {
         C->inv_variant = variant;
+        return MFFTB_OK;
+    }
+    if (stage == 1 && variant >= 0 && variant <= 1) {
+        C->fwd_variant = variant;
         return MFFTB_OK;
     }
     return MFFTB_ERR_ARG;

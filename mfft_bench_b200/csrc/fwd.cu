@@ -10,13 +10,16 @@
 //     Xhat_j[c] = sum_beta  s * X[beta*S + c'],   c' = (c - g j beta) mod 2K
 //                                                 (s = -1 when c' lands in [K, 2K))
 //
-// Both kernels evaluate these sums directly for 4 consecutive elements per
-// thread and write each value as d signed int8 digits; forward_simd_kernel
+// The kernels evaluate these sums directly for 4 consecutive elements per
+// thread and write each value as d signed int8 digits: forward_simd_kernel
 // (one-digit plans, int8 digit planes) keeps the digits in registers as
-// packed bytes with compile-time twiddles, forward_kernel (the rest) reads
-// them through L1 and spreads the evaluation points over gridDim.y when the
-// operand is small.  For B they write the F stack the pointwise kernel
-// expects: F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
+// packed bytes with compile-time twiddles; forward_pt_kernel (K = 8/16/32
+// otherwise, while the sums fit int16) gives each warp one point and adds
+// packed int16 pairs, the shift picked by a warp-uniform switch;
+// forward_kernel (the rest: K = 64, wide digits) reads the digits through L1
+// and spreads the evaluation points over gridDim.y when the operand is small.
+// For B they write the F stack the pointwise kernel expects:
+// F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -161,6 +164,136 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
     }
 }
 
+// One evaluation point per warp (multi-digit plans and int16 digit planes,
+// K = 8, 16 or 32).  Lane l holds elements e0..e0+3 (e0 = 4l + 128 x block)
+// as two packed int16 pairs per coefficient; block beta enters point j
+// shifted by e = g j beta mod 2K, which is warp-uniform, so a switch on e
+// picks a fully unrolled shift-and-add with constant register indices.  Every
+// partial sum is a signed sum of at most nc digits of at most 2^b, which the
+// launcher checks stays below 2^15.  The digits a warp loads are the ones
+// the other warps of the CTA (other points, same elements) load too, so they
+// come from L1 after the first.
+template <int K, int E>
+__device__ __forceinline__ void fwd_pt_shift_add(uint32_t (&acc)[K][2],
+                                                 const uint32_t (&x)[K / 2][2]) {
+    if constexpr (E < 2 * K) {
+        constexpr int S = K / 2;
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+            const int r = (c - E + 2 * K) % (2 * K);  // X coefficient landing on c
+            if (r < S) {
+                acc[c][0] = __vadd2(acc[c][0], x[r][0]);
+                acc[c][1] = __vadd2(acc[c][1], x[r][1]);
+            } else if (r >= K && r < K + S) {  // wrapped past y^K: negated
+                acc[c][0] = __vsub2(acc[c][0], x[r - K][0]);
+                acc[c][1] = __vsub2(acc[c][1], x[r - K][1]);
+            }
+        }
+    }
+}
+
+template <int DB>
+__device__ __forceinline__ void load4_pairs(const void* D, long long off, uint32_t& p01,
+                                            uint32_t& p23) {
+    if (DB == 2) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const int16_t*>(D) + off));
+        p01 = v.x;
+        p23 = v.y;
+    } else {
+        const char4 c = __ldg(reinterpret_cast<const char4*>(reinterpret_cast<const int8_t*>(D) + off));
+        p01 = (uint32_t)(uint16_t)(int16_t)c.x | ((uint32_t)(uint16_t)(int16_t)c.y << 16);
+        p23 = (uint32_t)(uint16_t)(int16_t)c.z | ((uint32_t)(uint16_t)(int16_t)c.w << 16);
+    }
+}
+
+#define FWD_PT_CASE(E)                      \
+    case E:                                 \
+        fwd_pt_shift_add<K, E>(acc, x);     \
+        break;
+
+template <int K, int DB>
+__global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a) {
+    constexpr int S = K / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j = blockIdx.y * (blockDim.x >> 5) + warp;
+    const long long e0 = (long long)blockIdx.x * 128 + 4 * lane;
+    if (j >= a.NB || e0 >= a.nelem) return;
+    const int step = (a.g * j) & (2 * K - 1);
+    uint32_t acc[K][2];
+#pragma unroll
+    for (int c = 0; c < K; ++c) acc[c][0] = acc[c][1] = 0u;
+    int e = 0;
+    for (int beta = 0; beta < a.nc; ++beta, e = (e + step) & (2 * K - 1)) {
+        uint32_t x[S][2];
+#pragma unroll
+        for (int r = 0; r < S; ++r) {
+            const int m = beta * S + r;
+            x[r][0] = x[r][1] = 0u;
+            if (m < a.Lb) load4_pairs<DB>(a.D, (long long)m * a.dplane + e0, x[r][0], x[r][1]);
+        }
+        switch (e) {
+            FWD_PT_CASE(0) FWD_PT_CASE(1) FWD_PT_CASE(2) FWD_PT_CASE(3)
+            FWD_PT_CASE(4) FWD_PT_CASE(5) FWD_PT_CASE(6) FWD_PT_CASE(7)
+            FWD_PT_CASE(8) FWD_PT_CASE(9) FWD_PT_CASE(10) FWD_PT_CASE(11)
+            FWD_PT_CASE(12) FWD_PT_CASE(13) FWD_PT_CASE(14) FWD_PT_CASE(15)
+            FWD_PT_CASE(16) FWD_PT_CASE(17) FWD_PT_CASE(18) FWD_PT_CASE(19)
+            FWD_PT_CASE(20) FWD_PT_CASE(21) FWD_PT_CASE(22) FWD_PT_CASE(23)
+            FWD_PT_CASE(24) FWD_PT_CASE(25) FWD_PT_CASE(26) FWD_PT_CASE(27)
+            FWD_PT_CASE(28) FWD_PT_CASE(29) FWD_PT_CASE(30) FWD_PT_CASE(31)
+            FWD_PT_CASE(32) FWD_PT_CASE(33) FWD_PT_CASE(34) FWD_PT_CASE(35)
+            FWD_PT_CASE(36) FWD_PT_CASE(37) FWD_PT_CASE(38) FWD_PT_CASE(39)
+            FWD_PT_CASE(40) FWD_PT_CASE(41) FWD_PT_CASE(42) FWD_PT_CASE(43)
+            FWD_PT_CASE(44) FWD_PT_CASE(45) FWD_PT_CASE(46) FWD_PT_CASE(47)
+            FWD_PT_CASE(48) FWD_PT_CASE(49) FWD_PT_CASE(50) FWD_PT_CASE(51)
+            FWD_PT_CASE(52) FWD_PT_CASE(53) FWD_PT_CASE(54) FWD_PT_CASE(55)
+            FWD_PT_CASE(56) FWD_PT_CASE(57) FWD_PT_CASE(58) FWD_PT_CASE(59)
+            FWD_PT_CASE(60) FWD_PT_CASE(61) FWD_PT_CASE(62) FWD_PT_CASE(63)
+            default: break;
+        }
+    }
+    // d signed int8 digits per value (balanced 7-bit low digits, top digit
+    // the rest), the same split as forward_kernel
+    const long long plane0 = (long long)j * a.d * (a.f_stack ? (2 * K - 1) : K);
+#pragma unroll
+    for (int c = 0; c < K; ++c) {
+        int x[4] = {(int)(int16_t)(acc[c][0] & 0xffffu), (int)(int16_t)(acc[c][0] >> 16),
+                    (int)(int16_t)(acc[c][1] & 0xffffu), (int)(int16_t)(acc[c][1] >> 16)};
+        for (int dd = 0; dd < a.d; ++dd) {
+            int dg[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (dd < a.d - 1) {
+                    const int lo = ((x[q] + 64) & 127) - 64;
+                    dg[q] = lo;
+                    x[q] = (x[q] - lo) >> 7;
+                } else {
+                    dg[q] = x[q];
+                }
+            }
+            if (!a.f_stack) {
+                store4(a.out + (plane0 + (long long)dd * K + c) * a.oplane + e0, dg[0], dg[1],
+                       dg[2], dg[3]);
+            } else {
+                const long long base = plane0 + (long long)dd * (2 * K - 1);
+                store4(a.out + (base + (K - 1 - c)) * a.oplane + e0, dg[0], dg[1], dg[2], dg[3]);
+                if (c >= 1)
+                    store4(a.out + (base + (2 * K - 1 - c)) * a.oplane + e0, -dg[0], -dg[1],
+                           -dg[2], -dg[3]);
+            }
+        }
+    }
+}
+#undef FWD_PT_CASE
+
+template <int K>
+static int launch_pt(const FwdArgs& a, cudaStream_t stream) {
+    const int wpb = a.NB < 8 ? a.NB : 8;  // warps (points) per CTA
+    const dim3 grid((unsigned)((a.nelem + 127) / 128), (unsigned)((a.NB + wpb - 1) / wpb));
+    if (a.dbytes == 1) forward_pt_kernel<K, 1><<<grid, 32 * wpb, 0, stream>>>(a);
+    else forward_pt_kernel<K, 2><<<grid, 32 * wpb, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
 template <int NB, int K>
 static int launch_simd(const FwdArgs& a, cudaStream_t stream) {
     long long blocks = (a.nelem / 4 + 255) / 256;
@@ -183,7 +316,7 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     long long blocks = (a.nelem / 4 + threads - 1) / threads;
     if (blocks <= 0) return MFFTB_OK;
     if ((1 << a.lgS) != a.S || (1 << a.lgK) != a.K) return MFFTB_ERR_ARG;
-    if (a.d == 1 && a.dbytes == 1 && 2 * a.S == a.K) {
+    if (a.variant == 0 && a.d == 1 && a.dbytes == 1 && 2 * a.S == a.K) {
         int rc = MFFTB_ERR_UNSUPPORTED;
         if (a.NB == 8 && a.K == 8) rc = launch_simd<8, 8>(a, stream);
         else if (a.NB == 4 && a.K == 4) rc = launch_simd<4, 4>(a, stream);
@@ -193,6 +326,14 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
         else if (a.NB == 16 && a.K == 8) rc = launch_simd<16, 8>(a, stream);
         else if (a.NB == 8 && a.K == 16) rc = launch_simd<8, 16>(a, stream);
         if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
+    }
+    // one point per warp with int16 lanes when every partial sum fits them:
+    // |sum| <= nc * 2^b < 2^15
+    if (a.variant == 0 && (a.dbytes == 1 || a.dbytes == 2) && 2 * a.S == a.K && a.b >= 1 &&
+        a.b <= 14 && ((long long)a.nc << a.b) < 32768 && a.NB >= 1 && a.nelem % 4 == 0) {
+        if (a.K == 8) return launch_pt<8>(a, stream);
+        if (a.K == 16) return launch_pt<16>(a, stream);
+        if (a.K == 32) return launch_pt<32>(a, stream);
     }
     long long jsplit = (4 * 148 + blocks - 1) / blocks;  // aim at >= 4 CTAs per SM
     if (jsplit > a.NB) jsplit = a.NB;

@@ -49,6 +49,8 @@ struct FwdArgs {
     int8_t* out;
     long long oplane;  // bytes per output plane
     int* err;
+    int b;             // digit width: every digit has |digit| <= 2^b
+    int variant;       // 0 auto, 1 the generic kernel only (for comparisons)
 };
 int forward_launch(const FwdArgs& a, cudaStream_t stream);
 

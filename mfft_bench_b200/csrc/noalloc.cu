@@ -121,6 +121,7 @@ extern "C" int mfftgpu_mm_i64_noalloc(const int64_t* A, const int64_t* B, int n,
     f.lgK = lg(P.K);
     f.oplane = nn;
     f.err = err;
+    f.b = P.b;
     FwdArgs fb = f;
     fb.D = DB;
     fb.Lb = P.LbB;

@@ -104,6 +104,37 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
     assert np.array_equal(got[:, rows, cols], oracle.entries(A, B, n, L, signed, rows, cols))
 
 
+# ---------------------------------------------------------------- the forward kernels
+@pytest.mark.parametrize("n,L,signed", [
+    (256, 64, False),   # b8 NB32 K16 d2, int16 digits (the c3 plan shape)
+    (130, 32, True),    # b4 NB16 K32, int8 digits
+    (64, 128, False),   # b8 NB32 K32 d2
+    (40, 17, False),    # b9 NB16 K8 d2
+    (96, 41, True),     # b11 NB8 K32 d2
+    (256, 12, False),   # b6 NB4 K32
+    (20, 49, True),     # b7 NB32 K16 d2, int8 digits
+    (300, 16, True),    # b4 NB16 K16: the byte-SIMD kernel
+    (24, 25, True),     # b13: sums too wide for int16 lanes, generic kernel either way
+])
+def test_forward_kernels_vs_generic(ctx, oracle, n, L, signed):
+    """The one-point-per-warp and byte-SIMD forward kernels against the
+    generic forward kernel (whole products, bit for bit) and the oracle."""
+    gen = oracle.signed_planes if signed else oracle.bigmat_rand
+    A, B = gen(n, L, 41 + n), gen(n, L, 43 + L)
+    got = ctx.mm_u16(A, B, n, L, signed=signed)
+    ctx.set_kernel_variant("forward", 1)
+    try:
+        ref = ctx.mm_u16(A, B, n, L, signed=signed)
+    finally:
+        ctx.set_kernel_variant("forward", 0)
+    assert np.array_equal(got, ref)
+    RL = 2 * L + 1
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 1500)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 1500)]
+    want = oracle.entries(A, B, n, L, signed, rows, cols)
+    assert np.array_equal(got.reshape(RL, n, n)[:, rows, cols], want)
+
+
 # ---------------------------------------------------------------- the inverse kernels
 @pytest.mark.parametrize("n,L,signed", [
     (256, 16, True),    # b4 NB16 K16
