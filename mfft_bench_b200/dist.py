@@ -109,55 +109,82 @@ class PeerOutput:
     stores its rows of C straight into it over NVLink -- the compute and the
     gather of C are one step, with no separate collective.  `ptr` is this
     rank's device address of the buffer; on the root, `tensor` views it.
-    close() is collective: mappings are closed before the root frees."""
+
+    Construction and close() are collective.  If the root cannot allocate or
+    any rank cannot map the buffer, every rank undoes what it set up and
+    raises, so no rank is left waiting in a later collective.  `lib` is the
+    loaded library (tests pass a stand-in)."""
 
     _TYPESTR = {"uint16": "<u2", "float32": "<f4", "float64": "<f8"}
+    _ESIZE = {"uint16": 2, "float32": 4, "float64": 8}
 
-    def __init__(self, count: int, dtype: str, group=None, root: int = 0):
+    def __init__(self, count: int, dtype: str, group=None, root: int = 0, lib=None):
         import ctypes as C
 
-        import torch
         import torch.distributed as dist
 
-        from ._lib import lib
+        if lib is None:
+            from ._lib import lib
+        self._lib = lib
         self.group, self.root = group, root
         self.rank = dist.get_rank(group)
-        esize = {"uint16": 2, "float32": 4, "float64": 8}[dtype]
+        self.count, self.dtype = count, dtype
+        self.esize = self._ESIZE[dtype]
+        self._tensor = None
         ptr = C.c_void_p()
         handle = (C.c_char * 64)()
         payload = [None]
+        ok, err = True, ""
         if self.rank == root:
-            rc = lib.mfftgpu_ipc_alloc(count * esize, C.byref(ptr), handle)
+            rc = lib.mfftgpu_ipc_alloc(count * self.esize, C.byref(ptr), handle)
             if rc:
-                raise RuntimeError(f"mfftgpu_ipc_alloc failed ({rc})")
-            payload = [bytes(handle)]
+                ok, err = False, f"mfftgpu_ipc_alloc failed ({rc})"
+            else:
+                payload = [bytes(handle)]
         dist.broadcast_object_list(payload, src=root, group=group)
         if self.rank != root:
-            buf = (C.c_char * 64).from_buffer_copy(payload[0])
-            rc = lib.mfftgpu_ipc_open(buf, C.byref(ptr))
-            if rc:
-                raise RuntimeError(f"mfftgpu_ipc_open failed ({rc})")
-        self.ptr = ptr.value
-        self.esize = esize
-        self.tensor = None
-        if self.rank == root:
-            self.tensor = torch.as_tensor(_DeviceArray(self.ptr, count, self._TYPESTR[dtype]),
-                                          device="cuda")
+            if payload[0] is None:
+                ok, err = False, "the root rank could not allocate the shared output"
+            else:
+                buf = (C.c_char * 64).from_buffer_copy(payload[0])
+                rc = lib.mfftgpu_ipc_open(buf, C.byref(ptr))
+                if rc:
+                    ok, err = False, f"mfftgpu_ipc_open failed ({rc})"
+        self.ptr = ptr.value if ok else None
+        oks = [None] * dist.get_world_size(group)
+        dist.all_gather_object(oks, ok, group=group)
+        if not all(oks):
+            self._release()
+            raise RuntimeError(err or "the shared output could not be mapped on another rank")
+
+    @property
+    def tensor(self):
+        """The whole buffer as a flat tensor on the root (None elsewhere)."""
+        if self.rank != self.root or self.ptr is None:
+            return None
+        if self._tensor is None:
+            import torch
+            self._tensor = torch.as_tensor(
+                _DeviceArray(self.ptr, self.count, self._TYPESTR[self.dtype]), device="cuda")
+        return self._tensor
+
+    def _release(self):
+        # mappings are closed on every rank before the root frees the memory
+        import torch.distributed as dist
+        self._tensor = None
+        dist.barrier(group=self.group)
+        if self.rank != self.root and self.ptr is not None:
+            self._lib.mfftgpu_ipc_close(self.ptr)
+        dist.barrier(group=self.group)
+        if self.rank == self.root and self.ptr is not None:
+            self._lib.mfftgpu_ipc_free(self.ptr)
+        self.ptr = None
 
     def close(self):
-        import torch.distributed as dist
-
-        from ._lib import lib
-        if self.ptr is None:
+        if getattr(self, "_closed", False):
             return
-        self.tensor = None
-        dist.barrier(group=self.group)
-        if self.rank != self.root:
-            lib.mfftgpu_ipc_close(self.ptr)
-        dist.barrier(group=self.group)
-        if self.rank == self.root:
-            lib.mfftgpu_ipc_free(self.ptr)
-        self.ptr = None
+        self._closed = True
+        self._release()
 
 
 def sub_ranges(r0: int, r1: int, nsub: int, align: int = 256):

@@ -132,3 +132,97 @@ def test_row_ranges_cover_and_align():
                 assert a % 128 == 0 and (b % 128 == 0 or b == n)
     rs = D.all_ranges(16384, 8)
     assert {b - a for a, b in rs} == {2048}
+
+
+class _FakeIpcLib:
+    """Stand-in for the library's CUDA IPC entry points: fixed device
+    addresses, optional failure codes, and a log of the calls of this rank."""
+
+    def __init__(self, fail_alloc=False, fail_open=False):
+        self.fail_alloc, self.fail_open, self.calls = fail_alloc, fail_open, []
+
+    def mfftgpu_ipc_alloc(self, nbytes, pptr, handle):
+        self.calls.append(("alloc", nbytes))
+        if self.fail_alloc:
+            return 2
+        pptr._obj.value = 0x7000
+        handle[0:8] = b"peer-out"
+        return 0
+
+    def mfftgpu_ipc_open(self, handle, pptr):
+        self.calls.append(("open", bytes(handle[0:8])))
+        if self.fail_open:
+            return 3
+        pptr._obj.value = 0x9000
+        return 0
+
+    def mfftgpu_ipc_close(self, ptr):
+        self.calls.append(("close", ptr))
+        return 0
+
+    def mfftgpu_ipc_free(self, ptr):
+        self.calls.append(("free", ptr))
+        return 0
+
+
+def _peer_worker(rank, world, port, case, errq):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        from mfft_bench_b200 import dist as D
+        lib = _FakeIpcLib(fail_alloc=(case == "alloc" and rank == 0),
+                          fail_open=(case == "open" and rank == 1))
+        if case == "ok":
+            peer = D.PeerOutput(100, "uint16", lib=lib)
+            assert peer.ptr == (0x7000 if rank == 0 else 0x9000)
+            if rank != 0:
+                assert peer.tensor is None
+            peer.close()
+            peer.close()  # a second close is a no-op
+            want = ([("alloc", 200), ("free", 0x7000)] if rank == 0 else
+                    [("open", b"peer-out"), ("close", 0x9000)])
+            assert lib.calls == want, lib.calls
+        else:
+            try:
+                D.PeerOutput(100, "float64", lib=lib)
+            except RuntimeError:
+                pass
+            else:
+                raise AssertionError("a failed setup must raise on every rank")
+            if case == "alloc":
+                want = [("alloc", 800)] if rank == 0 else []
+            else:  # the mapping failed on rank 1: the root frees what it allocated
+                want = [("alloc", 800), ("free", 0x7000)] if rank == 0 else [("open", b"peer-out")]
+            assert lib.calls == want, lib.calls
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent, never hang it
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+@pytest.mark.parametrize("case", ["ok", "alloc", "open"])
+def test_peer_output_setup_and_failures(case):
+    """The shared output of the sharded product: its collective setup and
+    teardown, and that a failed allocation on the root or a failed mapping on
+    another rank makes every rank raise instead of waiting."""
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, case, errq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    msgs = []
+    while not errq.empty():
+        msgs.append(errq.get())
+    assert not alive, "a rank did not finish"
+    assert all(p.exitcode == 0 for p in procs), msgs
