@@ -132,3 +132,53 @@ def test_plan_init_matches_reference(oracle, reflib):
             assert (a is None) == (b is None)
             if a is not None:
                 assert (a.S, a.NB, a.K, a.g, a.nprod) == (b.S, b.NB, b.K, b.g, b.nprod)
+
+
+def test_oracle_vs_reference_unsigned_random(oracle, reflib):
+    """mm_mfft of the restatement against the reference's mm_mfft and
+    mm_limbplane on the reference's own generator, including outputs shorter
+    and longer than 2L+1 limbs.  (The reference plans L = 2, 4, ..., 64.)"""
+    for n, L, seed in ((5, 2, 1), (12, 4, 2), (20, 8, 3), (9, 32, 4), (3, 64, 5)):
+        A, B = reflib.bigmat_rand(n, L, seed), reflib.bigmat_rand(n, L, seed ^ 0xABCDEF)
+        for RL in (2 * L + 1, L, 2 * L + 4):
+            want = reflib.mm_mfft(A, B, n, L, RL)
+            assert np.array_equal(oracle.mm_mfft(A, B, n, L, RL), want), (n, L, RL)
+            assert np.array_equal(reflib.mm_limbplane(A, B, n, L, RL), want), (n, L, RL)
+
+
+def test_sampled_entries_vs_reference(oracle, reflib):
+    """The per-entry checker the full-size GPU tests rely on, against the
+    reference itself: signed entries through conv_mfft + normalize_planes
+    (sign * limb planes, as the reference's signed route does), unsigned
+    through mm_mfft."""
+    rng = np.random.default_rng(11)
+    for n, L in ((16, 4), (24, 16), (10, 32)):  # L the reference plans (powers of two)
+        A, B = oracle.signed_planes(n, L, 21 + n), oracle.signed_planes(n, L, 22 + L)
+        RL = 2 * L + 1
+        cw = reflib.conv_mfft(oracle.signlimb(A, n, L), oracle.signlimb(B, n, L), n, L)
+        want = reflib.normalize_planes(cw, 2 * L - 1, n, RL).reshape(RL, n * n)
+        rows = rng.integers(0, n, 200)
+        cols = rng.integers(0, n, 200)
+        got = oracle.entries(A, B, n, L, True, rows, cols)
+        assert np.array_equal(got, want[:, rows * n + cols]), (n, L)
+        A, B = reflib.bigmat_rand(n, L, 5), reflib.bigmat_rand(n, L, 6)
+        want = reflib.mm_mfft(A, B, n, L).reshape(RL, n * n)
+        got = oracle.entries(A, B, n, L, False, rows, cols)
+        assert np.array_equal(got, want[:, rows * n + cols]), (n, L)
+
+
+def test_oracle_vs_reference_fp64_random(oracle, reflib):
+    """The fp64 embedding's per-entry restatement against the reference's
+    fpx_*_d path on random magnitudes, zeros and signed zeros, several grids."""
+    rng = np.random.default_rng(5)
+    n = 32
+    for fb in (512, 0, 256):
+        A = rng.standard_normal(n * n) * np.exp2(rng.integers(-30, 30, n * n))
+        B = rng.standard_normal(n * n) * np.exp2(rng.integers(-30, 30, n * n))
+        A[::19] = 0.0
+        B[3::11] = -0.0
+        ref, _ = reflib.fp64_gemm(A, B, n, fb)
+        rows = np.repeat(np.arange(n), n)
+        cols = np.tile(np.arange(n), n)
+        got = oracle.fpx64_entries(A, B, n, fb, rows, cols)
+        assert np.array_equal(got.view(np.uint64), ref.view(np.uint64)), fb
