@@ -32,3 +32,25 @@ def test_reference_arm_json_line(method):
     e = line["e2e"]
     assert e["value"] == line["value"] and e["h2d_bytes_per_step"] == 0
     assert e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_under_torchrun_prints_one_line():
+    """Launched the way the multi-GPU runs are (torchrun, world size 2): rank
+    0 alone times the reference and prints the line; rank 1 exits 0 without
+    work or output."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                        "--master-port", str(port), "bench.py", "--impl", "reference",
+                        "--gpus", "2", "--workload", "c2", "--sample-n", "32", "--steps", "1",
+                        "--warmup", "3"],
+                       cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["n_gpus"] == 2
+    assert line["cpu_baseline"]["kind"] == "reference" and line["value"] > 0
