@@ -226,3 +226,62 @@ def test_peer_output_setup_and_failures(case):
         msgs.append(errq.get())
     assert not alive, "a rank did not finish"
     assert all(p.exitcode == 0 for p in procs), msgs
+
+
+def _leaver_worker(rank, world, port, errq, outq):
+    try:
+        sys.path.insert(0, ROOT)
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import datetime
+        import time
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=5))
+        from mfft_bench_b200 import dist as D
+        n = 64
+        ranges = D.all_ranges(n, world, 16)
+        r0, r1 = ranges[rank]
+        full = torch.zeros(n * n, dtype=torch.int16)
+        local = torch.ones((r1 - r0) * n, dtype=torch.int16)
+        D.allgather_rows(local, full, n, ranges)  # step 1: everybody takes part
+        if rank == 1:
+            outq.put("rank 1 left")
+            os._exit(0)  # leaves between steps, with nothing in flight
+        t0 = time.monotonic()
+        try:
+            D.allgather_rows(local, full, n, ranges)  # step 2: rank 1 is gone
+        except Exception as e:  # the collective must end with an error
+            outq.put(f"rank 0 error after {time.monotonic() - t0:.1f}s: {type(e).__name__}")
+            os._exit(0)
+        outq.put("rank 0 completed a collective without its peer")
+        os._exit(0)
+    except Exception as e:
+        errq.put(f"rank {rank}: {type(e).__name__}: {e}")
+        raise
+
+
+def test_rank_that_leaves_ends_the_next_collective_with_an_error():
+    """A rank that leaves between steps: the remaining rank's next exchange
+    step (the B all-gather) ends with an error inside the process group's
+    short timeout instead of waiting for good."""
+    ctx = mp.get_context("spawn")
+    errq, outq = ctx.SimpleQueue(), ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver_worker, args=(r, 2, port, errq, outq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    msgs = []
+    while not outq.empty():
+        msgs.append(outq.get())
+    errs = []
+    while not errq.empty():
+        errs.append(errq.get())
+    assert not alive, "a rank waited for good"
+    assert not errs, errs
+    assert "rank 1 left" in msgs
+    assert any(m.startswith("rank 0 error after") for m in msgs), msgs
