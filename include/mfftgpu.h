@@ -49,7 +49,7 @@ typedef struct {
     long long acc_bound;
     double inv_bound_log2;
     double int8_macs;        /* issued int8 MACs for the whole n x n product */
-    double schoolbook_macs;  /* n^3 * LbA * LbB: the limb-plane schoolbook equivalent */
+    double schoolbook_macs;  /* n^3 * LbA * LbB: a schoolbook over this plan's own digits */
     int pw_kernel;           /* plane-product kernel of the last product: 1 one CTA per
                                 tile, 2 CTA pairs, 3 t-grouped CTA pairs; 0 not run */
     int kind;                /* 0 MFFT; 1 limb-plane schoolbook (NB = 1, no transform:
@@ -58,6 +58,9 @@ typedef struct {
     int balanced;            /* 1: balanced digits in [-2^(b-1), 2^(b-1)) (int64 operands) */
     int half_points;         /* 1: the last product skipped the zero plane products of the
                                 points 0 and NB/2 (int8_macs counts the issued ones) */
+    int wA, wB;              /* bits per entry: magnitude bits, or 16 x limbs (limb mode) */
+    double schoolbook7_macs; /* n^3 * ceil(wA/7) * ceil(wB/7): the useful work of the
+                                product, counted as a schoolbook over 7-bit digits */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -190,11 +193,13 @@ int mfftgpu_fp64(mfftgpu_ctx *ctx, const double *A, const double *B, int n, int 
  * held by each GPU that loads the library until the process exits; n > 256
  * does not fit and returns MFFTGPU_ERR_ARG.  The work is enqueued on
  * `stream` (a cudaStream_t; NULL = legacy default stream) on the current
- * device, and the call waits for that stream to return the status of the
- * device-side checks.  The first call on each device looks up the array's
- * device address; make that first call before any stream capture.  All
- * calls share the one array: calls that overlap on the GPU (other streams,
- * other threads) race and must be serialised by the caller. */
+ * device, and the call is synchronous: it waits for that stream to return
+ * the status of the device-side checks.  The first call on each device
+ * checks the device and looks up the array's device address, once, and
+ * keeps both for the life of the device context (after cudaDeviceReset they
+ * are stale); make that first call before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller. */
 int mfftgpu_mm_i64_noalloc(const int64_t *A, const int64_t *B, int n, uint16_t *out, int RL,
                            void *stream);
 

@@ -32,7 +32,8 @@ class PlanInfo(C.Structure):
                  "dA", "dB", "nW", "nchunk", "njobs", "positions")] + [
         ("acc_bound", C.c_longlong), ("inv_bound_log2", C.c_double),
         ("int8_macs", C.c_double), ("schoolbook_macs", C.c_double), ("pw_kernel", C.c_int),
-        ("kind", C.c_int), ("U", C.c_int), ("balanced", C.c_int), ("half_points", C.c_int)]
+        ("kind", C.c_int), ("U", C.c_int), ("balanced", C.c_int), ("half_points", C.c_int),
+        ("wA", C.c_int), ("wB", C.c_int), ("schoolbook7_macs", C.c_double)]
 
     def as_dict(self):
         return {f: getattr(self, f) for f, _ in self._fields_}

@@ -728,6 +728,9 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->inv_bound_log2 = P.inv_bound_log2;
     o->int8_macs = P.macs_per_elem * (double)P.n_int * P.n_int;
     o->schoolbook_macs = (double)n * n * (double)n * P.LbA * P.LbB;
+    o->wA = P.wA;
+    o->wB = P.wB;
+    o->schoolbook7_macs = (double)n * n * (double)n * ((P.wA + 6) / 7) * ((P.wB + 6) / 7);
     o->pw_kernel = 0;
     o->kind = P.kind;
     o->U = P.U;

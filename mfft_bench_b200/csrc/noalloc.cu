@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/mfftgpu.h"
 #include "kernels.h"
@@ -29,10 +30,46 @@ constexpr size_t kScratchBytes = 32u << 20;  // 32 MiB per device: n <= 256 for 
 static __device__ __align__(256) char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
-// Per device: the device address of g_noalloc_scratch, looked up once with
-// that device current.  In host code g_noalloc_scratch is only a host-side
-// stand-in for the symbol, not a device address.
-char* g_scratch_ptr[kMaxDevices] = {};
+// Per device, set up once with that device current: whether it is an sm_100
+// GPU, its SM count, and the device address of g_noalloc_scratch (in host
+// code g_noalloc_scratch is only a host-side stand-in for the symbol, not a
+// device address).  Filled under g_setup_mutex, so concurrent first calls
+// from several host threads are safe.  The cache assumes the device context
+// lives as long as the process: after cudaDeviceReset the address is stale.
+struct DeviceSetup {
+    bool done = false;
+    int status = 0;  // MFFTB_OK, or the error every later call returns
+    int num_sms = 0;
+    char* scratch = nullptr;
+};
+DeviceSetup g_setup[kMaxDevices];
+std::mutex g_setup_mutex;
+
+int device_setup(int dev, int* num_sms, char** scratch) {
+    using namespace mfftb;
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    DeviceSetup& d = g_setup[dev];
+    if (!d.done) {
+        int major = 0, minor = 0, sms = 0;
+        void* p = nullptr;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            return MFFTB_ERR_CUDA;  // not cached: a later call may try again
+        if (major != 10 || minor != 0) {
+            d.status = MFFTB_ERR_NODEVICE;
+        } else {
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p)
+                return MFFTB_ERR_CUDA;
+            d.scratch = static_cast<char*>(p);
+            d.num_sms = sms;
+        }
+        d.done = true;
+    }
+    *num_sms = d.num_sms;
+    *scratch = d.scratch;
+    return d.status;
+}
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
 
@@ -50,16 +87,9 @@ extern "C" int mfftgpu_mm_i64_noalloc(const int64_t* A, const int64_t* B, int n,
     if (!A || !B || !out || n <= 0 || RL <= 0) return MFFTB_ERR_ARG;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MFFTB_ERR_CUDA;
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return MFFTB_ERR_CUDA;
-    if (prop.major != 10 || prop.minor != 0) return MFFTB_ERR_NODEVICE;
-    if (!g_scratch_ptr[dev]) {
-        void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p)
-            return MFFTB_ERR_CUDA;
-        g_scratch_ptr[dev] = static_cast<char*>(p);
-    }
-    char* scratch = g_scratch_ptr[dev];
+    int num_sms = 0;
+    char* scratch = nullptr;
+    if (int rc0 = device_setup(dev, &num_sms, &scratch)) return rc0;
     cudaStream_t st = static_cast<cudaStream_t>(stream_handle);
 
     Plan P;
@@ -157,7 +187,7 @@ extern "C" int mfftgpu_mm_i64_noalloc(const int64_t* A, const int64_t* B, int n,
     L.ldo = n_int;
     L.err = err;
     L.timeout_ns = 4000000000ull;
-    L.num_sms = prop.multiProcessorCount;
+    L.num_sms = num_sms;
     if ((rc = pointwise_launch(L, st))) return rc;
 
     InvArgs ia{};

@@ -115,6 +115,8 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
             p.b = b;
             p.LbA = mode == PLAN_LIMB ? wA : (wA + b - 1) / b;
             p.LbB = mode == PLAN_LIMB ? wB : (wB + b - 1) / b;
+            p.wA = mode == PLAN_LIMB ? 16 * wA : wA;
+            p.wB = mode == PLAN_LIMB ? 16 * wB : wB;
             p.S = S;
             if (S > 2 * (p.LbA > p.LbB ? p.LbA : p.LbB) && S > 1) continue;
             if (!fill(p)) continue;
@@ -154,6 +156,8 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* out, int balanc
         // balanced digits of a W-bit two's complement value: ceil((W+1)/b)
         p.LbA = bal ? (wA + b) / b : (wA + b - 1) / b;
         p.LbB = bal ? (wB + b) / b : (wB + b - 1) / b;
+        p.wA = wA;
+        p.wB = wB;
         p.positions = p.LbA + p.LbB - 1;
         p.NB = 1;
         p.K = (p.positions + 3) / 4 * 4;

@@ -33,6 +33,8 @@ struct Plan {
     int mode;       // PlanMode
     int b;          // digit bits (16 in PLAN_LIMB)
     int LbA, LbB;   // digits (coefficients) per entry of A / B
+    int wA, wB;     // bits per entry of A / B: magnitude bits (PLAN_VALUE),
+                    // 16 x limbs (PLAN_LIMB)
     int S, NB, K, g;
     int ncA, ncB;   // nonzero input blocks of A / B
     int dA, dB;     // int8 digits per transformed value
