@@ -108,7 +108,9 @@ int mfftgpu_ipc_free(void *ptr);
  * stage 1 (forward transform): 0 auto, 1 the generic kernel;
  * stage 2 (plane products): 0 auto, 1 one CTA per tile, 2 CTA pairs,
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
- * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel. */
+ * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel,
+ *   2 the lane kernel wherever it covers the plan (also NB*K <= 64 plans,
+ *   which auto gives the register kernel). */
 int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
 /* At the evaluation points 0 and NB/2 the transformed blocks keep only their
  * low K/2 coefficients, so three quarters of those points' plane products

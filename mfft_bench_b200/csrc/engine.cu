@@ -59,7 +59,8 @@ struct mfftgpu_ctx {
     int pw_variant = 0;           // pointwise kernel: 0 auto, 1 single CTA, 2 CTA pairs, 3 grouped
     int wave_sync = 1;            // wave alignment of the t-grouped kernel
     int half_points = 1;          // skip the zero terms of points 0 and NB/2 (t-grouped kernel)
-    int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel
+    int inv_variant = 0;          // inverse kernel: 0 auto, 1 generic shared-memory kernel,
+                                  // 2 the lane kernel wherever it covers the plan
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
@@ -622,7 +623,7 @@ int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
         C->pw_variant = variant;
         return MFFTB_OK;
     }
-    if (stage == 3 && variant >= 0 && variant <= 1) {
+    if (stage == 3 && variant >= 0 && variant <= 2) {
         C->inv_variant = variant;
         return MFFTB_OK;
     }

@@ -654,7 +654,7 @@ static int try_lane(const InvArgs& a, cudaStream_t stream) {
     if (invl_seg(a.positions, a.K, a.b) * a.K < a.positions) return MFFTB_ERR_UNSUPPORTED;
 #define INVL_CASE(nb, k) \
     if (a.NB == nb && a.K == k) return launch_lane<nb, k>(a, stream);
-    INVL_CASE(16, 8) INVL_CASE(32, 8)
+    INVL_CASE(8, 8) INVL_CASE(16, 8) INVL_CASE(32, 8)
     INVL_CASE(4, 16) INVL_CASE(8, 16) INVL_CASE(16, 16) INVL_CASE(32, 16)
     INVL_CASE(4, 32) INVL_CASE(8, 32) INVL_CASE(16, 32) INVL_CASE(32, 32)
 #undef INVL_CASE
@@ -681,6 +681,10 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if ((a.out_kind == INV_F32 || a.out_kind == INV_F64) &&
         (long long)a.positions * a.b + 96 > 32LL * INV_MAXW)
         return MFFTB_ERR_UNSUPPORTED;
+    if (a.variant == 2) {  // the lane kernel first where it covers the plan
+        const int rc = try_lane(a, stream);
+        if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
+    }
     if (a.positions <= (a.NB + 1) * a.S) {
         if (a.NB == 8 && a.K == 8) return launch_reg<8, 8>(a, stream);
         if (a.NB == 4 && a.K == 4) return launch_reg<4, 4>(a, stream);

@@ -10,7 +10,8 @@ integers, N(0,1)*2^k floats and doubles) come from the oracle's generators or
 a seeded numpy generator and are stored in the fixture next to the outputs.
 
 Run from the repository root:  python tests/golden/make_golden.py [--big]
-(--big adds the n=1024 W=256 unsigned digest, ~100 s of reference CPU time).
+(--big adds the n=1024 W=256 digests, unsigned through mm_mfft and signed
+through conv_mfft + normalize_planes, ~100 s of reference CPU time each).
 """
 import argparse
 import json
@@ -56,6 +57,21 @@ def signed_case(r, o, n, L, kind):
     return {"n": n, "L": L, "RL": 2 * L + 1, "digest": f"{o.digest(out):016x}"}
 
 
+def signed_digest_case(r, o, n, L):
+    """configs[1]'s signed W=16L product, whole output, digest only: the
+    reference's signed route (sign-limb int32 planes -> conv_mfft ->
+    normalize_planes, two's complement output; src/mfft.c:302-422,
+    src/bigmat.c:48-60)."""
+    A, B = o.signed_planes(n, L, SEED_A), o.signed_planes(n, L, SEED_B)
+    A32, B32 = o.signlimb(A, n, L), o.signlimb(B, n, L)
+    t0 = time.time()
+    cw = r.conv_mfft(A32, B32, n, L)
+    out = r.normalize_planes(cw, 2 * L - 1, n, 2 * L + 1)
+    dt = time.time() - t0
+    return {"n": n, "L": L, "RL": 2 * L + 1, "digest": f"{o.digest(out):016x}",
+            "ref_seconds": round(dt, 4), "full": False}
+
+
 def fp32_case(r, o, n, force_bits):
     A, B = o.normal_f32(n, SEED_A)
     C, (L, SA, SB) = r.fp32_gemm(A, B, n, force_bits)
@@ -94,6 +110,8 @@ def main():
         meta["unsigned"].append(unsigned_case(r, o, 1024, 16, False))
     for n, L, kind in ((32, 4, "int64"), (64, 4, "int64"), (48, 16, "planes")):
         meta["signed"].append(signed_case(r, o, n, L, kind))
+    if args.big:
+        meta["signed"].append(signed_digest_case(r, o, 1024, 16))
     for n, fb in ((64, 512), (64, 0), (96, 512)):
         meta["fp32"].append(fp32_case(r, o, n, fb))
     # fp64: the 512-bit grid, the adaptive grid, and an adaptive case whose
@@ -107,10 +125,11 @@ def main():
         with open(path) as f:
             old = json.load(f)
     # keep a previously recorded --big digest when re-running without --big
-    have = {(c["n"], c["L"]) for c in meta["unsigned"]}
-    for c in old.get("unsigned", []):
-        if (c["n"], c["L"]) not in have:
-            meta["unsigned"].append(c)
+    for kind in ("unsigned", "signed"):
+        have = {(c["n"], c["L"]) for c in meta[kind]}
+        for c in old.get(kind, []):
+            if (c["n"], c["L"]) not in have:
+                meta[kind].append(c)
     with open(path, "w") as f:
         json.dump(meta, f, indent=1)
     print(json.dumps(meta, indent=1))

@@ -2,9 +2,11 @@
 
 Full CPU runs of the reference are infeasible beyond n = 1024 (hours), so
 full-size parity uses size-independent properties and sampled entries:
-* c2 shape: the full n=1024, W=256 unsigned output digest equals the digest of
-  the reference's own mm_mfft output (tests/golden, ~100 s of reference CPU);
-  the signed c2 product is checked on sampled entries and by checksum;
+* c2: the full n=1024, W=256 output digests equal the digests of the
+  reference's own outputs (tests/golden, ~100 s of reference CPU each):
+  unsigned through mm_mfft, signed through its signed route
+  conv_mfft + normalize_planes; the signed product is also checked on
+  sampled entries and by checksum;
 * every row and column sum of C equals A*(B*1) and (1^T A)*B modulo the
   prime 2^61-1, computed from all limbs of every entry (oracle checksum);
 * sampled entries -- including the first/last rows of every 128-row tile
@@ -42,12 +44,15 @@ def test_c2_shape_unsigned_full_digest(ctx, oracle, golden):
     assert f"{oracle.digest(out):016x}" == rec["digest"]
 
 
-def test_c2_signed(ctx, oracle):
-    """n=1024, W=256 signed."""
+def test_c2_signed(ctx, oracle, golden):
+    """n=1024, W=256 signed; the whole output vs the digest of the
+    reference's conv_mfft + normalize_planes on the same inputs."""
     n, L = 1024, 16
     A, B = oracle.signed_planes(n, L, SA), oracle.signed_planes(n, L, SB)
     out = ctx.mm_u16(A, B, n, L, signed=True)
     RL = 2 * L + 1
+    rec = next(c for c in golden["signed"] if c["n"] == n and c["L"] == L)
+    assert f"{oracle.digest(out):016x}" == rec["digest"]
     assert oracle.checksum(A, B, n, L, True, out, RL) == 0
     rows, cols = _sample(n, 1500)
     got = out.reshape(RL, n, n)[:, rows, cols]

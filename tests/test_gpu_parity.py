@@ -136,6 +136,49 @@ def test_forward_kernels_vs_generic(ctx, oracle, n, L, signed):
 
 
 # ---------------------------------------------------------------- the inverse kernels
+@pytest.mark.parametrize("kind,n", [("i64", 256), ("i64", 130), ("f32", 96), ("f32w0", 80),
+                                    ("f64", 72)])
+def test_inverse_lane_kernel_on_small_plans(ctx, oracle, kind, n):
+    """The lane inverse (inverse variant 2) on plans with NB*K <= 64, which
+    the register kernel serves by default: the W=64 (c5 plan NB8 K8), fp32
+    and fp64 products, bit-identical to the register kernel and to the
+    oracle."""
+    def run():
+        if kind == "i64":
+            return ctx.mm_i64(A, B, n, RL=9)
+        if kind == "f64":
+            return ctx.fp64(A, B, n, 512)
+        return ctx.fp32(A, B, n, 0 if kind == "f32w0" else 512)
+    if kind == "i64":
+        A, B = oracle.int64_entries(n, 71), oracle.int64_entries(n, 73)
+    elif kind == "f64":
+        g = np.random.default_rng(n)
+        A = g.standard_normal(n * n) * np.exp2(g.integers(-8, 9, n * n))
+        B = g.standard_normal(n * n) * np.exp2(g.integers(-8, 9, n * n))
+    else:
+        A, B = oracle.normal_f32(n, 79 + n)
+    ref = run()
+    plan = ctx.last_plan()
+    assert plan["NB"] * plan["K"] <= 64
+    ctx.set_kernel_variant("inverse", 2)
+    try:
+        got = run()
+    finally:
+        ctx.set_kernel_variant("inverse", 0)
+    assert np.array_equal(got.view(np.uint8), ref.view(np.uint8))
+    if kind == "i64":
+        rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 1500)]
+        cols = np.tile(np.arange(n), n)[:: max(1, n * n // 1500)]
+        want = oracle.entries(oracle.int64_to_planes(A, n), oracle.int64_to_planes(B, n), n, 4,
+                              True, rows, cols, 9)
+        assert np.array_equal(got.reshape(9, n, n)[:, rows, cols], want)
+    elif kind != "f64":
+        rows = np.repeat(np.arange(n), n)
+        cols = np.tile(np.arange(n), n)
+        want = oracle.fpx_entries(A, B, n, 0 if kind == "f32w0" else 512, rows, cols)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 @pytest.mark.parametrize("n,L,signed", [
     (256, 16, True),    # b4 NB16 K16
     (128, 64, False),   # b8 NB32 K16, 3 digit classes
