@@ -86,7 +86,9 @@ POINTWISE_TRAFFIC = {
 
 PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
               2: "pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)",
-              3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)"}
+              3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)",
+              4: "pointwise_kara_i8_kernel (tcgen05 cta_group::2 kind::i8, Karatsuba: 3 full "
+                 "length-4 convolutions per point)"}
 
 
 def load_peaks():
@@ -775,7 +777,7 @@ def main():
             line["int8_tops_issued"] = 2 * macs / (ms * 1e-3) / 1e12
             line["useful_tops"] = 2 * pi["schoolbook7_macs"] / (ms * 1e-3) / 1e12
             line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs",
-                                               "half_points")}
+                                               "half_points", "kara")}
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share

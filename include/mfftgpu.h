@@ -51,7 +51,8 @@ typedef struct {
     double int8_macs;        /* issued int8 MACs for the whole n x n product */
     double schoolbook_macs;  /* n^3 * LbA * LbB: a schoolbook over this plan's own digits */
     int pw_kernel;           /* plane-product kernel of the last product: 1 one CTA per
-                                tile, 2 CTA pairs, 3 t-grouped CTA pairs; 0 not run */
+                                tile, 2 CTA pairs, 3 t-grouped CTA pairs, 4 Karatsuba
+                                CTA pairs; 0 not run */
     int kind;                /* 0 MFFT; 1 limb-plane schoolbook (NB = 1, no transform:
                                 job t of chunk ch sums A_u B_(t-u), u in [ch*U, ch*U+U)) */
     int U;                   /* schoolbook: digit planes of A per contraction chunk */
@@ -61,6 +62,8 @@ typedef struct {
     int wA, wB;              /* bits per entry: magnitude bits, or 16 x limbs (limb mode) */
     double schoolbook7_macs; /* n^3 * ceil(wA/7) * ceil(wB/7): the useful work of the
                                 product, counted as a schoolbook over 7-bit digits */
+    int kara;                /* 1: Karatsuba pointwise (3 full length-4 convolutions per
+                                point; njobs = NB * 21 job planes) */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -112,6 +115,13 @@ int mfftgpu_ipc_free(void *ptr);
  *   2 the lane kernel wherever it covers the plan (also NB*K <= 64 plans,
  *   which auto gives the register kernel). */
 int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
+/* Karatsuba pointwise, on = 1 (the default, or $MFFTGPU_KARA): plans with
+ * K = 8 and one int8 digit whose sums a0 + a1 still fit int8 (the W = 64
+ * configuration) take each point's ring product as three full convolutions
+ * of length 4, P0 = a0 b0, P1 = a1 b1, P2 = (a0 + a1)(b0 + b1) with
+ * a = a0 + y^4 a1: 48 plane products per point instead of 64, 16 at the
+ * points 0 and NB/2.  Results are identical either way. */
+int mfftgpu_set_karatsuba(mfftgpu_ctx *ctx, int on);
 /* At the evaluation points 0 and NB/2 the transformed blocks keep only their
  * low K/2 coefficients, so three quarters of those points' plane products
  * are zero; on = 1 (the default, or $MFFTGPU_HALF_POINTS) lets the t-grouped
@@ -220,8 +230,10 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * the given job shape, the kernel's int32 job planes compared element by
  * element with a CUDA-core evaluation of the same job table.  variant: 0 the
  * product path's choice, 1 one CTA per 128-row tile, 2 CTA pairs (256-row
- * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs.  *mismatches receives
- * the number of differing elements. */
+ * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs, 4 the Karatsuba job
+ * table (K = 8, one digit, one chunk: NB * 12 operand planes per side, NB * 21
+ * job planes) on its CTA-pair kernel.  *mismatches receives the number of
+ * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,
                                long long *mismatches);

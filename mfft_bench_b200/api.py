@@ -125,6 +125,10 @@ class Context:
         at the evaluation points 0 and NB/2; identical results."""
         self._check(lib.mfftgpu_set_half_points(self._h, int(bool(on))), "set_half_points")
 
+    def set_karatsuba(self, on):
+        """Karatsuba pointwise on plans that allow it (default on); same bits."""
+        self._check(lib.mfftgpu_set_karatsuba(self._h, int(bool(on))), "set_karatsuba")
+
     def set_kernel_variant(self, stage, variant):
         """Pick the kernel of a stage ('forward', 'pointwise' or 'inverse'; 0 = auto).
         Every variant computes the same bits; this is for comparisons."""

@@ -63,13 +63,14 @@ struct mfftgpu_ctx {
                                   // 2 the lane kernel wherever it covers the plan
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
+    int kara = 1;                 // Karatsuba pointwise where the plan allows it
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
     bool b_valid = false;
     const void* b_ptr = nullptr;
     int b_fmt = -1, b_n = 0, b_b = 0, b_Lb = 0, b_S = 0, b_NB = 0, b_dB = 0, b_lo = 0, b_sgrid = 0,
-        b_trunc = 0, b_kind = 0;
+        b_trunc = 0, b_kind = 0, b_kara = 0;
     Plan last_plan{};
     bool have_plan = false;
     int last_pw_kernel = 0;
@@ -145,8 +146,14 @@ int log2i(int x) {
     return r;
 }
 
-int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& B,
+int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operand& B,
                 int row_begin, int row_end, const OutSpec& O) {
+    Plan P = plan;
+    // the Karatsuba pointwise runs on 256-row CTA-pair tiles with the default
+    // kernels of the other stages
+    if (P.kara && (C->inv_variant != 0 || C->pw_variant != 0 || P.n_int < 128 ||
+                   row_end - row_begin < 256 || C->num_sms < 2))
+        plan_set_kara(P, false);
     const int n_int = P.n_int;
     const int dbytes = plan_digit_bytes(P);
     const long long nn_int = (long long)n_int * n_int;
@@ -155,20 +162,31 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     // schoolbook plans multiply the digit planes themselves: no transform,
     // no F stack, no A-hat planes
     const bool school = P.kind == KIND_SCHOOL;
-    const int fpl = school ? 0 : P.NB * P.dB * (2 * P.K - 1);
-    const int apl = school ? 0 : P.NB * P.dA * P.K;
-    const size_t szDB = align256((size_t)P.LbB * nn_int * dbytes);
-    const size_t szF = align256((size_t)fpl * nn_int);
-    const size_t per_row = (size_t)n_int * ((size_t)P.LbA * dbytes + apl + 4 * (size_t)P.njobs);
-    size_t limit = C->ws_limit;
+    int fpl = 0, apl = 0;
+    size_t szDB = 0, szF = 0, per_row = 0;
+    long long R = 0;
+    const size_t limit = C->ws_limit;
     const int rows_pad = (rows + 15) / 16 * 16;
-    long long R;
-    if (limit > szDB + szF + per_row * 128)
-        R = (long long)((limit - szDB - szF) / per_row) / 128 * 128;
-    else
-        R = 128;
-    if (R > rows_pad) R = rows_pad;
-    if (R < 16) R = 16;
+    // row block R from the workspace limit: B's digit planes and operand
+    // planes whole, A's digit and operand planes and the job planes per row
+    auto size_blocks = [&]() {
+        fpl = school ? 0 : (P.kara ? P.NB * PWK_OPS : P.NB * P.dB * (2 * P.K - 1));
+        apl = school ? 0 : (P.kara ? P.NB * PWK_OPS : P.NB * P.dA * P.K);
+        szDB = align256((size_t)P.LbB * nn_int * dbytes);
+        szF = align256((size_t)fpl * nn_int);
+        per_row = (size_t)n_int * ((size_t)P.LbA * dbytes + apl + 4 * (size_t)P.njobs);
+        if (limit > szDB + szF + per_row * 128)
+            R = (long long)((limit - szDB - szF) / per_row) / 128 * 128;
+        else
+            R = 128;
+        if (R > rows_pad) R = rows_pad;
+        if (R < 16) R = 16;
+    };
+    size_blocks();
+    if (P.kara && R < 256) {  // every row block's tiles read 256 rows of each plane
+        plan_set_kara(P, false);
+        size_blocks();
+    }
     const size_t szDA = align256((size_t)P.LbA * R * n_int * dbytes);
     const size_t szAh = align256((size_t)apl * R * n_int);
     const size_t szAcc = align256((size_t)P.njobs * R * n_int * 4);
@@ -180,7 +198,8 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
                           C->b_fmt == B.fmt &&
                           C->b_n == P.n && C->b_b == P.b && C->b_Lb == P.LbB && C->b_S == P.S &&
                           C->b_NB == P.NB && C->b_dB == P.dB && C->b_lo == B.lo_bit &&
-                          C->b_sgrid == B.S_grid && C->b_trunc == B.trunc_rel;
+                          C->b_sgrid == B.S_grid && C->b_trunc == B.trunc_rel &&
+                          C->b_kara == P.kara;
     char* DB = C->ws;
     int8_t* F = reinterpret_cast<int8_t*>(DB + szDB);
     char* DA = DB + szDB + szF;
@@ -243,7 +262,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
     fb.d = P.dB;
     fb.lgS = log2i(P.S);
     fb.lgK = log2i(P.K);
-    fb.f_stack = 1;
+    fb.f_stack = P.kara ? 2 : 1;
     fb.out = F;
     fb.oplane = nn_int;
     fb.err = C->d_err;
@@ -274,6 +293,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         C->b_lo = B.lo_bit;
         C->b_sgrid = B.S_grid;
         C->b_trunc = B.trunc_rel;
+        C->b_kara = P.kara;
     }
 
     // ---- A row blocks
@@ -306,7 +326,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         fa.nelem = (long long)rb * n_int;
         fa.nc = P.ncA;
         fa.d = P.dA;
-        fa.f_stack = 0;
+        fa.f_stack = P.kara ? 2 : 0;
         fa.out = Ah;
         fa.oplane = R * n_int;
         if (!school) {
@@ -329,7 +349,9 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         L.cols = n_int;
         L.kdim = n_int;
         L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs, school ? 1 : 0, P.LbA, P.LbB, P.U,
-                        P.NB, (!school && C->half_points && P.K == 2 * P.S) ? P.S : 0};
+                        P.NB, (!school && !P.kara && C->half_points && P.K == 2 * P.S) ? P.S : 0,
+                        P.kara};
+        L.map_rows = (int)std::max<long long>(rb, 256);
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
         L.out = acc;
         L.out_plane = R * n_int;
@@ -380,6 +402,7 @@ int run_product(mfftgpu_ctx* C, const Plan& P, const Operand& A, const Operand& 
         ia.LbA = P.LbA;
         ia.LbB = P.LbB;
         ia.U = P.U;
+        ia.kara = P.kara;
         tick(3);
         if ((rc = inverse_launch(ia, st))) return set_err(C, rc, "inverse launch failed (%d)", rc);
         ++C->launches;
@@ -411,6 +434,7 @@ int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P,
     if (rc)
         return set_err(C, MFFTB_ERR_PLAN, "no exact int8 plan for n=%d mode=%d widths %d/%d", n,
                        mode, wA, wB);
+    plan_set_kara(*P, C->kara != 0);
     return MFFTB_OK;
 }
 
@@ -510,6 +534,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
+    if (const char* s = getenv("MFFTGPU_KARA")) C->kara = atoi(s) != 0;
     cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
@@ -617,6 +642,12 @@ int mfftgpu_set_half_points(mfftgpu_ctx* C, int on) {
     return MFFTB_OK;
 }
 
+int mfftgpu_set_karatsuba(mfftgpu_ctx* C, int on) {
+    if (!C) return MFFTB_ERR_ARG;
+    C->kara = on != 0;
+    return MFFTB_OK;
+}
+
 int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
     if (!C) return MFFTB_ERR_ARG;
     if (stage == 2 && variant >= 0 && variant <= 3) {
@@ -687,6 +718,8 @@ int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o)
         if (plan_search_school(n, wA, wB, 0, &P, mode == 3)) return MFFTB_ERR_PLAN;
     } else if (plan_search(n, mode, wA, wB, 0, 0, &P)) {
         return MFFTB_ERR_PLAN;
+    } else {
+        plan_set_kara(P, true);  // the default context setting
     }
     fill_info(P, o);
     return MFFTB_OK;
@@ -732,6 +765,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->wA = P.wA;
     o->wB = P.wB;
     o->schoolbook7_macs = (double)n * n * (double)n * ((P.wA + 6) / 7) * ((P.wB + 6) / 7);
+    o->kara = P.kara;
     o->pw_kernel = 0;
     o->kind = P.kind;
     o->U = P.U;
@@ -1050,12 +1084,23 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     cudaSetDevice(C->device);
     const int ld = (kdim + 15) / 16 * 16;
     PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
-    if (C->half_points && K % 2 == 0) {
+    // variant 4: the Karatsuba kernel (K = 8, one digit, one chunk) on random
+    // operand planes, NB * 12 per side; A planes span at least 256 rows
+    const bool kara = variant == 4;
+    if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
+        return MFFTB_ERR_ARG;
+    const int arows = kara ? std::max(rows, 256) : rows;
+    if (kara) {
+        J.NB = NB;
+        J.kara = 1;
+        J.njobs = NB * PWK_JOBS;
+    } else if (C->half_points && K % 2 == 0) {
         J.NB = NB;
         J.zpS = K / 2;
     }
-    const int apl = NB * dA * K, fpl = NB * dB * (2 * K - 1);
-    const size_t szA = align256((size_t)apl * rows * ld), szF = align256((size_t)fpl * cols * ld);
+    const int apl = kara ? NB * PWK_OPS : NB * dA * K;
+    const int fpl = kara ? NB * PWK_OPS : NB * dB * (2 * K - 1);
+    const size_t szA = align256((size_t)apl * arows * ld), szF = align256((size_t)fpl * cols * ld);
     const size_t szO = align256((size_t)J.njobs * rows * cols * 4);
     int rc = ensure(C, &C->ws, &C->ws_bytes, szA + szF + szO + 256);
     if (rc) return rc;
@@ -1069,6 +1114,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     gen_u16_kernel<<<C->num_sms * 4, 256, 0, C->stream>>>(reinterpret_cast<uint16_t*>(A),
                                                           (long long)(szA + szF) / 2, 0x5EEDull);
     CUDA_OK(cudaGetLastError());
+    if (kara && (long long)kdim * 4 * 16384LL > 2147483647LL) return MFFTB_ERR_ARG;
     if (J.zpS > 0) {
         // operands as a forward transform leaves them: at j = 0 and j = NB/2
         // Ahat[c] = Bhat[c] = 0 for c >= K/2, i.e. F planes [0, K/2) and
@@ -1090,7 +1136,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     PwLaunch L{};
     L.A = A;
     L.lda = ld;
-    L.a_plane_bytes = (long long)rows * ld;
+    L.a_plane_bytes = (long long)arows * ld;
     L.a_planes = apl;
     L.F = F;
     L.ldf = ld;
@@ -1100,6 +1146,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.cols = cols;
     L.kdim = kdim;
     L.jobs = J;
+    L.map_rows = arows;
     L.block_n = block_n;
     L.out = out;
     L.out_plane = (long long)rows * cols;
@@ -1107,7 +1154,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.err = C->d_err;
     L.timeout_ns = C->timeout_ns;
     L.num_sms = C->num_sms;
-    L.variant = variant;
+    L.variant = kara ? 0 : variant;
     L.wave_counter = reinterpret_cast<unsigned int*>(C->d_err + 32);
     if ((rc = pointwise_launch(L, C->stream))) return set_err(C, rc, "pointwise launch failed");
     if ((rc = pointwise_check_launch(L, mism, dcnt, C->stream))) return rc;

@@ -19,7 +19,9 @@
 // forward_kernel (the rest: K = 64, wide digits) reads the digits through L1
 // and spreads the evaluation points over gridDim.y when the operand is small.
 // For B they write the F stack the pointwise kernel expects:
-// F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].
+// F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].  In Karatsuba mode
+// (f_stack = 2, one digit) both operands are written as K + S planes per
+// point: Xhat[0..K-1], then Xhat[c] + Xhat[c+S] for c < S.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -71,6 +73,38 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
     // gridDim.y so that every SM gets work
     for (int j = blockIdx.y; j < a.NB; j += gridDim.y) {
         const int step = (a.g * j) & mask2K;
+        if (a.f_stack == 2) {
+            // Karatsuba operands (one digit): planes x[c], then x[c] + x[c+S]
+            auto coef = [&](int c, int (&x)[4]) {
+                x[0] = x[1] = x[2] = x[3] = 0;
+                int e = 0;
+                for (int beta = 0; beta < a.nc; ++beta, e = (e + step) & mask2K) {
+                    int r = (c - e) & mask2K;
+                    int sgn = 1;
+                    if (r >= a.K) {
+                        r -= a.K;
+                        sgn = -1;
+                    }
+                    if (r >= a.S) continue;
+                    const int m = (beta << a.lgS) + r;
+                    if (m >= a.Lb) continue;
+                    int v[4];
+                    load4<DB>(a.D, (long long)m * a.dplane + e0, v);
+                    for (int q = 0; q < 4; ++q) x[q] += sgn * v[q];
+                }
+            };
+            const long long base = (long long)j * (a.K + a.S);
+            for (int c = 0; c < a.S; ++c) {
+                int lo[4], hi[4];
+                coef(c, lo);
+                coef(c + a.S, hi);
+                store4(a.out + (base + c) * a.oplane + e0, lo[0], lo[1], lo[2], lo[3]);
+                store4(a.out + (base + c + a.S) * a.oplane + e0, hi[0], hi[1], hi[2], hi[3]);
+                store4(a.out + (base + a.K + c) * a.oplane + e0, lo[0] + hi[0], lo[1] + hi[1],
+                       lo[2] + hi[2], lo[3] + hi[3]);
+            }
+            continue;
+        }
         for (int c = 0; c < a.K; ++c) {
             int x[4] = {0, 0, 0, 0};
             int e = 0;  // g * j * beta mod 2K
@@ -140,6 +174,33 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
                     : 0u;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
+        if (a.f_stack == 2) {
+            // Karatsuba operands: x[0..S-1], x[S..K-1], x[c] + x[c+S]
+            uint32_t xs[K];
+#pragma unroll
+            for (int c = 0; c < K; ++c) {
+                uint32_t x = 0;
+#pragma unroll
+                for (int beta = 0; beta < NBLK; ++beta) {
+                    const int e = (G * j * beta) % TWO_K;
+                    int r = ((c - e) % TWO_K + TWO_K) % TWO_K;
+                    const bool neg = r >= K;
+                    if (neg) r -= K;
+                    if (r < S)
+                        x = neg ? __vsub4(x, dg[beta * S + r]) : __vadd4(x, dg[beta * S + r]);
+                }
+                xs[c] = x;
+            }
+            const long long base = (long long)j * (K + S);
+#pragma unroll
+            for (int c = 0; c < K; ++c)
+                *reinterpret_cast<uint32_t*>(a.out + (base + c) * a.oplane + e0) = xs[c];
+#pragma unroll
+            for (int c = 0; c < S; ++c)
+                *reinterpret_cast<uint32_t*>(a.out + (base + K + c) * a.oplane + e0) =
+                    __vadd4(xs[c], xs[c + S]);
+            continue;
+        }
 #pragma unroll
         for (int c = 0; c < K; ++c) {
             uint32_t x = 0;
@@ -312,6 +373,8 @@ static int launch_simd(const FwdArgs& a, cudaStream_t stream) {
 
 int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     if (a.nelem % 4 || a.d < 1 || a.d > 4) return MFFTB_ERR_ARG;
+    // Karatsuba operands: one int8 digit per value, blocks of S = K/2
+    if (a.f_stack == 2 && (a.d != 1 || 2 * a.S != a.K)) return MFFTB_ERR_ARG;
     const int threads = 256;
     long long blocks = (a.nelem / 4 + threads - 1) / threads;
     if (blocks <= 0) return MFFTB_OK;
@@ -329,7 +392,8 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     }
     // one point per warp with int16 lanes when every partial sum fits them:
     // |sum| <= nc * 2^b < 2^15
-    if (a.variant == 0 && (a.dbytes == 1 || a.dbytes == 2) && 2 * a.S == a.K && a.b >= 1 &&
+    if (a.variant == 0 && a.f_stack != 2 && (a.dbytes == 1 || a.dbytes == 2) && 2 * a.S == a.K &&
+        a.b >= 1 &&
         a.b <= 14 && ((long long)a.nc << a.b) < 32768 && a.NB >= 1 && a.nelem % 4 == 0) {
         if (a.K == 8) return launch_pt<8>(a, stream);
         if (a.K == 16) return launch_pt<16>(a, stream);

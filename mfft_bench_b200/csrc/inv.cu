@@ -218,6 +218,40 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
         return LGNB == 1 ? j : (LGNB == 2 ? (((j & 1) << 1) | (j >> 1))
                                           : (((j & 1) << 2) | (j & 2) | (j >> 2)));
     };
+    if constexpr (K == 8) {
+        if (a.kara) {
+            // Chat_j = P0 - P1 + y^4 (P2 - P0 - P1) mod y^8 + 1, with
+            // M = P2 - P0 - P1: Chat[t] = D[t] - M[t+4] (t < 3), D[3] (t = 3),
+            // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1
+#pragma unroll
+            for (int j = 0; j < NB; ++j) {
+                const int32_t* src = a.acc + (long long)j * 21 * a.acc_plane + e;
+                int64_t P0[7];
+#pragma unroll
+                for (int s = 0; s < 7; ++s) P0[s] = __ldg(src + (long long)s * a.acc_plane);
+                if (j == 0 || 2 * j == NB) {  // half point: P0 only
+#pragma unroll
+                    for (int t = 0; t < 7; ++t) x[bitrev(j)][t] = P0[t];
+                    x[bitrev(j)][7] = 0;
+                    continue;
+                }
+                int64_t P1[7], M[7];
+#pragma unroll
+                for (int s = 0; s < 7; ++s) P1[s] = __ldg(src + (long long)(7 + s) * a.acc_plane);
+#pragma unroll
+                for (int s = 0; s < 7; ++s)
+                    M[s] = (int64_t)__ldg(src + (long long)(14 + s) * a.acc_plane) - P0[s] - P1[s];
+                int64_t(&y)[K] = x[bitrev(j)];
+#pragma unroll
+                for (int t = 0; t < 3; ++t) y[t] = P0[t] - P1[t] - M[t + 4];
+                y[3] = P0[3] - P1[3];
+#pragma unroll
+                for (int t = 4; t < 7; ++t) y[t] = P0[t] - P1[t] + M[t - 4];
+                y[7] = M[3];
+            }
+            goto loaded;
+        }
+    }
     if (a.nW == 1 && a.nchunk == 1) {
         int32_t raw[NB * K];
 #pragma unroll
@@ -244,6 +278,7 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
             }
         }
     }
+loaded:
     // DIT stages with W = omega^-1 = y^-g
 #pragma unroll
     for (int len = 2; len <= NB; len <<= 1) {
@@ -673,6 +708,14 @@ static int school_carry_launch(const InvArgs& a, cudaStream_t stream);
 
 int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if (a.school) return school_carry_launch(a, stream);
+    if (a.kara) {
+        if (a.K != 8 || a.nW != 1 || a.nchunk != 1 || a.positions > (a.NB + 1) * a.S)
+            return MFFTB_ERR_ARG;
+        if (a.NB == 8) return launch_reg<8, 8>(a, stream);
+        if (a.NB == 4) return launch_reg<4, 8>(a, stream);
+        if (a.NB == 2) return launch_reg<2, 8>(a, stream);
+        return MFFTB_ERR_ARG;
+    }
     const int NK = a.NB * a.K;
     if (a.elems < 1 || a.elems > 32 || NK * a.elems > INV_VPT * INV_THREADS) return MFFTB_ERR_ARG;
     if ((1 << a.log2NB) != a.NB || (1 << a.lgS) != a.S || (1 << a.lgK) != a.K ||

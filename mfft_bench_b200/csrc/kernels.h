@@ -45,7 +45,8 @@ struct FwdArgs {
     long long nelem;   // elements per plane to transform (rows * ld), multiple of 4
     int S, NB, K, g, nc, d;
     int lgS, lgK;      // log2 of S and K (all plan sizes are powers of two)
-    int f_stack;       // 0: write Ahat [j][da][c]; 1: write F [j][db][r] (2K-1 planes)
+    int f_stack;       // 0: write Ahat [j][da][c]; 1: write F [j][db][r] (2K-1 planes);
+                       // 2: Karatsuba operands [j][K + S]: Xhat[c], then Xhat[c] + Xhat[c+S]
     int8_t* out;
     long long oplane;  // bytes per output plane
     int* err;
@@ -85,6 +86,12 @@ struct InvArgs {
     // of C_t = sum_u A_u B_(t-u); planes of jobs without terms are not read
     int school;
     int LbA, LbB, U;
+    // Karatsuba mode (K = 8, one digit class, one chunk): acc holds 21 job
+    // planes per point j, q = j*21 + p*7 + s, coefficient s of the full
+    // convolutions P0 = a0*b0, P1 = a1*b1, P2 = (a0+a1)*(b0+b1) (a = a0 +
+    // y^4 a1); the half points (j = 0, NB/2) hold P0 only.  Only the register
+    // kernel reads this layout.
+    int kara;
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);
 

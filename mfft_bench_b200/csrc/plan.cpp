@@ -131,6 +131,30 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
     return 0;
 }
 
+bool plan_kara_ok(const Plan& p) {
+    if (p.kind != KIND_MFFT || p.mode != PLAN_VALUE || p.K != 8 || p.S != 4 || p.dA != 1 ||
+        p.dB != 1 || p.nchunk != 1 || p.NB < 2 || p.NB > 8)
+        return false;
+    const long long sa = 2LL * p.boundA[0], sb = 2LL * p.boundB[0];
+    if (sa > 127 || sb > 127) return false;
+    return 4LL * p.n_int * sa * sb <= 2147483647LL;
+}
+
+void plan_set_kara(Plan& p, bool on) {
+    if (on && !plan_kara_ok(p)) on = false;
+    p.kara = on ? 1 : 0;
+    const double S2 = (double)p.S * p.S;
+    const double pts = p.NB <= 2 ? 0.0 : (double)p.NB - 2.0;  // ordinary points
+    const double half = p.NB <= 2 ? (double)p.NB : 2.0;
+    if (on) {
+        p.njobs = p.NB * 21;
+        p.macs_per_elem = (3.0 * S2 * pts + S2 * half) * p.n_int;
+    } else {
+        p.njobs = p.NB * p.K * p.nW * p.nchunk;
+        p.macs_per_elem = (double)p.NB * p.K * p.K * p.dA * p.dB * p.n_int;
+    }
+}
+
 int plan_search_school(int n, int wA, int wB, int force_b, Plan* out, int balanced_ok) {
     if (n <= 0 || wA <= 0 || wB <= 0 || !out) return 1;
     if (force_b > 8 || (force_b == 8 && !balanced_ok)) return 1;

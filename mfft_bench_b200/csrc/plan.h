@@ -54,6 +54,11 @@ struct Plan {
     // x + sum_i 2^(b*i + b-1), minus 2^(b-1), so digits lie in
     // [-2^(b-1), 2^(b-1)) and b = 8 still fits int8
     int balanced;
+    // Karatsuba pointwise (KIND_MFFT, K = 8): each point's ring product is
+    // three full convolutions of length S = 4 instead of the K^2 negacyclic
+    // terms -- 48 plane products per point, 16 at the half points; njobs is
+    // then the NB * 21 job planes, macs_per_elem the issued MACs
+    int kara;
 };
 
 // Returns 0 and fills *p on success.  wA / wB: magnitude bits per entry in
@@ -71,6 +76,13 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
 // balanced_ok: the operands are two's complement int64 entries, which may use
 // balanced 8-bit digits (ceil((W+1)/8) of them).
 int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced_ok = 0);
+// Whether the Karatsuba pointwise keeps the plan exact: one int8 digit per
+// transformed value with room for the sums a0 + a1 (2 |x| <= 127), K = 8,
+// one contraction chunk, and every int32 accumulator of P2 = (a0+a1)(b0+b1)
+// (4 terms of length n) below 2^31.
+bool plan_kara_ok(const Plan& p);
+// Switch a plan to / from the Karatsuba pointwise (job planes and issued MACs).
+void plan_set_kara(Plan& p, bool on);
 // Whether job (t, ch) of a schoolbook plan has any term.
 inline bool school_job_live(const Plan& p, int t, int ch) {
     const int lo = t - (p.LbB - 1) > ch * p.U ? t - (p.LbB - 1) : ch * p.U;

@@ -917,6 +917,252 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
     if (warp == 1) tmem_dealloc_pair(tmem_base, PW_TMEM_COLS);
 }
 
+// ---------------------------------------------------------------- Karatsuba CTA-pair variant
+// Karatsuba mode (PwJobs::kara): the ring product of point j is three full
+// convolutions of length 4 (P0 = a0*b0, P1 = a1*b1, P2 = (a0+a1)*(b0+b1);
+// half points P0 only), 16 plane products each, instead of the 64 of the
+// negacyclic product.  A tile group is (j, p, half): the "lo" half computes
+// output coefficients s = 0..3 of product p (the 10 terms u + v <= 3), the
+// "hi" half s = 4..6 (the 6 terms u + v >= 4, u, v in 1..3), so every
+// multiply of a stage holds a term: a stage loads the 4 (lo) or 3 (hi) A
+// planes and as many B planes of the product and issues all of its terms,
+// one 256 x 128 accumulator per output coefficient.  Stages are 96 KB (4 A
+// plane tiles of 16 KB + 4 B half-tiles of 8 KB per CTA), two of them.
+constexpr int PWK_STAGES = 2;
+constexpr int PWK_NS = 4;             // operand plane slots per side and stage
+constexpr int PWK_BN = 128;           // output columns per pair tile (MMA N)
+constexpr int PWK_A_BYTES = 128 * PW_BK;
+constexpr int PWK_B_BYTES = (PWK_BN / 2) * PW_BK;
+constexpr int PWK_STAGE_BYTES = PWK_NS * (PWK_A_BYTES + PWK_B_BYTES);
+constexpr int PWK_SMEM_BYTES = 1024 + PWK_STAGES * PWK_STAGE_BYTES + 256;
+
+__device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long tile, int& j, int& pr,
+                                                int& hi, int& mt, int& nt) {
+    const long long per_sj = (long long)p.tiles_m * p.tiles_n;
+    int sj = (int)(tile / per_sj);
+    const int r = (int)(tile % per_sj);
+    const int GM = p.group_m;
+    const int group = GM * p.tiles_n;
+    const int g = r / group;
+    const int first_m = g * GM;
+    const int gm = p.tiles_m - first_m < GM ? p.tiles_m - first_m : GM;
+    const int local = r % group;
+    mt = first_m + local % gm;
+    nt = local / gm;
+    for (j = 0; j < p.jobs.NB; ++j) {
+        const int ng = pw_kara_half(p.jobs, j) ? 2 : 6;
+        if (sj < ng) break;
+        sj -= ng;
+    }
+    pr = sj >> 1;
+    hi = sj & 1;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
+    pointwise_kara_i8_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB, const PwParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PWK_STAGES * PWK_STAGE_BYTES);
+    const uint32_t bar_full = smem_u32(bars);
+    const uint32_t bar_empty = smem_u32(bars + PWK_STAGES);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * PWK_STAGES);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * PWK_STAGES + 1);
+    const uint32_t bar_drain = smem_u32(bars + 2 * PWK_STAGES + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PWK_STAGES + 3);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const long long pair = blockIdx.x >> 1;
+    const long long npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PWK_STAGES; ++s) {
+            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_empty + 8 * s, 1);
+        }
+        mbar_init(bar_tfull, 1);
+        mbar_init(bar_tempty, 2 * 128);
+        mbar_init(bar_drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        prefetch_tensormap(&tmA);
+        prefetch_tensormap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), PW_TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const unsigned long long tmo = p.timeout_ns;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------ TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[PWK_STAGES];
+        for (int s = 0; s < PWK_STAGES; ++s) issued_parity[s] = -1;
+        const long long first_tile = p.stall_producer ? p.num_tiles : pair;
+        bool align = p.wave_counter != nullptr;
+        long long wave = 0;
+        for (long long tile = first_tile; tile < p.num_tiles && !*abort_flag;
+             tile += npairs, ++wave) {
+            if (align && (wave + 1) * npairs <= p.num_tiles) {
+                atomicAdd(p.wave_counter, 1u);
+                const unsigned target = gridDim.x * (unsigned)(wave + 1);
+                const uint64_t dl = global_timer_ns() + 2000000ull;  // 2 ms
+                while (*reinterpret_cast<volatile unsigned*>(p.wave_counter) < target) {
+                    if (global_timer_ns() > dl) {
+                        align = false;  // give up aligning; never wait again
+                        break;
+                    }
+                }
+            }
+            int j, pr, hi, mt, nt;
+            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
+            const int nsl = hi ? 3 : 4;   // planes per side: u, v in [hi, 3]
+            const int base = j * PWK_OPS + 4 * pr + hi;
+            const uint32_t stage_tx = 2u * (uint32_t)nsl * (PWK_A_BYTES + PWK_B_BYTES);
+            for (int kb = 0; kb < p.kblocks; ++kb) {
+                if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
+                                       global_timer_ns() + tmo))
+                    goto producer_done;
+                const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
+                if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
+                uint8_t* st = smem + stage * PWK_STAGE_BYTES;
+                for (int i = 0; i < nsl; ++i) {
+                    tma_load_3d_pair(smem_u32(st + i * PWK_A_BYTES), &tmA, full_leader,
+                                     kb * PW_BK, mt * 256 + (int)rank * 128, base + i);
+                    tma_load_3d_pair(smem_u32(st + PWK_NS * PWK_A_BYTES + i * PWK_B_BYTES), &tmB,
+                                     full_leader, kb * PW_BK,
+                                     nt * PWK_BN + (int)rank * (PWK_BN / 2), base + i);
+                }
+                issued_parity[stage] = (int)phase;
+                if (++stage == PWK_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+    producer_done:
+        for (int s = 0; s < PWK_STAGES; ++s)
+            if (issued_parity[s] >= 0)
+                if (!mbar_wait_deadline(bar_empty + 8 * s, (uint32_t)issued_parity[s],
+                                        global_timer_ns() + tmo))
+                    *abort_flag = 1;
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------ MMA issuer (leader only)
+        const uint32_t idesc = idesc_i8(256, PWK_BN);
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
+            int j, pr, hi, mt, nt;
+            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
+            if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            for (int kb = 0; kb < p.kblocks; ++kb) {
+                if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
+                                       global_timer_ns() + tmo))
+                    goto mma_done;
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + stage * PWK_STAGE_BYTES);
+                const uint32_t acc0 = kb != 0 ? 1u : 0u;  // the first k-block starts every sum
+                // slot i holds plane u = hi + i (A) / v = hi + i (B); the term
+                // (u, v) belongs to output s = u + v, accumulator s - 4 hi
+#pragma unroll
+                for (int ia = 0; ia < PWK_NS; ++ia) {
+#pragma unroll
+                    for (int ib = 0; ib < PWK_NS; ++ib) {
+                        const int s = ia + ib + 2 * hi;  // u + v
+                        if (hi ? (ia == 3 || ib == 3 || s < 4) : s > 3) continue;
+                        const int accn = hi ? s - 4 : s;
+                        // the first term of each accumulator in loop order --
+                        // ia = 0 (lo), ia = accn (hi) -- starts it in k-block 0
+                        const bool init = ia == (hi ? accn : 0);
+                        const uint32_t a0 = st + ia * PWK_A_BYTES;
+                        const uint32_t b0 = st + PWK_NS * PWK_A_BYTES + ib * PWK_B_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < PW_BK / 32; ++kk)
+                            mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
+                                        sdesc_kmajor_sw128(a0 + kk * 32),
+                                        sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                        (acc0 | (uint32_t)kk | (init ? 0u : 1u)) != 0 ? 1u : 0u);
+                    }
+                }
+                mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                if (++stage == PWK_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_pair_mc(bar_tfull, 0x3);
+            acc_phase ^= 1;
+        }
+    mma_done:
+        mma_commit_pair(bar_drain);
+        if (!mbar_wait_deadline(bar_drain, 0, global_timer_ns() + tmo)) *abort_flag = 1;
+    } else if (warp >= 2) {
+        // ------------------------------------------------------ epilogue (both CTAs)
+        const int quarter = warp & 3;
+        uint32_t acc_phase = 0;
+        for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
+            int j, pr, hi, mt, nt;
+            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
+            if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
+                break;
+            tc_fence_after();
+            const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
+            const int col0 = nt * PWK_BN;
+            const int colmax = p.cols - col0;
+            const int nout = hi ? 3 : 4;
+            for (int a = 0; a < nout; ++a) {
+                const int q = j * PWK_JOBS + pr * 7 + 4 * hi + a;
+                int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
+                for (int c = 0; c < PWK_BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                           (uint32_t)(a * PWK_BN + c * 32),
+                                       v);
+                    tmem_ld_wait();
+                    if (row < p.rows) {
+#pragma unroll
+                        for (int e = 0; e < 32; e += 4) {
+                            const int col = c * 32 + e;
+                            if (col < colmax) {
+                                int4 o;
+                                o.x = (int)v[e];
+                                o.y = (int)v[e + 1];
+                                o.z = (int)v[e + 2];
+                                o.w = (int)v[e + 3];
+                                *reinterpret_cast<int4*>(orow + col) = o;
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(mapa_shared(bar_tempty, 0));
+            acc_phase ^= 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();
+    tc_fence_after();
+    if (threadIdx.x == 0 && *abort_flag) atomicCAS(p.err, 0, MFFTB_ERR_TIMEOUT);
+    if (warp == 1) tmem_dealloc_pair(tmem_base, PW_TMEM_COLS);
+}
+
 // ---------------------------------------------------------------- host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -948,6 +1194,60 @@ static int make_map(CUtensorMap* m, const void* base, int kdim, int rows, int pl
     return r == CUDA_SUCCESS ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
+static int launch_kara(const PwLaunch& L, cudaStream_t stream) {
+    // one digit class and chunk, K = 8 (S = 4), CTA pairs over 256-row tiles
+    // (map_rows >= 256: rows past L.rows are read from the plane's padding and
+    // their outputs are not stored)
+    if (L.jobs.K != 8 || L.jobs.dA != 1 || L.jobs.dB != 1 || L.jobs.nchunk != 1 ||
+        L.num_sms < 2 || L.cols < 128 || L.map_rows < 256 || L.map_rows < L.rows ||
+        L.a_planes != L.jobs.NB * PWK_OPS || L.f_planes != L.jobs.NB * PWK_OPS)
+        return MFFTB_ERR_ARG;
+    if (L.chosen) *L.chosen = 4;
+    PwParams p;
+    p.jobs = L.jobs;
+    p.rows = L.rows;
+    p.cols = L.cols;
+    p.kdim = L.kdim;
+    p.kblocks = (L.kdim + PW_BK - 1) / PW_BK;
+    p.block_n = PWK_BN;
+    p.tiles_m = (L.rows + 255) / 256;
+    p.tiles_n = (L.cols + PWK_BN - 1) / PWK_BN;
+    p.num_tiles = (long long)p.tiles_m * p.tiles_n * pw_kara_groups(L.jobs);
+    p.out = L.out;
+    p.out_plane = L.out_plane;
+    p.ldo = L.ldo;
+    p.err = L.err;
+    p.timeout_ns = L.timeout_ns;
+    p.stall_producer = L.stall_producer;
+    p.raster = L.raster;
+    p.group_m = L.group_m > 0 ? L.group_m : PW_GROUP_M / 2;
+    p.wave_counter = L.wave_counter;
+    if (p.wave_counter &&
+        cudaMemsetAsync(p.wave_counter, 0, sizeof(unsigned int), stream) != cudaSuccess)
+        return MFFTB_ERR_CUDA;
+    CUtensorMap tmA, tmB;
+    int rc = make_map(&tmA, L.A, L.kdim, L.map_rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);
+    if (rc) return rc;
+    rc = make_map(&tmB, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, PWK_BN / 2);
+    if (rc) return rc;
+    static int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        if (cudaFuncSetAttribute(pointwise_kara_i8_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 PWK_SMEM_BYTES) != cudaSuccess)
+            return MFFTB_ERR_CUDA;
+        attr_dev = dev;
+    }
+    long long pairs = L.num_sms / 2;
+    if (pairs > p.num_tiles) pairs = p.num_tiles;
+    if (pairs <= 0) return MFFTB_OK;
+    pointwise_kara_i8_kernel<<<(unsigned)(2 * pairs), PW_THREADS, PWK_SMEM_BYTES, stream>>>(tmA, tmB,
+                                                                                          p);
+    return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     if (L.kdim <= 0 || L.rows <= 0 || L.cols <= 0) return MFFTB_ERR_ARG;
     if ((L.lda % 16) || (L.ldf % 16) || (L.ldo % 4) || (L.a_plane_bytes % 16) ||
@@ -956,6 +1256,7 @@ int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {
     if (reinterpret_cast<uintptr_t>(L.A) % 16 || reinterpret_cast<uintptr_t>(L.F) % 16 ||
         reinterpret_cast<uintptr_t>(L.out) % 16)
         return MFFTB_ERR_ARG;
+    if (L.jobs.kara) return launch_kara(L, stream);
     // t-grouped CTA pairs for one-chunk plans, CTA pairs when both dimensions
     // fill at least one 256 x 256 pair tile, single CTAs otherwise.  The
     // schoolbook job table runs on the t-grouped kernel only, at any size
@@ -1076,6 +1377,20 @@ __global__ void pointwise_simt_check_kernel(const int8_t* A, long long lda, long
     int r = (int)((idx % per_job) / cols);
     int c = (int)(idx % cols);
     long long acc = 0;
+    if (J.kara) {  // q = j*21 + p*7 + s: sum over u + v = s of A(j,p,u) * B(j,p,v)
+        const int j = q / PWK_JOBS, pr = (q % PWK_JOBS) / 7, s = q % 7;
+        if (pr > 0 && pw_kara_half(J, j)) return;  // not computed at a half point
+        for (int u = s > 3 ? s - 3 : 0; u <= (s < 3 ? s : 3); ++u) {
+            const int8_t* a = A + (j * PWK_OPS + 4 * pr + u) * a_plane + r * lda;
+            const int8_t* f = F + (j * PWK_OPS + 4 * pr + (s - u)) * f_plane + c * ldf;
+            for (int k = 0; k < kdim; ++k) acc += (long long)a[k] * (long long)f[k];
+        }
+        int32_t got = out[q * out_plane + (long long)r * ldo + c];
+        if ((long long)got != acc) {
+            if (atomicAdd(mismatch, 1) == 0) *first_bad = idx;
+        }
+        return;
+    }
     if (J.school) {
         const int t = q / J.nchunk, ch = q % J.nchunk;
         int lo, hi;

@@ -59,7 +59,29 @@ struct PwJobs {
     // may skip the terms that are zero for that reason; 0 = no skipping.
     int NB;
     int zpS;
+    // Karatsuba mode (kara = 1; K = 8, one digit, one chunk): point j's ring
+    // product is taken as three full convolutions of length S = 4 --
+    // P0 = a0*b0, P1 = a1*b1, P2 = (a0+a1)*(b0+b1), with a = a0 + y^4 a1 --
+    // 3*16 plane products instead of K^2 = 64; the half points need only P0
+    // (a1 = b1 = 0 there).  The operands are 12 planes per point, in order
+    // a0[0..3], a1[0..3], (a0+a1)[0..3] (the same for B), and product p's
+    // output coefficient s (s = 0..6) goes to job plane j*21 + p*7 + s; the
+    // inverse combines them into Chat_j.
+    int kara;
 };
+
+constexpr int PWK_OPS = 12;   // operand planes per point in Karatsuba mode
+constexpr int PWK_JOBS = 21;  // job planes per point in Karatsuba mode
+
+// Karatsuba mode: the half points (j = 0, NB/2) need P0 only
+__host__ __device__ inline bool pw_kara_half(const PwJobs& J, int j) {
+    return j == 0 || 2 * j == J.NB;
+}
+// tile groups (product p, output half hi) of all points: 6 per ordinary
+// point, 2 per half point
+__host__ __device__ inline int pw_kara_groups(const PwJobs& J) {
+    return J.NB <= 2 ? 2 * J.NB : 6 * J.NB - 8;
+}
 
 __host__ __device__ inline bool pw_half_point(const PwJobs& J, int j) {
     return !J.school && J.zpS > 0 && (j == 0 || 2 * j == J.NB);

@@ -43,7 +43,10 @@ struct PwLaunch {
     int raster, group_m;      // tile order (see PwParams); 0 = defaults
     int variant;              // 0 auto, 1 one CTA per tile, 2 CTA pairs, 3 t-grouped CTA pairs
     unsigned int* wave_counter;  // optional 4-byte device word for wave alignment (see PwParams)
-    int* chosen;              // optional host out: kernel used (1 single CTA, 2 pair, 3 grouped)
+    int* chosen;              // optional host out: kernel used (1 single CTA, 2 pair, 3 grouped,
+                              // 4 Karatsuba)
+    int map_rows;             // Karatsuba mode: rows the A tensor map spans (>= rows, >= 256;
+                              // the rows past `rows` lie inside the plane stride)
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

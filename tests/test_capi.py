@@ -107,8 +107,20 @@ def test_plan_exactness_invariants(n, mode, w):
         T = (T + 64) // 128
     bounds.append(T)
     assert T <= 127 and _split_ok(MA, pi["dA"], bounds)
-    assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
-    assert pi["int8_macs"] == pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"] * float(pi["n_int"]) ** 3
+    if pi["kara"]:
+        # Karatsuba pointwise: three full length-S convolutions per ordinary
+        # point, one per half point; the sums a0 + a1 fit int8 and P2's
+        # accumulators (S terms of length n) fit int32
+        NB, S = pi["NB"], pi["S"]
+        assert pi["K"] == 8 and pi["dA"] == pi["dB"] == 1 and pi["nchunk"] == 1 and NB <= 8
+        assert 2 * MA <= 127 and 2 * pi["ncB"] * dmax <= 127
+        assert S * pi["n_int"] * (2 * MA) * (2 * pi["ncB"] * dmax) < 2 ** 31
+        assert pi["njobs"] == NB * 21
+        assert pi["int8_macs"] == (3 * S * S * (NB - 2) + 2 * S * S) * float(pi["n_int"]) ** 3
+    else:
+        assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
+        assert pi["int8_macs"] == (pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"]
+                                   * float(pi["n_int"]) ** 3)
 
 
 @pytest.mark.parametrize("n", [1, 16, 100, 1024, 4096, 16384])

@@ -86,14 +86,17 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
     same bits, and match the oracle's exact entries."""
     gen = oracle.signed_planes if signed else oracle.bigmat_rand
     A, B = gen(n, L, 71 + n), gen(n, L, 73 + L)
+    ctx.set_karatsuba(False)  # the t-grouped kernel's own half-point skip
     ctx.set_half_points(0)
     try:
         dense = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
         pd = ctx.last_plan()
+        ctx.set_half_points(1)
+        got = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
+        ph = ctx.last_plan()
     finally:
         ctx.set_half_points(1)
-    got = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
-    ph = ctx.last_plan()
+        ctx.set_karatsuba(True)
     assert ph["pw_kernel"] == 3 and ph["half_points"] == 1 and pd["half_points"] == 0
     NB, K, S = ph["NB"], ph["K"], ph["S"]
     assert ph["int8_macs"] == pytest.approx(pd["int8_macs"] * ((NB - 2) * K * K + 2 * S * S)
@@ -393,3 +396,47 @@ def test_host_entry_points_chunked_readback(ctx):
     h = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16)  # noqa: E731
     got = ctx.mm_u16(h(uA), h(uB), n, L, signed=True, RL=5)
     assert np.array_equal(got, h(want))
+
+
+@pytest.mark.parametrize("rows,cols,kdim,NB", [
+    (256, 128, 512, 8),
+    (300, 272, 1000, 8),   # ragged rows, columns and contraction
+    (512, 256, 2048, 4),
+    (100, 128, 256, 2),    # fewer rows than one pair tile
+])
+def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB):
+    """The Karatsuba plane-product kernel on random int8 operand planes
+    (NB * 12 per side) against a CUDA-core evaluation of its job table:
+    P0, P1, P2 of every ordinary point, P0 of the half points."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256, variant=4) == 0
+
+
+@pytest.mark.parametrize("n,kind", [(256, "i64"), (300, "i64"), (1000, "i64"), (2112, "i64"),
+                                    (512, "u16s"), (384, "u16")])
+def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
+    """Whole W=64 products with the Karatsuba pointwise (the default for this
+    plan) and without it are the same bits, and match the oracle."""
+    if kind == "i64":
+        A, B = oracle.int64_entries(n, 5 + n), oracle.int64_entries(n, 7 + n)
+        run = lambda: ctx.mm_i64(A, B, n, RL=9)  # noqa: E731
+        Ap, Bp, signed = oracle.int64_to_planes(A, n), oracle.int64_to_planes(B, n), True
+    else:
+        signed = kind == "u16s"
+        gen = oracle.signed_planes if signed else oracle.bigmat_rand
+        Ap, Bp = gen(n, 4, 11 + n), gen(n, 4, 13 + n)
+        run = lambda: ctx.mm_u16(Ap, Bp, n, 4, signed=signed)  # noqa: E731
+    got = run()
+    pk = ctx.last_plan()
+    assert pk["kara"] == 1 and pk["pw_kernel"] == 4
+    assert pk["int8_macs"] == 320 * float(pk["n_int"]) ** 3
+    ctx.set_karatsuba(False)
+    try:
+        ref = run()
+        assert ctx.last_plan()["kara"] == 0
+    finally:
+        ctx.set_karatsuba(True)
+    assert np.array_equal(got, ref)
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 2000)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 2000)]
+    want = oracle.entries(Ap, Bp, n, 4, signed, rows, cols, 9)
+    assert np.array_equal(got.reshape(9, n, n)[:, rows, cols], want)

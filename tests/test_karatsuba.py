@@ -1,0 +1,101 @@
+"""The Karatsuba pointwise step, on the CPU: the algebra the kernels rely on
+and the planner's choice of it.
+
+At an evaluation point the MFFT multiplies two ring elements of
+Z[y]/(y^8 + 1) (src/mfft.c:383-396: 64 plane products per point).  With
+a = a0 + y^4 a1 and b = b0 + y^4 b1 (a0, a1, b0, b1 of degree < 4), and
+y^8 = -1:
+
+    a b = P0 - P1 + y^4 (P2 - P0 - P1)      P0 = a0 b0, P1 = a1 b1,
+                                            P2 = (a0 + a1)(b0 + b1)
+
+so three full convolutions of length 4 (48 plane products) give the same
+coefficients; at the points 0 and NB/2 the blocks have a1 = b1 = 0 and P0 is
+the whole product.  The inverse kernel recombines the 21 job planes of a
+point with exactly the formulas restated here.
+"""
+import random
+
+import pytest
+
+import mfft_bench_b200 as m
+
+
+def _negacyclic(a, b, K=8):
+    c = [0] * K
+    for i in range(K):
+        for j in range(K):
+            if i + j < K:
+                c[i + j] += a[i] * b[j]
+            else:
+                c[i + j - K] -= a[i] * b[j]
+    return c
+
+
+def _conv4(a, b):
+    c = [0] * 7
+    for i in range(4):
+        for j in range(4):
+            c[i + j] += a[i] * b[j]
+    return c
+
+
+def _recombine(P0, P1, P2):
+    """Chat from the job planes, as the register inverse kernel forms it."""
+    M = [P2[s] - P0[s] - P1[s] for s in range(7)]
+    y = [0] * 8
+    for t in range(3):
+        y[t] = P0[t] - P1[t] - M[t + 4]
+    y[3] = P0[3] - P1[3]
+    for t in range(4, 7):
+        y[t] = P0[t] - P1[t] + M[t - 4]
+    y[7] = M[3]
+    return y
+
+
+@pytest.mark.parametrize("half", [False, True])
+def test_karatsuba_identity(half):
+    rng = random.Random(7 + half)
+    for _ in range(2000):
+        a = [rng.randint(-60, 60) for _ in range(8)]
+        b = [rng.randint(-60, 60) for _ in range(8)]
+        if half:
+            a[4:] = b[4:] = [0] * 4
+        sa = [a[i] + a[i + 4] for i in range(4)]
+        sb = [b[i] + b[i + 4] for i in range(4)]
+        assert max(map(abs, sa + sb)) <= 120  # the int8 operands of P2
+        P0, P1, P2 = _conv4(a[:4], b[:4]), _conv4(a[4:], b[4:]), _conv4(sa, sb)
+        want = _negacyclic(a, b)
+        assert _recombine(P0, P1, P2) == want
+        if half:
+            assert P0 + [0] == want  # the half points read P0 alone
+
+
+def test_karatsuba_extremes():
+    """All-extreme operands: every job value and the recombined coefficients
+    stay within the int32 accumulator and int64 inverse bounds the planner
+    proves (|digit sum| <= 60, 4 terms of a length-n contraction)."""
+    n = 16384
+    for sa in (60, -60):
+        for sb in (60, -60):
+            a, b = [sa] * 8, [sb] * 8
+            ha = [a[i] + a[i + 4] for i in range(4)]
+            hb = [b[i] + b[i + 4] for i in range(4)]
+            P2 = _conv4(ha, hb)
+            assert max(abs(v) * n for v in P2) < 2 ** 31
+            got = _recombine(_conv4(a[:4], b[:4]), _conv4(a[4:], b[4:]), P2)
+            assert got == _negacyclic(a, b)
+
+
+def test_planner_uses_karatsuba_on_the_w64_plan():
+    pi = m.plan_info(16384, 0, 64)
+    assert (pi["b"], pi["S"], pi["NB"], pi["K"], pi["dA"]) == (4, 4, 8, 8, 1)
+    assert pi["kara"] == 1 and pi["njobs"] == 8 * 21
+    # 6 ordinary points x 3 x 16 + 2 half points x 16 = 320 plane products
+    assert pi["int8_macs"] == 320 * 16384.0 ** 3
+    # past n ~ 37000 the P2 accumulators (4 * n * 120^2) would pass 2^31
+    assert m.plan_info(40000, 0, 64)["kara"] == 0
+    # plans whose transformed sums do not leave room for a0 + a1 keep the
+    # negacyclic pointwise
+    assert m.plan_info(8192, 0, 68)["kara"] == 0
+    assert m.plan_info(4096, 0, 1024)["kara"] == 0
