@@ -149,9 +149,9 @@ int log2i(int x) {
 int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operand& B,
                 int row_begin, int row_end, const OutSpec& O) {
     Plan P = plan;
-    // the Karatsuba pointwise runs on 256-row CTA-pair tiles with the default
-    // kernels of the other stages
-    if (P.kara && (C->inv_variant != 0 || C->pw_variant != 0 || P.n_int < 128 ||
+    // the Karatsuba pointwise runs on 256-row CTA-pair tiles; its job planes
+    // are read by the register and lane inverse kernels
+    if (P.kara && (C->inv_variant == 1 || C->pw_variant != 0 || P.n_int < 128 ||
                    row_end - row_begin < 256 || C->num_sms < 2))
         plan_set_kara(P, false);
     const int n_int = P.n_int;

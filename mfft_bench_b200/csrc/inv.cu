@@ -474,14 +474,18 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     const long long e_base = (long long)blockIdx.x * E;
     const long long total = (long long)a.rows * a.lda;
     const int ncls = a.nW * a.nchunk;
+    // Karatsuba job planes (K = 8): 21 per point, staged as they are; the
+    // P1 / P2 planes of the half points are never written and not loaded
+    const bool kara = K == 8 && a.kara;
+    const int NQ = kara ? NB * 21 : NK;
 
-    // ---- phase 1: stage [NK][E] int64 = sum over digit classes w and chunks
+    // ---- phase 1: stage [NQ][E] int64 = sum over digit classes w and chunks
     // of 2^(7w) * acc; one pass per (class, chunk) plane set, INVL_UNROLL
     // 16-byte loads in flight per thread.  Each thread revisits only its own
     // smem words across passes, so no barrier is needed between them.
     for (int k = 0; k < ncls; ++k) {
         const int64_t f = (int64_t)1 << (7 * (k / a.nchunk));
-        for (int idx0 = threadIdx.x; idx0 < NK * VE; idx0 += INVL_UNROLL * INVL_THREADS) {
+        for (int idx0 = threadIdx.x; idx0 < NQ * VE; idx0 += INVL_UNROLL * INVL_THREADS) {
             int4 r[INVL_UNROLL];
 #pragma unroll
             for (int u = 0; u < INVL_UNROLL; ++u) {
@@ -489,14 +493,19 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
                 const int q = idx / VE, v = idx % VE;
                 const long long e = e_base + 4 * v;
                 r[u] = make_int4(0, 0, 0, 0);
-                if (idx < NK * VE && e < total)
+                bool live = idx < NQ * VE && e < total;
+                if (kara) {
+                    const int jq = q / 21;
+                    live = live && (q % 21 < 7 || !(jq == 0 || 2 * jq == NB));
+                }
+                if (live)
                     r[u] = __ldg(reinterpret_cast<const int4*>(
                         a.acc + (long long)(q * ncls + k) * a.acc_plane + e));
             }
 #pragma unroll
             for (int u = 0; u < INVL_UNROLL; ++u) {
                 const int idx = idx0 + u * INVL_THREADS;
-                if (idx < NK * VE) {
+                if (idx < NQ * VE) {
                     const int q = idx / VE, v = idx % VE;
                     int64_t* d = sm + q * LD + 4 * v;
                     const int64_t s0 = (int64_t)r[u].x * f, s1 = (int64_t)r[u].y * f;
@@ -522,8 +531,29 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     const int es = lane / K, c = lane % K;
     const int ei = warp * EPW + es;
     int64_t x[NB];
+    if (kara) {
+        // coefficient c of Chat_j = P0 - P1 + y^4 (P2 - P0 - P1) mod y^8 + 1:
+        // (P0 - P1)[c] + sign * M[c ^ 4], M = P2 - P0 - P1, sign -1 for c < 4
+        // (the wrapped half), no M term for c = 3; half points: P0[c]
+        const int cx = c ^ 4;
 #pragma unroll
-    for (int j = 0; j < NB; ++j) x[j] = sm[(bitrev_c<LGNB>(j) * K + c) * LD + ei];  // DIT order
+        for (int j = 0; j < NB; ++j) {
+            const int64_t* pj = sm + (bitrev_c<LGNB>(j) * 21) * LD + ei;
+            const bool half = bitrev_c<LGNB>(j) == 0 || 2 * bitrev_c<LGNB>(j) == NB;
+            int64_t v = c < 7 ? pj[c * LD] : 0;
+            if (!half) {
+                if (c < 7) v -= pj[(7 + c) * LD];
+                if (cx < 7) {
+                    const int64_t Mx = pj[(14 + cx) * LD] - pj[cx * LD] - pj[(7 + cx) * LD];
+                    v += c < 4 ? -Mx : Mx;
+                }
+            }
+            x[j] = v;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < NB; ++j) x[j] = sm[(bitrev_c<LGNB>(j) * K + c) * LD + ei];  // DIT order
+    }
     lane_dit<NB, K, 2>(x, c);
 #pragma unroll
     for (int j = 0; j < NB; ++j) x[j] >>= LGNB;  // exact division by NB
@@ -655,7 +685,7 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
         RL = ((a.positions * a.b + 15) / 16 + 4 + 1) / 2 * 2;
         if (RL > 2 * INV_MAXW) return MFFTB_ERR_UNSUPPORTED;
     }
-    const size_t stage = (size_t)NB * K * (E + 1) * sizeof(int64_t);
+    const size_t stage = (size_t)(a.kara ? NB * 21 : NB * K) * (E + 1) * sizeof(int64_t);
     const size_t carry = (size_t)E * PMAX * sizeof(int64_t) + (size_t)RL * E * sizeof(uint16_t);
     const size_t smem = (stage > carry ? stage : carry + 16);
     if (smem > 200 * 1024) return MFFTB_ERR_UNSUPPORTED;
@@ -683,6 +713,7 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
 // MFFTB_ERR_UNSUPPORTED when the lane variant does not cover the plan
 static int try_lane(const InvArgs& a, cudaStream_t stream) {
     if (a.out_kind == INV_I64) return MFFTB_ERR_UNSUPPORTED;
+    if (a.kara && (a.K != 8 || a.nW != 1 || a.nchunk != 1)) return MFFTB_ERR_UNSUPPORTED;
     if (a.positions > (a.NB + 1) * a.S || a.b < 2 || a.b > 15) return MFFTB_ERR_UNSUPPORTED;
     if (a.lda % 4 || a.acc_plane % 4 || reinterpret_cast<uintptr_t>(a.acc) % 16)
         return MFFTB_ERR_UNSUPPORTED;
@@ -711,6 +742,10 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if (a.kara) {
         if (a.K != 8 || a.nW != 1 || a.nchunk != 1 || a.positions > (a.NB + 1) * a.S)
             return MFFTB_ERR_ARG;
+        if (a.variant == 2) {
+            const int rc = try_lane(a, stream);
+            if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
+        }
         if (a.NB == 8) return launch_reg<8, 8>(a, stream);
         if (a.NB == 4) return launch_reg<4, 8>(a, stream);
         if (a.NB == 2) return launch_reg<2, 8>(a, stream);

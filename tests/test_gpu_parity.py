@@ -429,6 +429,13 @@ def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
     pk = ctx.last_plan()
     assert pk["kara"] == 1 and pk["pw_kernel"] == 4
     assert pk["int8_macs"] == 320 * float(pk["n_int"]) ** 3
+    ctx.set_kernel_variant("inverse", 2)  # the lane inverse on the Karatsuba job planes
+    try:
+        lane = run()
+        assert ctx.last_plan()["kara"] == 1
+    finally:
+        ctx.set_kernel_variant("inverse", 0)
+    assert np.array_equal(lane, got)
     ctx.set_karatsuba(False)
     try:
         ref = run()
