@@ -439,10 +439,10 @@ class Workload:
             ctx.set_reuse_b(False)
             self._compute((self.r0, self.r1), self.peer.ptr + self.r0 * n * self.out.element_size(),
                           plane_stride=n * n)
-            # the stores are complete once this rank's stream is; rank 0's
-            # stream continues only after every rank's all-reduce, i.e. after
-            # every rank's final kernel
-            self.torch.cuda.current_stream().synchronize()
+            # stream-ordered completion: each rank's all-reduce starts after
+            # its final kernel (NCCL's stream waits on this one), and rank 0's
+            # stream continues only after every rank's all-reduce -- so after
+            # every rank's stores -- with no host synchronisation in the step
             self.torch.distributed.all_reduce(self.flag)
             return
         works = []
