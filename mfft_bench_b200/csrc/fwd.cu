@@ -273,11 +273,15 @@ __device__ __forceinline__ void load4_pairs(const void* D, long long off, uint32
         break;
 
 template <int K, int DB>
-__global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a) {
+__global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a, int npg) {
     constexpr int S = K / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = blockIdx.y * (blockDim.x >> 5) + warp;
-    const long long e0 = (long long)blockIdx.x * 128 + 4 * lane;
+    // the npg point groups of one 128-element slice are consecutive blocks,
+    // so they run together and read the slice's digit planes from L2 once
+    const int pg = (int)(blockIdx.x % npg);
+    const long long eb = blockIdx.x / npg;
+    const int j = pg * (blockDim.x >> 5) + warp;
+    const long long e0 = eb * 128 + 4 * lane;
     if (j >= a.NB || e0 >= a.nelem) return;
     const int step = (a.g * j) & (2 * K - 1);
     uint32_t acc[K][2];
@@ -349,9 +353,11 @@ __global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a) {
 template <int K>
 static int launch_pt(const FwdArgs& a, cudaStream_t stream) {
     const int wpb = a.NB < 8 ? a.NB : 8;  // warps (points) per CTA
-    const dim3 grid((unsigned)((a.nelem + 127) / 128), (unsigned)((a.NB + wpb - 1) / wpb));
-    if (a.dbytes == 1) forward_pt_kernel<K, 1><<<grid, 32 * wpb, 0, stream>>>(a);
-    else forward_pt_kernel<K, 2><<<grid, 32 * wpb, 0, stream>>>(a);
+    const int npg = (a.NB + wpb - 1) / wpb;
+    const long long blocks = (a.nelem + 127) / 128 * npg;
+    if (blocks > 0x7fffffffLL) return MFFTB_ERR_ARG;
+    if (a.dbytes == 1) forward_pt_kernel<K, 1><<<(unsigned)blocks, 32 * wpb, 0, stream>>>(a, npg);
+    else forward_pt_kernel<K, 2><<<(unsigned)blocks, 32 * wpb, 0, stream>>>(a, npg);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 

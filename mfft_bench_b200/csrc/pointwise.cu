@@ -1141,16 +1141,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             for (int a = 0; a < nout; ++a) {
                 const int q = j * PWK_JOBS + pr * 7 + 4 * hi + a;
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
-                for (int c = 0; c < PWK_BN / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                                           (uint32_t)(a * PWK_BN + c * 32),
-                                       v);
-                    tmem_ld_wait();
+                for (int c = 0; c < PWK_BN / 64; ++c) {
+                    uint32_t v[64];  // 64 columns per load, one wait each
+                    tmem_ld_32x32b_x64_wait(tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                                (uint32_t)(a * PWK_BN + c * 64),
+                                            v);
                     if (row < p.rows) {
 #pragma unroll
-                        for (int e = 0; e < 32; e += 4) {
-                            const int col = c * 32 + e;
+                        for (int e = 0; e < 64; e += 4) {
+                            const int col = c * 64 + e;
                             if (col < colmax) {
                                 int4 o;
                                 o.x = (int)v[e];
