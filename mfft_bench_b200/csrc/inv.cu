@@ -405,7 +405,6 @@ loaded:
 // segment again from its exact carry-in and emits its 16-bit limbs (segment
 // boundaries sit on limb boundaries: SEG*b is a multiple of 16).
 constexpr int INVL_THREADS = 256;
-constexpr int INVL_UNROLL = 8;  // staging loads in flight per thread
 
 template <int LG>
 __host__ __device__ constexpr int bitrev_c(int j) {
@@ -480,37 +479,51 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     const int NQ = kara ? NB * 21 : NK;
 
     // ---- phase 1: stage [NQ][E] int64 = sum over digit classes w and chunks
-    // of 2^(7w) * acc; one pass per (class, chunk) plane set, INVL_UNROLL
-    // 16-byte loads in flight per thread.  Each thread revisits only its own
-    // smem words across passes, so no barrier is needed between them.
-    for (int k = 0; k < ncls; ++k) {
-        const int64_t f = (int64_t)1 << (7 * (k / a.nchunk));
-        for (int idx0 = threadIdx.x; idx0 < NQ * VE; idx0 += INVL_UNROLL * INVL_THREADS) {
-            int4 r[INVL_UNROLL];
+    // of 2^(7w) * acc.  The planes of up to INVL_KB (class, chunk) pairs are
+    // loaded together -- INVL_UB x INVL_KB 16-byte loads in flight per thread
+    // -- and summed before one smem update per element.  Each thread revisits
+    // only its own smem words across batches, so no barrier is needed between
+    // them.
+    constexpr int INVL_UB = 4, INVL_KB = 3;
+    for (int k0 = 0; k0 < ncls; k0 += INVL_KB) {
+        const int kn = ncls - k0 < INVL_KB ? ncls - k0 : INVL_KB;
+        for (int idx0 = threadIdx.x; idx0 < NQ * VE; idx0 += INVL_UB * INVL_THREADS) {
+            int4 r[INVL_UB][INVL_KB];
 #pragma unroll
-            for (int u = 0; u < INVL_UNROLL; ++u) {
+            for (int u = 0; u < INVL_UB; ++u) {
                 const int idx = idx0 + u * INVL_THREADS;
                 const int q = idx / VE, v = idx % VE;
                 const long long e = e_base + 4 * v;
-                r[u] = make_int4(0, 0, 0, 0);
                 bool live = idx < NQ * VE && e < total;
                 if (kara) {
                     const int jq = q / 21;
                     live = live && (q % 21 < 7 || !(jq == 0 || 2 * jq == NB));
                 }
-                if (live)
-                    r[u] = __ldg(reinterpret_cast<const int4*>(
-                        a.acc + (long long)(q * ncls + k) * a.acc_plane + e));
+#pragma unroll
+                for (int kk = 0; kk < INVL_KB; ++kk) {
+                    r[u][kk] = make_int4(0, 0, 0, 0);
+                    if (live && kk < kn)
+                        r[u][kk] = __ldg(reinterpret_cast<const int4*>(
+                            a.acc + (long long)(q * ncls + k0 + kk) * a.acc_plane + e));
+                }
             }
 #pragma unroll
-            for (int u = 0; u < INVL_UNROLL; ++u) {
+            for (int u = 0; u < INVL_UB; ++u) {
                 const int idx = idx0 + u * INVL_THREADS;
                 if (idx < NQ * VE) {
                     const int q = idx / VE, v = idx % VE;
                     int64_t* d = sm + q * LD + 4 * v;
-                    const int64_t s0 = (int64_t)r[u].x * f, s1 = (int64_t)r[u].y * f;
-                    const int64_t s2 = (int64_t)r[u].z * f, s3 = (int64_t)r[u].w * f;
-                    if (k == 0) {
+                    int64_t s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+                    for (int kk = 0; kk < INVL_KB; ++kk) {
+                        if (kk >= kn) break;
+                        const int64_t f = (int64_t)1 << (7 * ((k0 + kk) / a.nchunk));
+                        s0 += (int64_t)r[u][kk].x * f;
+                        s1 += (int64_t)r[u][kk].y * f;
+                        s2 += (int64_t)r[u][kk].z * f;
+                        s3 += (int64_t)r[u][kk].w * f;
+                    }
+                    if (k0 == 0) {
                         d[0] = s0;
                         d[1] = s1;
                         d[2] = s2;

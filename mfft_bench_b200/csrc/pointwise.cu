@@ -930,6 +930,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
 // plane tiles of 16 KB + 4 B half-tiles of 8 KB per CTA), two of them.
 constexpr int PWK_NS = 4;             // operand plane slots per side and stage
 constexpr int PWK_BN = 128;           // output columns per pair tile (MMA N)
+// warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 epilogue: two warps per
+// 32-lane TMEM quarter, each draining 64 of an accumulator's 128 columns, so
+// the tensor pipe waits half as long between tiles
+constexpr int PWK_EPI_WARPS = 8;
+constexpr int PWK_THREADS = 32 * (2 + PWK_EPI_WARPS);
 // Stage geometry by contraction depth BK: 128-byte rows with 128-byte
 // swizzling, two 96 KB stages; or 64-byte rows with 64-byte swizzling, four
 // 48 KB stages (the same bytes in flight, refilled in finer steps).
@@ -971,7 +976,7 @@ __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long til
 }
 
 template <int BK>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
     pointwise_kara_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB, const PwParams p) {
     using Cfg = KaraCfg<BK>;
@@ -1000,7 +1005,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             mbar_init(bar_empty + 8 * s, 1);
         }
         mbar_init(bar_tfull, 1);
-        mbar_init(bar_tempty, 2 * 128);
+        mbar_init(bar_tempty, 2 * 32 * PWK_EPI_WARPS);
         mbar_init(bar_drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -1126,7 +1131,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
         if (!mbar_wait_deadline(bar_drain, 0, global_timer_ns() + tmo)) *abort_flag = 1;
     } else if (warp >= 2) {
         // ------------------------------------------------------ epilogue (both CTAs)
-        const int quarter = warp & 3;
+        const int quarter = warp & 3;               // TMEM lanes this warp may access
+        const int half = (warp - 2) / 4;            // columns [64 half, 64 half + 64)
         uint32_t acc_phase = 0;
         for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
             int j, pr, hi, mt, nt;
@@ -1141,8 +1147,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             for (int a = 0; a < nout; ++a) {
                 const int q = j * PWK_JOBS + pr * 7 + 4 * hi + a;
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
-                for (int c = 0; c < PWK_BN / 64; ++c) {
-                    uint32_t v[64];  // 64 columns per load, one wait each
+                {
+                    const int c = half;
+                    uint32_t v[64];  // this warp's 64 columns, one wait
                     tmem_ld_32x32b_x64_wait(tmem_base + ((uint32_t)(quarter * 32) << 16) +
                                                 (uint32_t)(a * PWK_BN + c * 64),
                                             v);
@@ -1260,7 +1267,7 @@ static int launch_kara_bk(const PwLaunch& L, cudaStream_t stream) {
     long long pairs = L.num_sms / 2;
     if (pairs > p.num_tiles) pairs = p.num_tiles;
     if (pairs <= 0) return MFFTB_OK;
-    pointwise_kara_i8_kernel<BK><<<(unsigned)(2 * pairs), PW_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB,
+    pointwise_kara_i8_kernel<BK><<<(unsigned)(2 * pairs), PWK_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB,
                                                                                           p);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
