@@ -74,14 +74,22 @@ def env_int(k, d):
         return d
 
 
-# DRAM bytes (read + write) of one pointwise launch, from a one-pass ncu
-# capture of dram__bytes_read.sum / dram__bytes_write.sum.
+# DRAM bytes (read + write) of one plane-product launch (one row block), from
+# a one-pass ncu capture of dram__bytes_read.sum / dram__bytes_write.sum on
+# the full workload (one pass checked on n = 4096 first), keyed by workload
+# and kernel (3 t-grouped, 4 Karatsuba).
 POINTWISE_TRAFFIC = {
-    "c5": {"bytes_per_launch": 848.51e9 + 52.15e9,
-           "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows), "
-                    "half-point terms skipped: 848.5 GB read + 52.2 GB written; "
-                    "algorithmic operand bytes of that launch 43.9 GB read + 46.7 GB "
-                    "of int32 job planes written")},
+    ("c5", 4): {"bytes_per_launch": 310.06e9 + 52.87e9,
+                "note": ("ncu, the second launch of a 1-GPU product (a row block of the plan's "
+                         "rblock rows x 16384 columns), Karatsuba kernel: 310.1 GB read + 52.9 GB "
+                         "written in 363 ms; algorithmic: 96 A operand planes of the block + 96 B "
+                         "operand planes (about 34 GB) read, 140 int32 job planes per element of "
+                         "the block written")},
+    ("c5", 3): {"bytes_per_launch": 848.51e9 + 52.15e9,
+                "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows), "
+                         "t-grouped kernel with the half-point terms skipped: 848.5 GB read + "
+                         "52.2 GB written; algorithmic operand bytes of that launch 43.9 GB read "
+                         "+ 46.7 GB of int32 job planes written")},
 }
 
 PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
@@ -777,13 +785,13 @@ def main():
             line["int8_tops_issued"] = 2 * macs / (ms * 1e-3) / 1e12
             line["useful_tops"] = 2 * pi["schoolbook7_macs"] / (ms * 1e-3) / 1e12
             line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs",
-                                               "half_points", "kara")}
+                                               "half_points", "kara", "rblock")}
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share
-    tr = POINTWISE_TRAFFIC.get(args.workload)
+    tr = POINTWISE_TRAFFIC.get((args.workload, pi.get("pw_kernel")))
     if ("roofline" in line and tr and world == 1 and n == DEFAULT_N[args.workload]
-            and pi.get("pw_kernel") == 3 and pi.get("kind") == 0):
+            and pi.get("kind") == 0):
         line["roofline"]["traffic"] = tr["bytes_per_launch"]
         line["roofline"]["traffic_note"] = tr["note"]
 

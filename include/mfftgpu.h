@@ -64,6 +64,8 @@ typedef struct {
                                 product, counted as a schoolbook over 7-bit digits */
     int kara;                /* 1: Karatsuba pointwise (3 full length-4 convolutions per
                                 point; njobs = NB * 21 job planes) */
+    int rblock;              /* rows per row block of the last product (each block is one
+                                launch of every A-side kernel); 0 from mfftgpu_plan_info_get */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------

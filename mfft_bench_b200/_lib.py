@@ -33,7 +33,8 @@ class PlanInfo(C.Structure):
         ("acc_bound", C.c_longlong), ("inv_bound_log2", C.c_double),
         ("int8_macs", C.c_double), ("schoolbook_macs", C.c_double), ("pw_kernel", C.c_int),
         ("kind", C.c_int), ("U", C.c_int), ("balanced", C.c_int), ("half_points", C.c_int),
-        ("wA", C.c_int), ("wB", C.c_int), ("schoolbook7_macs", C.c_double), ("kara", C.c_int)]
+        ("wA", C.c_int), ("wB", C.c_int), ("schoolbook7_macs", C.c_double), ("kara", C.c_int),
+        ("rblock", C.c_int)]
 
     def as_dict(self):
         return {f: getattr(self, f) for f, _ in self._fields_}

@@ -75,6 +75,7 @@ struct mfftgpu_ctx {
     Plan last_plan{};
     bool have_plan = false;
     int last_pw_kernel = 0;
+    int last_rblock = 0;  // rows per row block of the last product
     int last_half = 0;  // the last product's plane-product kernel skipped the half-point terms
     char msg[512] = {};
 };
@@ -209,6 +210,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     cudaStream_t st = C->stream;
     C->launches = 0;
     C->last_plan = P;
+    C->last_rblock = (int)R;
     C->have_plan = true;
     CUDA_OK(cudaMemsetAsync(C->d_err, 0, sizeof(int), st));
     if (C->profile != 2) C->ev_used = 0;
@@ -732,6 +734,7 @@ int mfftgpu_last_plan(mfftgpu_ctx* C, mfftgpu_plan_info* o) {
     if (!C || !o || !C->have_plan) return MFFTB_ERR_ARG;
     fill_info(C->last_plan, o);
     o->pw_kernel = C->last_pw_kernel;
+    o->rblock = C->last_rblock;
     const Plan& P = C->last_plan;
     if (C->last_half && P.kind == KIND_MFFT && P.NB >= 2) {
         // points 0 and NB/2 issue S^2 of their K^2 plane products
@@ -769,6 +772,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->wB = P.wB;
     o->schoolbook7_macs = (double)n * n * (double)n * ((P.wA + 6) / 7) * ((P.wB + 6) / 7);
     o->kara = P.kara;
+    o->rblock = 0;
     o->pw_kernel = 0;
     o->kind = P.kind;
     o->U = P.U;
