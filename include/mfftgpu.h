@@ -234,8 +234,8 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * product path's choice, 1 one CTA per 128-row tile, 2 CTA pairs (256-row
  * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs, 4 the Karatsuba job
  * table (K = 8, one digit, one chunk: NB * 12 operand planes per side, NB * 21
- * job planes) on its CTA-pair kernel with 128-byte stages, 5 the same with
- * 64-byte stages.  *mismatches receives the number of differing elements. */
+ * job planes) on its CTA-pair kernel.  *mismatches receives the number of
+ * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,
                                long long *mismatches);

@@ -64,7 +64,6 @@ struct mfftgpu_ctx {
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     int kara = 1;                 // Karatsuba pointwise where the plan allows it
-    int kara_bk = 0;              // its contraction bytes per stage: 64, 128 (0 = default)
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
@@ -355,7 +354,6 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
                         P.NB, (!school && !P.kara && C->half_points && P.K == 2 * P.S) ? P.S : 0,
                         P.kara};
         L.map_rows = (int)std::max<long long>(rb, 256);
-        L.kara_bk = C->kara_bk;
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
         L.out = acc;
         L.out_plane = R * n_int;
@@ -539,7 +537,6 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
     if (const char* s = getenv("MFFTGPU_KARA")) C->kara = atoi(s) != 0;
-    if (const char* s = getenv("MFFTGPU_KARA_BK")) C->kara_bk = atoi(s);
     cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
@@ -1091,10 +1088,9 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     cudaSetDevice(C->device);
     const int ld = (kdim + 15) / 16 * 16;
     PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
-    // variant 4 / 5: the Karatsuba kernel (K = 8, one digit, one chunk) with
-    // 128- / 64-byte stages on random operand planes, NB * 12 per side; A
-    // planes span at least 256 rows
-    const bool kara = variant == 4 || variant == 5;
+    // variant 4: the Karatsuba kernel (K = 8, one digit, one chunk) on random
+    // operand planes, NB * 12 per side; A planes span at least 256 rows
+    const bool kara = variant == 4;
     if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;
@@ -1155,7 +1151,6 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.kdim = kdim;
     L.jobs = J;
     L.map_rows = arows;
-    L.kara_bk = variant == 5 ? 64 : 128;
     L.block_n = block_n;
     L.out = out;
     L.out_plane = (long long)rows * cols;

@@ -926,8 +926,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
 // "hi" half s = 4..6 (the 6 terms u + v >= 4, u, v in 1..3), so every
 // multiply of a stage holds a term: a stage loads the 4 (lo) or 3 (hi) A
 // planes and as many B planes of the product and issues all of its terms,
-// one 256 x 128 accumulator per output coefficient.  Stages are 96 KB (4 A
-// plane tiles of 16 KB + 4 B half-tiles of 8 KB per CTA), two of them.
+// one 256 x 128 accumulator per output coefficient.
 constexpr int PWK_NS = 4;             // operand plane slots per side and stage
 constexpr int PWK_BN = 128;           // output columns per pair tile (MMA N)
 // warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 epilogue: two warps per
@@ -935,23 +934,14 @@ constexpr int PWK_BN = 128;           // output columns per pair tile (MMA N)
 // the tensor pipe waits half as long between tiles
 constexpr int PWK_EPI_WARPS = 8;
 constexpr int PWK_THREADS = 32 * (2 + PWK_EPI_WARPS);
-// Stage geometry by contraction depth BK: 128-byte rows with 128-byte
-// swizzling, two 96 KB stages; or 64-byte rows with 64-byte swizzling, four
-// 48 KB stages (the same bytes in flight, refilled in finer steps).
-template <int BK>
-struct KaraCfg {
-    static constexpr int STAGES = BK == 128 ? 2 : 4;
-    static constexpr int A_BYTES = 128 * BK;
-    static constexpr int B_BYTES = (PWK_BN / 2) * BK;
-    static constexpr int STAGE_BYTES = PWK_NS * (A_BYTES + B_BYTES);
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-};
-
-template <int BK>
-__device__ __forceinline__ uint64_t kara_sdesc(uint32_t saddr) {
-    if constexpr (BK == 128) return sdesc_kmajor_sw128(saddr);
-    else return sdesc_kmajor_sw64(saddr);
-}
+// A stage: 4 A plane tiles (128 rows) and 4 B half-tiles (64 columns) of
+// 128 contraction bytes per CTA, 96 KB, two of them.  (Four 48 KB stages of
+// 64 contraction bytes with 64-byte swizzling were measured slower.)
+constexpr int PWK_STAGES = 2;
+constexpr int PWK_A_BYTES = 128 * PW_BK;
+constexpr int PWK_B_BYTES = (PWK_BN / 2) * PW_BK;
+constexpr int PWK_STAGE_BYTES = PWK_NS * (PWK_A_BYTES + PWK_B_BYTES);
+constexpr int PWK_SMEM_BYTES = 1024 + PWK_STAGES * PWK_STAGE_BYTES + 256;
 
 __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long tile, int& j, int& pr,
                                                 int& hi, int& mt, int& nt) {
@@ -975,21 +965,19 @@ __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long til
     hi = sj & 1;
 }
 
-template <int BK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
     pointwise_kara_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB, const PwParams p) {
-    using Cfg = KaraCfg<BK>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PWK_STAGES * PWK_STAGE_BYTES);
     const uint32_t bar_full = smem_u32(bars);
-    const uint32_t bar_empty = smem_u32(bars + Cfg::STAGES);
-    const uint32_t bar_tfull = smem_u32(bars + 2 * Cfg::STAGES);
-    const uint32_t bar_tempty = smem_u32(bars + 2 * Cfg::STAGES + 1);
-    const uint32_t bar_drain = smem_u32(bars + 2 * Cfg::STAGES + 2);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * Cfg::STAGES + 3);
+    const uint32_t bar_empty = smem_u32(bars + PWK_STAGES);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * PWK_STAGES);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * PWK_STAGES + 1);
+    const uint32_t bar_drain = smem_u32(bars + 2 * PWK_STAGES + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PWK_STAGES + 3);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -1000,7 +988,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
     const long long npairs = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < Cfg::STAGES; ++s) {
+        for (int s = 0; s < PWK_STAGES; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
@@ -1026,8 +1014,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
         // ------------------------------------------------------ TMA producer (both CTAs)
         int stage = 0;
         uint32_t phase = 0;
-        int issued_parity[Cfg::STAGES];
-        for (int s = 0; s < Cfg::STAGES; ++s) issued_parity[s] = -1;
+        int issued_parity[PWK_STAGES];
+        for (int s = 0; s < PWK_STAGES; ++s) issued_parity[s] = -1;
         const long long first_tile = p.stall_producer ? p.num_tiles : pair;
         bool align = p.wave_counter != nullptr;
         long long wave = 0;
@@ -1048,30 +1036,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
             pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
             const int nsl = hi ? 3 : 4;   // planes per side: u, v in [hi, 3]
             const int base = j * PWK_OPS + 4 * pr + hi;
-            const uint32_t stage_tx = 2u * (uint32_t)nsl * (Cfg::A_BYTES + Cfg::B_BYTES);
+            const uint32_t stage_tx = 2u * (uint32_t)nsl * (PWK_A_BYTES + PWK_B_BYTES);
             for (int kb = 0; kb < p.kblocks; ++kb) {
                 if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
                                        global_timer_ns() + tmo))
                     goto producer_done;
                 const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
                 if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
-                uint8_t* st = smem + stage * Cfg::STAGE_BYTES;
+                uint8_t* st = smem + stage * PWK_STAGE_BYTES;
                 for (int i = 0; i < nsl; ++i) {
-                    tma_load_3d_pair(smem_u32(st + i * Cfg::A_BYTES), &tmA, full_leader,
-                                     kb * BK, mt * 256 + (int)rank * 128, base + i);
-                    tma_load_3d_pair(smem_u32(st + PWK_NS * Cfg::A_BYTES + i * Cfg::B_BYTES), &tmB,
-                                     full_leader, kb * BK,
+                    tma_load_3d_pair(smem_u32(st + i * PWK_A_BYTES), &tmA, full_leader,
+                                     kb * PW_BK, mt * 256 + (int)rank * 128, base + i);
+                    tma_load_3d_pair(smem_u32(st + PWK_NS * PWK_A_BYTES + i * PWK_B_BYTES), &tmB,
+                                     full_leader, kb * PW_BK,
                                      nt * PWK_BN + (int)rank * (PWK_BN / 2), base + i);
                 }
                 issued_parity[stage] = (int)phase;
-                if (++stage == Cfg::STAGES) {
+                if (++stage == PWK_STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
         }
     producer_done:
-        for (int s = 0; s < Cfg::STAGES; ++s)
+        for (int s = 0; s < PWK_STAGES; ++s)
             if (issued_parity[s] >= 0)
                 if (!mbar_wait_deadline(bar_empty + 8 * s, (uint32_t)issued_parity[s],
                                         global_timer_ns() + tmo))
@@ -1093,7 +1081,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                                        global_timer_ns() + tmo))
                     goto mma_done;
                 tc_fence_after();
-                const uint32_t st = smem_u32(smem + stage * Cfg::STAGE_BYTES);
+                const uint32_t st = smem_u32(smem + stage * PWK_STAGE_BYTES);
                 const uint32_t acc0 = kb != 0 ? 1u : 0u;  // the first k-block starts every sum
                 // slot i holds plane u = hi + i (A) / v = hi + i (B); the term
                 // (u, v) belongs to output s = u + v, accumulator s - 4 hi
@@ -1107,18 +1095,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                         // the first term of each accumulator in loop order --
                         // ia = 0 (lo), ia = accn (hi) -- starts it in k-block 0
                         const bool init = ia == (hi ? accn : 0);
-                        const uint32_t a0 = st + ia * Cfg::A_BYTES;
-                        const uint32_t b0 = st + PWK_NS * Cfg::A_BYTES + ib * Cfg::B_BYTES;
+                        const uint32_t a0 = st + ia * PWK_A_BYTES;
+                        const uint32_t b0 = st + PWK_NS * PWK_A_BYTES + ib * PWK_B_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < BK / 32; ++kk)
+                        for (int kk = 0; kk < PW_BK / 32; ++kk)
                             mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
-                                        kara_sdesc<BK>(a0 + kk * 32),
-                                        kara_sdesc<BK>(b0 + kk * 32), idesc,
+                                        sdesc_kmajor_sw128(a0 + kk * 32),
+                                        sdesc_kmajor_sw128(b0 + kk * 32), idesc,
                                         (acc0 | (uint32_t)kk | (init ? 0u : 1u)) != 0 ? 1u : 0u);
                     }
                 }
                 mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
-                if (++stage == Cfg::STAGES) {
+                if (++stage == PWK_STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
@@ -1201,24 +1189,20 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 // 3-D int8 tensor [planes][rows][kdim] with row stride ld bytes and plane
 // stride plane_bytes; box = box_rows x 128 bytes of one plane, 128B swizzle.
 static int make_map(CUtensorMap* m, const void* base, int kdim, int rows, int planes, long long ld,
-                    long long plane_bytes, int box_rows, int box_k = PW_BK) {
+                    long long plane_bytes, int box_rows) {
     auto enc = get_encode_fn();
     if (!enc) return MFFTB_ERR_CUDA;
-    if (box_k != 128 && box_k != 64) return MFFTB_ERR_ARG;
     cuuint64_t dims[3] = {(cuuint64_t)kdim, (cuuint64_t)rows, (cuuint64_t)planes};
     cuuint64_t strides[2] = {(cuuint64_t)ld, (cuuint64_t)plane_bytes};
-    cuuint32_t box[3] = {(cuuint32_t)box_k, (cuuint32_t)box_rows, 1};
+    cuuint32_t box[3] = {(cuuint32_t)PW_BK, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                     box_k == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
-template <int BK>
-static int launch_kara_bk(const PwLaunch& L, cudaStream_t stream) {
-    using Cfg = KaraCfg<BK>;
+static int launch_kara(const PwLaunch& L, cudaStream_t stream) {
     // one digit class and chunk, K = 8 (S = 4), CTA pairs over 256-row tiles
     // (map_rows >= 256: rows past L.rows are read from the plane's padding and
     // their outputs are not stored)
@@ -1232,7 +1216,7 @@ static int launch_kara_bk(const PwLaunch& L, cudaStream_t stream) {
     p.rows = L.rows;
     p.cols = L.cols;
     p.kdim = L.kdim;
-    p.kblocks = (L.kdim + BK - 1) / BK;
+    p.kblocks = (L.kdim + PW_BK - 1) / PW_BK;
     p.block_n = PWK_BN;
     p.tiles_m = (L.rows + 255) / 256;
     p.tiles_n = (L.cols + PWK_BN - 1) / PWK_BN;
@@ -1250,35 +1234,26 @@ static int launch_kara_bk(const PwLaunch& L, cudaStream_t stream) {
         cudaMemsetAsync(p.wave_counter, 0, sizeof(unsigned int), stream) != cudaSuccess)
         return MFFTB_ERR_CUDA;
     CUtensorMap tmA, tmB;
-    int rc = make_map(&tmA, L.A, L.kdim, L.map_rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM, BK);
+    int rc = make_map(&tmA, L.A, L.kdim, L.map_rows, L.a_planes, L.lda, L.a_plane_bytes, PW_BM);
     if (rc) return rc;
-    rc = make_map(&tmB, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, PWK_BN / 2, BK);
+    rc = make_map(&tmB, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, PWK_BN / 2);
     if (rc) return rc;
     static int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {
-        if (cudaFuncSetAttribute(pointwise_kara_i8_kernel<BK>,
+        if (cudaFuncSetAttribute(pointwise_kara_i8_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 Cfg::SMEM_BYTES) != cudaSuccess)
+                                 PWK_SMEM_BYTES) != cudaSuccess)
             return MFFTB_ERR_CUDA;
         attr_dev = dev;
     }
     long long pairs = L.num_sms / 2;
     if (pairs > p.num_tiles) pairs = p.num_tiles;
     if (pairs <= 0) return MFFTB_OK;
-    pointwise_kara_i8_kernel<BK><<<(unsigned)(2 * pairs), PWK_THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB,
+    pointwise_kara_i8_kernel<<<(unsigned)(2 * pairs), PWK_THREADS, PWK_SMEM_BYTES, stream>>>(tmA, tmB,
                                                                                           p);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
-}
-
-// Karatsuba kernel with 128-byte (2 stages) or 64-byte (4 stages) contraction
-// steps: L.kara_bk, 0 = the default
-static int launch_kara(const PwLaunch& L, cudaStream_t stream) {
-    const int bk = L.kara_bk ? L.kara_bk : 128;
-    if (bk == 64) return launch_kara_bk<64>(L, stream);
-    if (bk == 128) return launch_kara_bk<128>(L, stream);
-    return MFFTB_ERR_ARG;
 }
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream) {

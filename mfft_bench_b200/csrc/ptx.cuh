@@ -125,19 +125,6 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
-// The same for 64-byte swizzling (TMA CU_TENSOR_MAP_SWIZZLE_64B): rows of 64
-// bytes, 8-row atoms of 512 bytes (stride-dimension byte offset 512), layout
-// code 4 = SWIZZLE_64B.
-__device__ __forceinline__ uint64_t sdesc_kmajor_sw64(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)1u << 16;           // LBO (ignored), 16 bytes
-    d |= (uint64_t)(512u >> 4) << 32;  // SBO = 512 bytes
-    d |= (uint64_t)1u << 46;           // version
-    d |= (uint64_t)4u << 61;           // SWIZZLE_64B
-    return d;
-}
-
 // Instruction descriptor for kind::i8: signed A, signed B, S32 accumulator,
 // both operands K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {

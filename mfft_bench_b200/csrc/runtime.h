@@ -47,7 +47,6 @@ struct PwLaunch {
                               // 4 Karatsuba)
     int map_rows;             // Karatsuba mode: rows the A tensor map spans (>= rows, >= 256;
                               // the rows past `rows` lie inside the plane stride)
-    int kara_bk;              // Karatsuba mode: contraction bytes per stage, 64 or 128 (0 = 128)
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);

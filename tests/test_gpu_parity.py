@@ -404,13 +404,11 @@ def test_host_entry_points_chunked_readback(ctx):
     (512, 256, 2048, 4),
     (100, 128, 256, 2),    # fewer rows than one pair tile
 ])
-@pytest.mark.parametrize("variant", [4, 5])
-def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, variant):
-    """The Karatsuba plane-product kernel (128-byte stages: variant 4; 64-byte
-    stages: variant 5) on random int8 operand planes (NB * 12 per side)
-    against a CUDA-core evaluation of its job table: P0, P1, P2 of every
-    ordinary point, P0 of the half points."""
-    assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256, variant=variant) == 0
+def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB):
+    """The Karatsuba plane-product kernel on random int8 operand planes
+    (NB * 12 per side) against a CUDA-core evaluation of its job table:
+    P0, P1, P2 of every ordinary point, P0 of the half points."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256, variant=4) == 0
 
 
 @pytest.mark.parametrize("n,kind", [(256, "i64"), (300, "i64"), (1000, "i64"), (2112, "i64"),
