@@ -260,6 +260,11 @@ def _ref_leaf_seconds(args):
     return time.perf_counter() - t0
 
 
+def _ref_whole_seconds(args):
+    workload, n, method = args
+    return _ref_path_sample(workload, n, method)[0]
+
+
 class RefProjection:
     """The reference's CPU path projected to the workload's full size, on one
     core and on `cores` cores.  The reference path is single-threaded
@@ -274,22 +279,38 @@ class RefProjection:
         self.n = w["n"]
         self.n_s = min(CPU_PHASE_N[workload], self.n)
         self.n_l = min(CPU_LEAF_N[workload], self.n)
+        # the full size runs whole (c1): the measured path is the value, and
+        # the concurrent rounds run whole paths instead of leaves
+        self.whole = self.n_s == self.n
         t_path, self.calls = _ref_path_sample(workload, self.n_s, method)
-        leaf_s = min(_ref_leaf_seconds((self.n_s, 1)) for _ in range(2))
         self.t_path = t_path
+        if self.whole:
+            self.phases, self.leaf_single = 0.0, t_path
+            return
+        leaf_s = min(_ref_leaf_seconds((self.n_s, 1)) for _ in range(2))
         self.phases = max(0.0, t_path - self.calls * leaf_s)
         self.leaf_single = _ref_leaf_seconds((self.n_l, 2))
 
     def value(self, leaf):
+        if self.whole:
+            return leaf
         return (self.phases * (self.n / self.n_s) ** 2
                 + self.calls * leaf * (self.n / self.n_l) ** 3)
 
     def concurrent_leaf(self, pool):
-        ts = pool.map(_ref_leaf_seconds, [(self.n_l, 3 + i) for i in range(self.cores)])
+        if self.whole:
+            ts = pool.map(_ref_whole_seconds, [(self.workload, self.n, self.method)] * self.cores)
+        else:
+            ts = pool.map(_ref_leaf_seconds, [(self.n_l, 3 + i) for i in range(self.cores)])
         return statistics.mean(ts)
 
     def describe(self, leaf_conc):
         what = "limb-plane schoolbook" if self.method == "schoolbook" else "MFFT path"
+        if self.whole:
+            return (f"measured: reference {what} (oracle/_ref, packed leaf) run whole at n={self.n}: "
+                    f"{self.t_path:.3f} s alone, {leaf_conc:.3f} s with {self.cores} copies running "
+                    f"concurrently; the all-core value is {self.cores} concurrent single-threaded "
+                    f"products (the reference path is single-threaded) divided by {self.cores}")
         return (f"projected: reference {what} (oracle/_ref, packed leaf) = phases measured at "
                 f"n={self.n_s} ({self.phases:.3f} s) x (n/{self.n_s})^2 + {self.calls} leaves x "
                 f"one mm_accum at n={self.n_l} x (n/{self.n_l})^3; leaf alone "
@@ -325,7 +346,7 @@ def reference_line(args):
             "config": {"workload": args.workload, "desc": w["desc"], "n": w["n"],
                        "phase_n": proj.n_s, "leaf_n": proj.n_l, "method": args.method},
             "cpu_baseline": {"value": value, "unit": "s", "cores": T, "kind": "reference",
-                             "projected": True, "sample": proj.describe(leaf),
+                             "projected": not proj.whole, "sample": proj.describe(leaf),
                              "single_thread_value": proj.value(proj.leaf_single)},
             "e2e": {"value": value, "unit": "s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -341,7 +362,7 @@ def cpu_baseline_line(workload, method):
     with mp.get_context("spawn").Pool(T) as pool:
         leaf = proj.concurrent_leaf(pool)
     return {"value": proj.value(leaf) / T, "unit": "s", "cores": T, "kind": "reference",
-            "projected": True, "sample": proj.describe(leaf),
+            "projected": not proj.whole, "sample": proj.describe(leaf),
             "single_thread_value": proj.value(proj.leaf_single)}
 
 
