@@ -319,6 +319,38 @@ __global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a, int np
     // d signed int8 digits per value (balanced 7-bit low digits, top digit
     // the rest), the same split as forward_kernel
     const long long plane0 = (long long)j * a.d * (a.f_stack ? (2 * K - 1) : K);
+    if (a.d <= 2) {
+        // the same split on the packed int16 pairs: lo = ((x + 64) & 127) - 64
+        // per halfword (only its low 7 bits matter, so a wrapping add is
+        // exact), hi = (x - lo) / 128, whose byte is bits 7..14 of each
+        // halfword (the plan bounds |hi| <= 127, so x - lo does not wrap);
+        // bytes of four elements gathered with one byte permute each
+        auto store_planes = [&](int dd, int c, uint32_t v) {
+            if (!a.f_stack) {
+                *reinterpret_cast<uint32_t*>(a.out + (plane0 + (long long)dd * K + c) * a.oplane +
+                                             e0) = v;
+            } else {
+                const long long base = plane0 + (long long)dd * (2 * K - 1);
+                *reinterpret_cast<uint32_t*>(a.out + (base + (K - 1 - c)) * a.oplane + e0) = v;
+                if (c >= 1)
+                    *reinterpret_cast<uint32_t*>(a.out + (base + (2 * K - 1 - c)) * a.oplane + e0) =
+                        __vsub4(0u, v);
+            }
+        };
+#pragma unroll
+        for (int c = 0; c < K; ++c) {
+            const uint32_t p01 = acc[c][0], p23 = acc[c][1];
+            if (a.d == 1) {
+                store_planes(0, c, __byte_perm(p01, p23, 0x6420));
+                continue;
+            }
+            const uint32_t lo01 = __vsub2(__vadd2(p01, 0x00400040u) & 0x007F007Fu, 0x00400040u);
+            const uint32_t lo23 = __vsub2(__vadd2(p23, 0x00400040u) & 0x007F007Fu, 0x00400040u);
+            store_planes(0, c, __byte_perm(lo01, lo23, 0x6420));
+            store_planes(1, c, __byte_perm(__vsub2(p01, lo01) >> 7, __vsub2(p23, lo23) >> 7, 0x6420));
+        }
+        return;
+    }
 #pragma unroll
     for (int c = 0; c < K; ++c) {
         int x[4] = {(int)(int16_t)(acc[c][0] & 0xffffu), (int)(int16_t)(acc[c][0] >> 16),

@@ -414,6 +414,17 @@ __host__ __device__ constexpr int bitrev_c(int j) {
 }
 __host__ __device__ constexpr int ilog2_c(int v) { return v <= 1 ? 0 : 1 + ilog2_c(v >> 1); }
 
+// Shared-memory layouts of the lane kernel's carry stage, padded so that the
+// K lanes of an element, each walking its own segment of positions / limbs,
+// hit different banks (without the pad every lane of a 16-position segment
+// maps position p to the same bank).  Fold buffer of a warp: [PMAX][EPW]
+// int64 with one extra word per 16 positions; limb buffer: [RL][E] uint16
+// with 8 extra limbs (16 bytes, keeping 16-byte vectors aligned) per 8 rows.
+__host__ __device__ constexpr int invl_pidx(int p, int epw) { return p * epw + (p >> 4); }
+__host__ __device__ constexpr int invl_pbw(int pmax, int epw) { return pmax * epw + (pmax >> 4) + 1; }
+__host__ __device__ constexpr int invl_oidx(int w, int e) { return w * e + 8 * (w >> 3); }
+__host__ __device__ constexpr int invl_obsize(int rl, int e) { return invl_oidx(rl, e) + 8; }
+
 struct InvLaneGeom {
     int seg;   // positions per lane
     int pmax;  // (NB + 1) * S fold positions
@@ -573,12 +584,13 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     __syncthreads();  // staging reads done: the buffer is reused below
 
     // ---- fold: position beta*S + c (c < S) = C_beta[c] + C_{beta-1}[c + S]
-    int64_t* pb = sm + (long long)warp * EPW * PMAX;  // this warp's [PMAX][EPW]
+    constexpr int PBW = invl_pbw(PMAX, EPW);
+    int64_t* pb = sm + (long long)warp * PBW;  // this warp's [PMAX][EPW], padded
 #pragma unroll
     for (int beta = 0; beta <= NB; ++beta) {
         const int64_t hi = beta >= 1 ? __shfl_down_sync(FULL, x[beta - 1], S, K) : 0;
         const int64_t lo = beta < NB ? x[beta] : 0;
-        if (c < S) pb[(beta * S + c) * EPW + es] = lo + hi;
+        if (c < S) pb[invl_pidx(beta * S + c, EPW) + es] = lo + hi;
     }
     __syncwarp();
 
@@ -591,7 +603,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     int64_t carry = 0, dlo = 0;
     bool ones = true, zeros = true;
     for (int p = p0, i = 0; p < p1; ++p, ++i) {
-        const int64_t v = mine[p * EPW] + carry;
+        const int64_t v = mine[invl_pidx(p, EPW)] + carry;
         const int64_t d = v & mask;
         carry = v >> b;
         if (i < L) {
@@ -620,17 +632,17 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     }
     carry = c == 0 ? 0 : co_prev + delta_prev;
 
-    uint16_t* ob = reinterpret_cast<uint16_t*>(sm + (long long)E * PMAX);  // [RL][E]
+    uint16_t* ob = reinterpret_cast<uint16_t*>(sm + (long long)(INVL_THREADS / 32) * PBW);  // [RL][E]
     int w = p0 * b / 16;
     uint64_t bits = 0;
     int nb = 0;
     for (int p = p0; p < p1; ++p) {
-        const int64_t v = mine[p * EPW] + carry;
+        const int64_t v = mine[invl_pidx(p, EPW)] + carry;
         bits |= ((uint64_t)v & (uint64_t)mask) << nb;
         nb += b;
         carry = v >> b;
         while (nb >= 16) {
-            if (w < RL) ob[w * E + ei] = (uint16_t)(bits & 0xFFFFu);
+            if (w < RL) ob[invl_oidx(w, E) + ei] = (uint16_t)(bits & 0xFFFFu);
             bits >>= 16;
             nb -= 16;
             ++w;
@@ -641,7 +653,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
             const int need = 16 - nb;
             bits |= ((uint64_t)carry & ((1ULL << need) - 1ULL)) << nb;
             carry >>= need;
-            ob[w * E + ei] = (uint16_t)(bits & 0xFFFFu);
+            ob[invl_oidx(w, E) + ei] = (uint16_t)(bits & 0xFFFFu);
             bits = 0;
             nb = 0;
             ++w;
@@ -659,8 +671,8 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
         uint32_t words[INV_MAXW];
         const int nw = RL / 2;
         for (int k = 0; k < nw; ++k)
-            words[k] = (uint32_t)ob[(2 * k) * E + threadIdx.x] |
-                       ((uint32_t)ob[(2 * k + 1) * E + threadIdx.x] << 16);
+            words[k] = (uint32_t)ob[invl_oidx(2 * k, E) + threadIdx.x] |
+                       ((uint32_t)ob[invl_oidx(2 * k + 1, E) + threadIdx.x] << 16);
         store_float(a, (long long)row * a.ldo + col, words, nw);
         return;
     }
@@ -673,7 +685,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
             const long long e = e_base + 8 * v;
             if (e < total)
                 *reinterpret_cast<uint4*>(out + (long long)wv * a.out_plane + e) =
-                    *reinterpret_cast<const uint4*>(ob + wv * E + 8 * v);
+                    *reinterpret_cast<const uint4*>(ob + invl_oidx(wv, E) + 8 * v);
         }
     } else {
         for (int idx = threadIdx.x; idx < RL * E; idx += INVL_THREADS) {
@@ -682,7 +694,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
             if (e >= total) continue;
             const int row = (int)(e / a.lda), col = (int)(e % a.lda);
             if (row >= a.rows || col >= a.cols) continue;
-            out[(long long)wv * a.out_plane + (long long)row * a.ldo + col] = ob[wv * E + i];
+            out[(long long)wv * a.out_plane + (long long)row * a.ldo + col] = ob[invl_oidx(wv, E) + i];
         }
     }
 }
@@ -699,7 +711,8 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
         if (RL > 2 * INV_MAXW) return MFFTB_ERR_UNSUPPORTED;
     }
     const size_t stage = (size_t)(a.kara ? NB * 21 : NB * K) * (E + 1) * sizeof(int64_t);
-    const size_t carry = (size_t)E * PMAX * sizeof(int64_t) + (size_t)RL * E * sizeof(uint16_t);
+    const size_t carry = (size_t)(INVL_THREADS / 32) * invl_pbw(PMAX, 32 / K) * sizeof(int64_t) +
+                         (size_t)invl_obsize(RL, E) * sizeof(uint16_t);
     const size_t smem = (stage > carry ? stage : carry + 16);
     if (smem > 200 * 1024) return MFFTB_ERR_UNSUPPORTED;
     static int attr_dev = -1;
