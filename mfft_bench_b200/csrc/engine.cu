@@ -182,6 +182,15 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
             R = 128;
         if (R > rows_pad) R = rows_pad;
         if (R < 16) R = 16;
+        // several blocks: equal blocks of whole 256-row CTA-pair tiles (a
+        // block ending half-way through a pair tile leaves that tile's other
+        // 128 rows idle in every plane product)
+        if (R >= 256 && R < rows_pad) {
+            const long long nblk = (rows_pad + R - 1) / R;
+            const long long even = (rows_pad + nblk - 1) / nblk;
+            const long long r256 = (even + 255) / 256 * 256;
+            R = r256 <= R ? r256 : R / 256 * 256;
+        }
     };
     size_blocks();
     if (P.kara && R < 256) {  // every row block's tiles read 256 rows of each plane
