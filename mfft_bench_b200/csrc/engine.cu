@@ -939,7 +939,15 @@ template <typename F>
 static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB, char* dA,
                           char* dB, int a_planes, size_t a_esize, int planes, size_t esize,
                           char* dO, void* out, bool whole_a, F compute) {
-    const int nchunks = n >= 4096 ? 4 : 1;
+    // more chunks for the largest products: the first chunk's upload and the
+    // last chunk's read-back are the copies no compute hides
+    const int nchunks = n >= 16384 ? 8 : (n >= 4096 ? 4 : 1);
+    // chunk c covers rows [bound(c), bound(c + 1)), boundaries on whole
+    // 256-row CTA-pair tiles
+    auto bound = [&](int c) {
+        if (c >= nchunks) return n;
+        return (int)(((long long)n * c / nchunks) / 256 * 256);
+    };
     const size_t in = (size_t)a_planes * n * n * a_esize;
     if (nchunks == 1) {
         CUDA_OK(cudaMemcpyAsync(dA, hA, in, cudaMemcpyHostToDevice, C->stream));
@@ -956,7 +964,7 @@ static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB,
         CUDA_OK(cudaStreamWaitEvent(C->up_stream, C->up_ev[8], 0));
         CUDA_OK(cudaMemcpyAsync(dB, hB, in, cudaMemcpyHostToDevice, C->up_stream));
         for (int c = 0; c < nchunks; ++c) {
-            const int r0 = (int)((long long)n * c / nchunks), r1 = (int)((long long)n * (c + 1) / nchunks);
+            const int r0 = bound(c), r1 = bound(c + 1);
             const size_t w = (size_t)(r1 - r0) * n * a_esize, off = (size_t)r0 * n * a_esize;
             CUDA_OK(cudaMemcpy2DAsync(dA + off, (size_t)n * n * a_esize,
                                       static_cast<const char*>(hA) + off, (size_t)n * n * a_esize,
@@ -970,7 +978,7 @@ static int rows_pipelined(mfftgpu_ctx* C, int n, const void* hA, const void* hB,
     int rc = MFFTB_OK;
     C->b_valid = false;
     for (int c = 0; c < nchunks && !rc; ++c) {
-        const int r0 = (int)((long long)n * c / nchunks), r1 = (int)((long long)n * (c + 1) / nchunks);
+        const int r0 = bound(c), r1 = bound(c + 1);
         if (r1 <= r0) continue;
         if (nchunks > 1)
             CUDA_OK(cudaStreamWaitEvent(C->stream, C->up_ev[whole_a ? nchunks - 1 : c], 0));

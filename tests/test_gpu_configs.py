@@ -117,6 +117,9 @@ def test_c5_signed_64bit(ctx, oracle):
     A, B = dA.cpu().numpy(), dB.cpu().numpy()
     C = out.view(torch.int16).cpu().numpy().view(np.uint16)
     del dA, dB, out
+    # the host-buffer entry point: chunked uploads and read-backs overlapped
+    # with the row blocks' compute, the same bits
+    assert np.array_equal(ctx.mm_i64(A, B, n, RL=9), C)
     assert np.array_equal(A[:4096], oracle.int64_entries(64, SA))
     assert oracle.checksum(A, B, n, 4, True, C, 9) == 0
     rows, cols = _sample(n, 3000)
