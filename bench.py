@@ -741,6 +741,9 @@ def main():
     ctx.sync()
     ms = t_start.elapsed_time(t_end) / args.steps
     ph = ctx.phase_ms()
+    if ctx.phase_dropped():  # per-kernel times must cover every timed launch
+        raise RuntimeError(f"{ctx.phase_dropped()} launches past the profile's capacity; "
+                           "time fewer steps")
     ctx.set_profile(0)
     if world > 1:
         t = torch.tensor([ms], device=device, dtype=torch.float64)

@@ -150,6 +150,9 @@ int mfftgpu_last_plan(mfftgpu_ctx *ctx, mfftgpu_plan_info *out);
  * [pack, forward, pointwise, inverse+carry, first-to-last event]. */
 int mfftgpu_set_profile(mfftgpu_ctx *ctx, int mode);
 int mfftgpu_last_phase_ms(mfftgpu_ctx *ctx, float out[5]);
+/* Launches the profile could not record (past its 2048-launch capacity);
+ * their time is missing from mfftgpu_last_phase_ms. */
+int mfftgpu_last_phase_dropped(mfftgpu_ctx *ctx);
 /* Number of kernel launches of the last product. */
 int mfftgpu_last_launches(mfftgpu_ctx *ctx);
 

@@ -87,6 +87,7 @@ _sig("mfftgpu_plan_info_get", i32, i32, i32, i32, i32, C.POINTER(PlanInfo))
 _sig("mfftgpu_last_plan", i32, vp, C.POINTER(PlanInfo))
 _sig("mfftgpu_last_phase_ms", i32, vp, C.POINTER(C.c_float))
 _sig("mfftgpu_last_launches", i32, vp)
+_sig("mfftgpu_last_phase_dropped", i32, vp)
 _sig("mfftgpu_set_profile", i32, vp, i32)
 _sig("mfftgpu_mm_u16_dev", i32, vp, vp, vp, i32, i32, i32, vp, i32, i32, i32)
 _sig("mfftgpu_mm_u16", i32, vp, vp, vp, i32, i32, i32, vp, i32)

@@ -144,6 +144,10 @@ class Context:
     def launches(self):
         return lib.mfftgpu_last_launches(self._h)
 
+    def phase_dropped(self):
+        """Launches past the profile's capacity (their time is not in phase_ms)."""
+        return lib.mfftgpu_last_phase_dropped(self._h)
+
     def last_plan(self):
         pi = PlanInfo()
         self._check(lib.mfftgpu_last_plan(self._h, C.byref(pi)), "last_plan")

@@ -48,10 +48,12 @@ struct mfftgpu_ctx {
     int profile = 0;  // 0 off, 1 last product, 2 accumulate across products
     // profiling: start/end events per launch, recorded without host syncs;
     // times are read back lazily by mfftgpu_last_phase_ms
-    static constexpr int kMaxEv = 512;
+    // (2 events per launch: 2048 launches, e.g. 100 products of 14 launches)
+    static constexpr int kMaxEv = 4096;
     cudaEvent_t ev[kMaxEv] = {};
     int ev_phase[kMaxEv / 2] = {};
     int ev_used = 0;
+    int ev_dropped = 0;  // launches past the event capacity, not in the phase times
     float phase_ms[5] = {};
     bool phase_valid = true;
     int launches = 0;
@@ -221,7 +223,10 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     C->last_rblock = (int)R;
     C->have_plan = true;
     CUDA_OK(cudaMemsetAsync(C->d_err, 0, sizeof(int), st));
-    if (C->profile != 2) C->ev_used = 0;
+    if (C->profile != 2) {
+        C->ev_used = 0;
+        C->ev_dropped = 0;
+    }
     C->phase_valid = false;
     // phase ids: 0 pack, 1 forward, 2 pointwise, 3 inverse
     int cur_phase = 0;
@@ -235,6 +240,8 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
             cudaEventRecord(C->ev[C->ev_used + 1], st);
             C->ev_phase[C->ev_used / 2] = cur_phase;
             C->ev_used += 2;
+        } else if (C->profile) {
+            ++C->ev_dropped;
         }
     };
 
@@ -680,9 +687,12 @@ int mfftgpu_set_profile(mfftgpu_ctx* C, int mode) {
     if (!C || mode < 0 || mode > 2) return MFFTB_ERR_ARG;
     C->profile = mode;
     C->ev_used = 0;
+    C->ev_dropped = 0;
     C->phase_valid = false;
     return MFFTB_OK;
 }
+
+int mfftgpu_last_phase_dropped(mfftgpu_ctx* C) { return C ? C->ev_dropped : 0; }
 
 int mfftgpu_last_phase_ms(mfftgpu_ctx* C, float out[5]) {
     if (!C || !out) return MFFTB_ERR_ARG;
