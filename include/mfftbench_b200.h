@@ -87,6 +87,13 @@ typedef struct {
     long long nprod;
 } mfft_plan;
 int mfft_plan_init(mfft_plan *p, int L, int sigma_override);   /* src/mfft.c:77-95 */
+/* the recursive plan (rec = 1): same S/NB/K choice and product count as the
+ * reference's; mm_mfft / conv_mfft run it on the B200 path like any plan */
+int mfft_plan_init_rec(mfft_plan *p, int L, int n, int sigma_override); /* src/mfft.c:665-686 */
+/* C (K int64 planes) = A * B mod (y^K + 1) over n x n int32 planes, exact;
+ * Mbits (the reference's magnitude hint) is not needed by the GPU product */
+void ssa_negconv(int64_t *C, const int32_t *A, const int32_t *B, int K, int n, int Mbits,
+                 kernel_t kern);                                /* src/mfft.c:560-662 */
 long long mfft_plan_products(const mfft_plan *p);               /* src/mfft.c:97-100 */
 double mfft_plan_maxbits(const mfft_plan *p, int n);            /* src/mfft.c:102-110 */
 void mfft_plan_describe(const mfft_plan *p, int n);             /* src/mfft.c:112-122 */

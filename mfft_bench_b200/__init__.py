@@ -10,6 +10,6 @@ from .api import (KERNEL_PACKED, KERNEL_SM100, PLAN_LIMB, PLAN_VALUE, Context, F
                   MfftError, bigmat_rand, conv_mfft, decode_words_f32, device_count,
                   Fpx64, conv_limbplane, decode_words_f64, decode_words_round, fpx_gemm_f32,
                   fpx_gemm_f32_limbplane, fpx_gemm_f64, fpx_gemm_f64_limbplane, gen_normal_f32,
-                  mfft_plan_init, mm_limbplane, mm_limbplane_signed, mm_mfft, mm_mfft_signed,
-                  normalize_planes, plan_info)
+                  mfft_plan_init, mfft_plan_init_rec, mm_limbplane, mm_limbplane_signed, mm_mfft, mm_mfft_signed,
+                  normalize_planes, plan_info, ssa_negconv)
 from ._lib import LIB_PATH  # noqa: F401

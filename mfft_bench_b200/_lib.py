@@ -119,11 +119,13 @@ _sig("bigmat_rand", None, vp, i32, i32, u64)
 _sig("normalize_planes", None, vp, i32, i32, vp, i32)
 _sig("bigres_equal", i32, vp, vp, i32, i32, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32))
 _sig("mfft_plan_init", i32, C.POINTER(MfftPlan), i32, i32)
+_sig("mfft_plan_init_rec", i32, C.POINTER(MfftPlan), i32, i32, i32)
 _sig("mfft_plan_products", C.c_longlong, C.POINTER(MfftPlan))
 _sig("mfft_plan_maxbits", C.c_double, C.POINTER(MfftPlan), i32)
 _sig("mm_mfft", None, vp, vp, i32, i32, C.POINTER(MfftPlan), i32, vp, i32)
 _sig("mm_mfft_signed", None, vp, vp, i32, i32, vp, i32)
 _sig("conv_mfft", None, vp, vp, vp, i32, i32, C.POINTER(MfftPlan), i32)
+_sig("ssa_negconv", None, vp, vp, vp, i32, i32, i32, i32)
 _sig("fpx_init", i32, C.POINTER(FpxCtx), vp, vp, i32, i32)
 _sig("fpx_encode", None, C.POINTER(FpxCtx), vp, vp)
 _sig("fpx_decode_f32", None, C.POINTER(FpxCtx), vp)

@@ -125,9 +125,10 @@ class Context:
         at the evaluation points 0 and NB/2; identical results."""
         self._check(lib.mfftgpu_set_half_points(self._h, int(bool(on))), "set_half_points")
 
-    def set_karatsuba(self, on):
-        """Karatsuba pointwise on plans that allow it (default on); same bits."""
-        self._check(lib.mfftgpu_set_karatsuba(self._h, int(bool(on))), "set_karatsuba")
+    def set_karatsuba(self, level):
+        """Karatsuba pointwise level on plans that allow it: 0 off, 1 one
+        level (True), 2 P0 and P1 split again (the default); same bits."""
+        self._check(lib.mfftgpu_set_karatsuba(self._h, int(level)), "set_karatsuba")
 
     def set_kernel_variant(self, stage, variant):
         """Pick the kernel of a stage ('forward', 'pointwise' or 'inverse'; 0 = auto).
@@ -273,6 +274,23 @@ def mfft_plan_init(L, sigma=0):
     """src/mfft.c:77-95; returns an ``mfft_plan`` or None when L is invalid."""
     p = MfftPlan()
     return p if lib.mfft_plan_init(C.byref(p), L, sigma) == 0 else None
+
+
+def mfft_plan_init_rec(L, n, sigma=0):
+    """src/mfft.c:665-686: the recursive plan (``rec`` = 1) for n x n
+    matrices, or None when L admits none."""
+    p = MfftPlan()
+    return p if lib.mfft_plan_init_rec(C.byref(p), L, n, sigma) == 0 else None
+
+
+def ssa_negconv(A32, B32, K, n, Mbits=0, kernel=KERNEL_SM100):
+    """src/mfft.c:560-662 through the drop-in C symbol: the K int64 planes of
+    A * B mod (y^K + 1), A and B K int32 planes of n x n matrices."""
+    C_ = np.zeros(K * n * n, np.int64)
+    A32, B32 = np.ascontiguousarray(A32, np.int32), np.ascontiguousarray(B32, np.int32)
+    lib.ssa_negconv(_ptr(C_), _ptr(A32), _ptr(B32), K, n, Mbits, kernel)
+    _status("ssa_negconv")
+    return C_
 
 
 def bigmat_rand(n, L, seed):

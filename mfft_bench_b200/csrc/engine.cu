@@ -28,6 +28,10 @@
 
 using namespace mfftb;
 
+// Karatsuba level of the pointwise step where a plan allows it (the W = 64
+// plans): 2 splits P0 and P1 into length-2 convolutions as well
+constexpr int kDefaultKara = 2;
+
 struct mfftgpu_ctx {
     int device = 0;
     int num_sms = 148;
@@ -65,7 +69,7 @@ struct mfftgpu_ctx {
                                   // 2 the lane kernel wherever it covers the plan
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
-    int kara = 1;                 // Karatsuba pointwise where the plan allows it
+    int kara = kDefaultKara;      // Karatsuba level where the plan allows it
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
@@ -156,7 +160,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     // are read by the register and lane inverse kernels
     if (P.kara && (C->inv_variant == 1 || C->pw_variant != 0 || P.n_int < 128 ||
                    row_end - row_begin < 256 || C->num_sms < 2))
-        plan_set_kara(P, false);
+        plan_set_kara(P, 0);
     const int n_int = P.n_int;
     const int dbytes = plan_digit_bytes(P);
     const long long nn_int = (long long)n_int * n_int;
@@ -173,8 +177,9 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     // row block R from the workspace limit: B's digit planes and operand
     // planes whole, A's digit and operand planes and the job planes per row
     auto size_blocks = [&]() {
-        fpl = school ? 0 : (P.kara ? P.NB * PWK_OPS : P.NB * P.dB * (2 * P.K - 1));
-        apl = school ? 0 : (P.kara ? P.NB * PWK_OPS : P.NB * P.dA * P.K);
+        const int kops = P.kara == 2 ? PWK2_OPS : PWK_OPS;
+        fpl = school ? 0 : (P.kara ? P.NB * kops : P.NB * P.dB * (2 * P.K - 1));
+        apl = school ? 0 : (P.kara ? P.NB * kops : P.NB * P.dA * P.K);
         szDB = align256((size_t)P.LbB * nn_int * dbytes);
         szF = align256((size_t)fpl * nn_int);
         per_row = (size_t)n_int * ((size_t)P.LbA * dbytes + apl + 4 * (size_t)P.njobs);
@@ -196,7 +201,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     };
     size_blocks();
     if (P.kara && R < 256) {  // every row block's tiles read 256 rows of each plane
-        plan_set_kara(P, false);
+        plan_set_kara(P, 0);
         size_blocks();
     }
     const size_t szDA = align256((size_t)P.LbA * R * n_int * dbytes);
@@ -280,7 +285,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     fb.d = P.dB;
     fb.lgS = log2i(P.S);
     fb.lgK = log2i(P.K);
-    fb.f_stack = P.kara ? 2 : 1;
+    fb.f_stack = P.kara ? 1 + P.kara : 1;
     fb.out = F;
     fb.oplane = nn_int;
     fb.err = C->d_err;
@@ -344,7 +349,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
         fa.nelem = (long long)rb * n_int;
         fa.nc = P.ncA;
         fa.d = P.dA;
-        fa.f_stack = P.kara ? 2 : 0;
+        fa.f_stack = P.kara ? 1 + P.kara : 0;
         fa.out = Ah;
         fa.oplane = R * n_int;
         if (!school) {
@@ -452,7 +457,7 @@ int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P,
     if (rc)
         return set_err(C, MFFTB_ERR_PLAN, "no exact int8 plan for n=%d mode=%d widths %d/%d", n,
                        mode, wA, wB);
-    plan_set_kara(*P, C->kara != 0);
+    plan_set_kara(*P, C->kara);
     return MFFTB_OK;
 }
 
@@ -552,7 +557,10 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
-    if (const char* s = getenv("MFFTGPU_KARA")) C->kara = atoi(s) != 0;
+    if (const char* s = getenv("MFFTGPU_KARA")) {
+        const int v = atoi(s);
+        C->kara = v < 0 ? 0 : (v > 2 ? 2 : v);
+    }
     cudaMemset(C->d_err, 0, 256);
     *out = C;
     return MFFTB_OK;
@@ -660,9 +668,9 @@ int mfftgpu_set_half_points(mfftgpu_ctx* C, int on) {
     return MFFTB_OK;
 }
 
-int mfftgpu_set_karatsuba(mfftgpu_ctx* C, int on) {
-    if (!C) return MFFTB_ERR_ARG;
-    C->kara = on != 0;
+int mfftgpu_set_karatsuba(mfftgpu_ctx* C, int level) {
+    if (!C || level < 0 || level > 2) return MFFTB_ERR_ARG;
+    C->kara = level;
     return MFFTB_OK;
 }
 
@@ -740,7 +748,7 @@ int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o)
     } else if (plan_search(n, mode, wA, wB, 0, 0, &P)) {
         return MFFTB_ERR_PLAN;
     } else {
-        plan_set_kara(P, true);  // the default context setting
+        plan_set_kara(P, kDefaultKara);  // the default context setting
     }
     fill_info(P, o);
     return MFFTB_OK;
@@ -1115,22 +1123,23 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     cudaSetDevice(C->device);
     const int ld = (kdim + 15) / 16 * 16;
     PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
-    // variant 4: the Karatsuba kernel (K = 8, one digit, one chunk) on random
-    // operand planes, NB * 12 per side; A planes span at least 256 rows
-    const bool kara = variant == 4;
+    // variants 4 and 5: the Karatsuba kernel (K = 8, one digit, one chunk)
+    // at level 1 / 2 on random operand planes, NB * 12 / NB * 16 per side; A
+    // planes span at least 256 rows
+    const bool kara = variant == 4 || variant == 5;
     if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;
     if (kara) {
         J.NB = NB;
-        J.kara = 1;
-        J.njobs = NB * PWK_JOBS;
+        J.kara = variant - 3;
+        J.njobs = NB * pw_kara_jobs(J);
     } else if (C->half_points && K % 2 == 0) {
         J.NB = NB;
         J.zpS = K / 2;
     }
-    const int apl = kara ? NB * PWK_OPS : NB * dA * K;
-    const int fpl = kara ? NB * PWK_OPS : NB * dB * (2 * K - 1);
+    const int apl = kara ? NB * pw_kara_ops(J) : NB * dA * K;
+    const int fpl = kara ? NB * pw_kara_ops(J) : NB * dB * (2 * K - 1);
     const size_t szA = align256((size_t)apl * arows * ld), szF = align256((size_t)fpl * cols * ld);
     const size_t szO = align256((size_t)J.njobs * rows * cols * 4);
     int rc = ensure(C, &C->ws, &C->ws_bytes, szA + szF + szO + 256);

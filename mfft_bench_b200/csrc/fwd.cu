@@ -21,7 +21,9 @@
 // For B they write the F stack the pointwise kernel expects:
 // F[K-1-c] = +Bhat[c] and F[2K-1-c] = -Bhat[c].  In Karatsuba mode
 // (f_stack = 2, one digit) both operands are written as K + S planes per
-// point: Xhat[0..K-1], then Xhat[c] + Xhat[c+S] for c < S.
+// point: Xhat[0..K-1], then Xhat[c] + Xhat[c+S] for c < S; with the second
+// Karatsuba level (f_stack = 3) S more follow: Xhat[c] + Xhat[c+S/2] for the
+// first S/2 coefficients c of each half (c = 0..S/2-1, then S..S+S/2-1).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -73,8 +75,9 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
     // gridDim.y so that every SM gets work
     for (int j = blockIdx.y; j < a.NB; j += gridDim.y) {
         const int step = (a.g * j) & mask2K;
-        if (a.f_stack == 2) {
+        if (a.f_stack >= 2) {
             // Karatsuba operands (one digit): planes x[c], then x[c] + x[c+S]
+            // (and for f_stack = 3 the half-block sums)
             auto coef = [&](int c, int (&x)[4]) {
                 x[0] = x[1] = x[2] = x[3] = 0;
                 int e = 0;
@@ -93,7 +96,8 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                     for (int q = 0; q < 4; ++q) x[q] += sgn * v[q];
                 }
             };
-            const long long base = (long long)j * (a.K + a.S);
+            const int per_j = a.f_stack == 3 ? a.K + 2 * a.S : a.K + a.S;
+            const long long base = (long long)j * per_j;
             for (int c = 0; c < a.S; ++c) {
                 int lo[4], hi[4];
                 coef(c, lo);
@@ -102,6 +106,17 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                 store4(a.out + (base + c + a.S) * a.oplane + e0, hi[0], hi[1], hi[2], hi[3]);
                 store4(a.out + (base + a.K + c) * a.oplane + e0, lo[0] + hi[0], lo[1] + hi[1],
                        lo[2] + hi[2], lo[3] + hi[3]);
+            }
+            if (a.f_stack == 3) {
+                const int h = a.S / 2;
+                for (int i = 0; i < a.S; ++i) {
+                    const int c = (i / h) * a.S + i % h;  // first coefficient of the pair
+                    int x0[4], x1[4];
+                    coef(c, x0);
+                    coef(c + h, x1);
+                    store4(a.out + (base + a.K + a.S + i) * a.oplane + e0, x0[0] + x1[0],
+                           x0[1] + x1[1], x0[2] + x1[2], x0[3] + x1[3]);
+                }
             }
             continue;
         }
@@ -174,8 +189,9 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
                     : 0u;
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-        if (a.f_stack == 2) {
-            // Karatsuba operands: x[0..S-1], x[S..K-1], x[c] + x[c+S]
+        if (a.f_stack >= 2) {
+            // Karatsuba operands: x[0..S-1], x[S..K-1], x[c] + x[c+S] (and
+            // for f_stack = 3 the half-block sums x[c] + x[c+S/2])
             uint32_t xs[K];
 #pragma unroll
             for (int c = 0; c < K; ++c) {
@@ -191,7 +207,7 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
                 }
                 xs[c] = x;
             }
-            const long long base = (long long)j * (K + S);
+            const long long base = (long long)j * (a.f_stack == 3 ? K + 2 * S : K + S);
 #pragma unroll
             for (int c = 0; c < K; ++c)
                 *reinterpret_cast<uint32_t*>(a.out + (base + c) * a.oplane + e0) = xs[c];
@@ -199,6 +215,15 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
             for (int c = 0; c < S; ++c)
                 *reinterpret_cast<uint32_t*>(a.out + (base + K + c) * a.oplane + e0) =
                     __vadd4(xs[c], xs[c + S]);
+            if (a.f_stack == 3) {
+                constexpr int H = S / 2 > 0 ? S / 2 : 1;
+#pragma unroll
+                for (int i = 0; i < S; ++i) {
+                    const int c = (i / H) * S + i % H;
+                    *reinterpret_cast<uint32_t*>(a.out + (base + K + S + i) * a.oplane + e0) =
+                        __vadd4(xs[c], xs[c + H]);
+                }
+            }
             continue;
         }
 #pragma unroll
@@ -412,7 +437,8 @@ static int launch_simd(const FwdArgs& a, cudaStream_t stream) {
 int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     if (a.nelem % 4 || a.d < 1 || a.d > 4) return MFFTB_ERR_ARG;
     // Karatsuba operands: one int8 digit per value, blocks of S = K/2
-    if (a.f_stack == 2 && (a.d != 1 || 2 * a.S != a.K)) return MFFTB_ERR_ARG;
+    if (a.f_stack >= 2 && (a.d != 1 || 2 * a.S != a.K)) return MFFTB_ERR_ARG;
+    if (a.f_stack == 3 && a.S < 2) return MFFTB_ERR_ARG;
     const int threads = 256;
     long long blocks = (a.nelem / 4 + threads - 1) / threads;
     if (blocks <= 0) return MFFTB_OK;
@@ -430,7 +456,7 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     }
     // one point per warp with int16 lanes when every partial sum fits them:
     // |sum| <= nc * 2^b < 2^15
-    if (a.variant == 0 && a.f_stack != 2 && (a.dbytes == 1 || a.dbytes == 2) && 2 * a.S == a.K &&
+    if (a.variant == 0 && a.f_stack < 2 && (a.dbytes == 1 || a.dbytes == 2) && 2 * a.S == a.K &&
         a.b >= 1 &&
         a.b <= 14 && ((long long)a.nc << a.b) < 32768 && a.NB >= 1 && a.nelem % 4 == 0) {
         if (a.K == 8) return launch_pt<8>(a, stream);

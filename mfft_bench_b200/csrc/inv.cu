@@ -201,6 +201,28 @@ __device__ __forceinline__ void ring_mul_pow(const int64_t (&v)[K], int64_t (&o)
     }
 }
 
+// kara = 2: a length-4 convolution P from the 9 job planes of its three
+// length-2 convolutions Q0, Q1, Q2 (3 coefficients each):
+// P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1
+__device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane,
+                                             int64_t (&P)[7]) {
+    int64_t q0[3], q1[3], m[3];
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+        q0[s] = __ldg(src + s * plane);
+        q1[s] = __ldg(src + (3 + s) * plane);
+    }
+#pragma unroll
+    for (int s = 0; s < 3; ++s) m[s] = (int64_t)__ldg(src + (6 + s) * plane) - q0[s] - q1[s];
+    P[0] = q0[0];
+    P[1] = q0[1];
+    P[2] = q0[2] + m[0];
+    P[3] = m[1];
+    P[4] = q1[0] + m[2];
+    P[5] = q1[1];
+    P[6] = q1[2];
+}
+
 template <int NB, int K>
 __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
     constexpr int S = K / 2, LGNB = NB == 2 ? 1 : (NB == 4 ? 2 : 3);
@@ -222,13 +244,20 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
         if (a.kara) {
             // Chat_j = P0 - P1 + y^4 (P2 - P0 - P1) mod y^8 + 1, with
             // M = P2 - P0 - P1: Chat[t] = D[t] - M[t+4] (t < 3), D[3] (t = 3),
-            // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1
+            // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1.  kara = 2
+            // first forms P0 and P1 from their length-2 convolutions.
+            const bool two = a.kara == 2;
+            const int nq = two ? 25 : 21, p2 = two ? 18 : 14;
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
-                const int32_t* src = a.acc + (long long)j * 21 * a.acc_plane + e;
+                const int32_t* src = a.acc + (long long)j * nq * a.acc_plane + e;
                 int64_t P0[7];
+                if (two) {
+                    kara2_expand(src, a.acc_plane, P0);
+                } else {
 #pragma unroll
-                for (int s = 0; s < 7; ++s) P0[s] = __ldg(src + (long long)s * a.acc_plane);
+                    for (int s = 0; s < 7; ++s) P0[s] = __ldg(src + (long long)s * a.acc_plane);
+                }
                 if (j == 0 || 2 * j == NB) {  // half point: P0 only
 #pragma unroll
                     for (int t = 0; t < 7; ++t) x[bitrev(j)][t] = P0[t];
@@ -236,11 +265,16 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
                     continue;
                 }
                 int64_t P1[7], M[7];
+                if (two) {
+                    kara2_expand(src + 9 * a.acc_plane, a.acc_plane, P1);
+                } else {
 #pragma unroll
-                for (int s = 0; s < 7; ++s) P1[s] = __ldg(src + (long long)(7 + s) * a.acc_plane);
+                    for (int s = 0; s < 7; ++s)
+                        P1[s] = __ldg(src + (long long)(7 + s) * a.acc_plane);
+                }
 #pragma unroll
                 for (int s = 0; s < 7; ++s)
-                    M[s] = (int64_t)__ldg(src + (long long)(14 + s) * a.acc_plane) - P0[s] - P1[s];
+                    M[s] = (int64_t)__ldg(src + (long long)(p2 + s) * a.acc_plane) - P0[s] - P1[s];
                 int64_t(&y)[K] = x[bitrev(j)];
 #pragma unroll
                 for (int t = 0; t < 3; ++t) y[t] = P0[t] - P1[t] - M[t + 4];
@@ -486,7 +520,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
     const int ncls = a.nW * a.nchunk;
     // Karatsuba job planes (K = 8): 21 per point, staged as they are; the
     // P1 / P2 planes of the half points are never written and not loaded
-    const bool kara = K == 8 && a.kara;
+    const bool kara = K == 8 && a.kara == 1;
     const int NQ = kara ? NB * 21 : NK;
 
     // ---- phase 1: stage [NQ][E] int64 = sum over digit classes w and chunks
@@ -710,7 +744,7 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
         RL = ((a.positions * a.b + 15) / 16 + 4 + 1) / 2 * 2;
         if (RL > 2 * INV_MAXW) return MFFTB_ERR_UNSUPPORTED;
     }
-    const size_t stage = (size_t)(a.kara ? NB * 21 : NB * K) * (E + 1) * sizeof(int64_t);
+    const size_t stage = (size_t)(a.kara == 1 ? NB * 21 : NB * K) * (E + 1) * sizeof(int64_t);
     const size_t carry = (size_t)(INVL_THREADS / 32) * invl_pbw(PMAX, 32 / K) * sizeof(int64_t) +
                          (size_t)invl_obsize(RL, E) * sizeof(uint16_t);
     const size_t smem = (stage > carry ? stage : carry + 16);
@@ -739,7 +773,8 @@ static int launch_lane(const InvArgs& a, cudaStream_t stream) {
 // MFFTB_ERR_UNSUPPORTED when the lane variant does not cover the plan
 static int try_lane(const InvArgs& a, cudaStream_t stream) {
     if (a.out_kind == INV_I64) return MFFTB_ERR_UNSUPPORTED;
-    if (a.kara && (a.K != 8 || a.nW != 1 || a.nchunk != 1)) return MFFTB_ERR_UNSUPPORTED;
+    if (a.kara && (a.kara != 1 || a.K != 8 || a.nW != 1 || a.nchunk != 1))
+        return MFFTB_ERR_UNSUPPORTED;
     if (a.positions > (a.NB + 1) * a.S || a.b < 2 || a.b > 15) return MFFTB_ERR_UNSUPPORTED;
     if (a.lda % 4 || a.acc_plane % 4 || reinterpret_cast<uintptr_t>(a.acc) % 16)
         return MFFTB_ERR_UNSUPPORTED;
@@ -766,7 +801,8 @@ static int school_carry_launch(const InvArgs& a, cudaStream_t stream);
 int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if (a.school) return school_carry_launch(a, stream);
     if (a.kara) {
-        if (a.K != 8 || a.nW != 1 || a.nchunk != 1 || a.positions > (a.NB + 1) * a.S)
+        if (a.K != 8 || a.nW != 1 || a.nchunk != 1 || a.positions > (a.NB + 1) * a.S ||
+            a.kara > 2)
             return MFFTB_ERR_ARG;
         if (a.variant == 2) {
             const int rc = try_lane(a, stream);

@@ -46,7 +46,9 @@ struct FwdArgs {
     int S, NB, K, g, nc, d;
     int lgS, lgK;      // log2 of S and K (all plan sizes are powers of two)
     int f_stack;       // 0: write Ahat [j][da][c]; 1: write F [j][db][r] (2K-1 planes);
-                       // 2: Karatsuba operands [j][K + S]: Xhat[c], then Xhat[c] + Xhat[c+S]
+                       // 2: Karatsuba operands [j][K + S]: Xhat[c], then Xhat[c] + Xhat[c+S];
+                       // 3: two levels [j][K + 2S]: those, then Xhat[c] + Xhat[c+S/2] for
+                       //    c = 0..S/2-1 and S..S+S/2-1
     int8_t* out;
     long long oplane;  // bytes per output plane
     int* err;
@@ -89,8 +91,11 @@ struct InvArgs {
     // Karatsuba mode (K = 8, one digit class, one chunk): acc holds 21 job
     // planes per point j, q = j*21 + p*7 + s, coefficient s of the full
     // convolutions P0 = a0*b0, P1 = a1*b1, P2 = (a0+a1)*(b0+b1) (a = a0 +
-    // y^4 a1); the half points (j = 0, NB/2) hold P0 only.  Only the register
-    // kernel reads this layout.
+    // y^4 a1); the half points (j = 0, NB/2) hold P0 only.  kara = 2: 25
+    // job planes per point, q = j*25 + ...: the length-2 convolutions Q0, Q1,
+    // Q2 of P0 (3 coefficients each, 0..8) and of P1 (9..17), from which
+    // P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1, then P2 (18..24).  The register
+    // kernel reads both layouts, the lane kernel kara = 1 only.
     int kara;
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);

@@ -140,15 +140,19 @@ bool plan_kara_ok(const Plan& p) {
     return 4LL * p.n_int * sa * sb <= 2147483647LL;
 }
 
-void plan_set_kara(Plan& p, bool on) {
-    if (on && !plan_kara_ok(p)) on = false;
-    p.kara = on ? 1 : 0;
+void plan_set_kara(Plan& p, int level) {
+    if (level < 0 || level > 2 || (level && !plan_kara_ok(p))) level = 0;
+    p.kara = level;
     const double S2 = (double)p.S * p.S;
     const double pts = p.NB <= 2 ? 0.0 : (double)p.NB - 2.0;  // ordinary points
     const double half = p.NB <= 2 ? (double)p.NB : 2.0;
-    if (on) {
+    if (level == 1) {  // P0, P1, P2: S^2 plane products each
         p.njobs = p.NB * 21;
         p.macs_per_elem = (3.0 * S2 * pts + S2 * half) * p.n_int;
+    } else if (level == 2) {  // P0, P1 as three length-S/2 convolutions each
+        const double q = 3.0 * S2 / 4.0;
+        p.njobs = p.NB * 25;
+        p.macs_per_elem = ((2.0 * q + S2) * pts + q * half) * p.n_int;
     } else {
         p.njobs = p.NB * p.K * p.nW * p.nchunk;
         p.macs_per_elem = (double)p.NB * p.K * p.K * p.dA * p.dB * p.n_int;

@@ -57,7 +57,9 @@ struct Plan {
     // Karatsuba pointwise (KIND_MFFT, K = 8): each point's ring product is
     // three full convolutions of length S = 4 instead of the K^2 negacyclic
     // terms -- 48 plane products per point, 16 at the half points; njobs is
-    // then the NB * 21 job planes, macs_per_elem the issued MACs
+    // then the NB * 21 job planes, macs_per_elem the issued MACs.  kara = 2
+    // splits P0 and P1 once more into three length-2 convolutions each (40
+    // plane products per point, 12 at the half points, NB * 25 job planes).
     int kara;
 };
 
@@ -79,10 +81,13 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced
 // Whether the Karatsuba pointwise keeps the plan exact: one int8 digit per
 // transformed value with room for the sums a0 + a1 (2 |x| <= 127), K = 8,
 // one contraction chunk, and every int32 accumulator of P2 = (a0+a1)(b0+b1)
-// (4 terms of length n) below 2^31.
+// (4 terms of length n) below 2^31.  The second level needs nothing more:
+// its sums u0 + u1 are sums of two single digits like a0 + a1, and its
+// accumulators have at most 2 terms.
 bool plan_kara_ok(const Plan& p);
-// Switch a plan to / from the Karatsuba pointwise (job planes and issued MACs).
-void plan_set_kara(Plan& p, bool on);
+// Set a plan's Karatsuba level (0 = negacyclic, 1, 2; job planes and issued
+// MACs); a level the plan cannot take falls back to 0.
+void plan_set_kara(Plan& p, int level);
 // Whether job (t, ch) of a schoolbook plan has any term.
 inline bool school_job_live(const Plan& p, int t, int ch) {
     const int lo = t - (p.LbB - 1) > ch * p.U ? t - (p.LbB - 1) : ch * p.U;

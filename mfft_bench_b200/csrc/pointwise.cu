@@ -943,8 +943,13 @@ constexpr int PWK_B_BYTES = (PWK_BN / 2) * PW_BK;
 constexpr int PWK_STAGE_BYTES = PWK_NS * (PWK_A_BYTES + PWK_B_BYTES);
 constexpr int PWK_SMEM_BYTES = 1024 + PWK_STAGES * PWK_STAGE_BYTES + 256;
 
-__device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long tile, int& j, int& pr,
-                                                int& hi, int& mt, int& nt) {
+// A tile group of the Karatsuba kernel: kind 0 ("lo", 4 + 4 planes, output
+// coefficients 0..3 of a length-4 convolution), 1 ("hi", 3 + 3 planes,
+// coefficients 4..6) or 2 (a length-2 convolution of kara = 2: 2 + 2 planes,
+// coefficients 0..2, two k-blocks per stage); abase is its first operand
+// plane, qbase its first job plane.
+__device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long tile, int& kind,
+                                                int& abase, int& qbase, int& mt, int& nt) {
     const long long per_sj = (long long)p.tiles_m * p.tiles_n;
     int sj = (int)(tile / per_sj);
     const int r = (int)(tile % per_sj);
@@ -956,13 +961,27 @@ __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long til
     const int local = r % group;
     mt = first_m + local % gm;
     nt = local / gm;
+    int j;
     for (j = 0; j < p.jobs.NB; ++j) {
-        const int ng = pw_kara_half(p.jobs, j) ? 2 : 6;
+        const int ng = pw_kara_point_groups(p.jobs, pw_kara_half(p.jobs, j));
         if (sj < ng) break;
         sj -= ng;
     }
-    pr = sj >> 1;
-    hi = sj & 1;
+    if (p.jobs.kara == 2) {
+        if (sj < 6) {
+            kind = 2;
+            abase = j * PWK2_OPS + pw_kara2_qplane(sj);
+            qbase = j * PWK2_JOBS + 3 * sj;
+        } else {
+            kind = sj - 6;
+            abase = j * PWK2_OPS + 8 + kind;
+            qbase = j * PWK2_JOBS + 18 + 4 * kind;
+        }
+    } else {
+        kind = sj & 1;
+        abase = j * PWK_OPS + 4 * (sj >> 1) + kind;
+        qbase = j * PWK_JOBS + 7 * (sj >> 1) + 4 * kind;
+    }
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
@@ -1032,25 +1051,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                     }
                 }
             }
-            int j, pr, hi, mt, nt;
-            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
-            const int nsl = hi ? 3 : 4;   // planes per side: u, v in [hi, 3]
-            const int base = j * PWK_OPS + 4 * pr + hi;
-            const uint32_t stage_tx = 2u * (uint32_t)nsl * (PWK_A_BYTES + PWK_B_BYTES);
-            for (int kb = 0; kb < p.kblocks; ++kb) {
+            int kind, abase, qbase, mt, nt;
+            pwk_tile_decode(p, tile, kind, abase, qbase, mt, nt);
+            // planes per side and k-blocks per stage: lo u, v in [0, 3];
+            // hi u, v in [1, 3]; a length-2 convolution, u, v in [0, 1] for
+            // two consecutive k-blocks
+            const int nsl = kind == 2 ? 2 : (kind ? 3 : 4);
+            const int ksub = kind == 2 ? 2 : 1;
+            for (int kb = 0; kb < p.kblocks; kb += ksub) {
+                const int nk = kb + ksub <= p.kblocks ? ksub : 1;
+                const uint32_t stage_tx =
+                    2u * (uint32_t)(nk * nsl) * (PWK_A_BYTES + PWK_B_BYTES);
                 if (!mbar_wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag,
                                        global_timer_ns() + tmo))
                     goto producer_done;
                 const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
                 if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
                 uint8_t* st = smem + stage * PWK_STAGE_BYTES;
-                for (int i = 0; i < nsl; ++i) {
-                    tma_load_3d_pair(smem_u32(st + i * PWK_A_BYTES), &tmA, full_leader,
-                                     kb * PW_BK, mt * 256 + (int)rank * 128, base + i);
-                    tma_load_3d_pair(smem_u32(st + PWK_NS * PWK_A_BYTES + i * PWK_B_BYTES), &tmB,
-                                     full_leader, kb * PW_BK,
-                                     nt * PWK_BN + (int)rank * (PWK_BN / 2), base + i);
-                }
+                for (int h = 0; h < nk; ++h)
+                    for (int i = 0; i < nsl; ++i) {
+                        const int slot = h * nsl + i;
+                        tma_load_3d_pair(smem_u32(st + slot * PWK_A_BYTES), &tmA, full_leader,
+                                         (kb + h) * PW_BK, mt * 256 + (int)rank * 128, abase + i);
+                        tma_load_3d_pair(smem_u32(st + PWK_NS * PWK_A_BYTES + slot * PWK_B_BYTES),
+                                         &tmB, full_leader, (kb + h) * PW_BK,
+                                         nt * PWK_BN + (int)rank * (PWK_BN / 2), abase + i);
+                    }
                 issued_parity[stage] = (int)phase;
                 if (++stage == PWK_STAGES) {
                     stage = 0;
@@ -1071,17 +1097,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
         uint32_t phase = 0;
         uint32_t acc_phase = 0;
         for (long long tile = pair; tile < p.num_tiles && !*abort_flag; tile += npairs) {
-            int j, pr, hi, mt, nt;
-            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
+            int kind, abase, qbase, mt, nt;
+            pwk_tile_decode(p, tile, kind, abase, qbase, mt, nt);
+            const int hi = kind & 1;
+            const int ksub = kind == 2 ? 2 : 1;
             if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
-            for (int kb = 0; kb < p.kblocks; ++kb) {
+            for (int kb = 0; kb < p.kblocks; kb += ksub) {
                 if (!mbar_wait_bounded(bar_full + 8 * stage, phase, abort_flag,
                                        global_timer_ns() + tmo))
                     goto mma_done;
                 tc_fence_after();
                 const uint32_t st = smem_u32(smem + stage * PWK_STAGE_BYTES);
+                if (kind == 2) {
+                    // slots 2h + u (A) / 2h + v (B) hold k-block kb + h; the
+                    // term (u, v) belongs to accumulator u + v, started by
+                    // its first term in loop order -- (0,0), (0,1), (1,1) --
+                    // in k-block 0
+                    const int nk = kb + 2 <= p.kblocks ? 2 : 1;
+                    for (int h = 0; h < nk; ++h) {
+                        const uint32_t acc0 = kb + h != 0 ? 1u : 0u;
+#pragma unroll
+                        for (int ia = 0; ia < 2; ++ia) {
+#pragma unroll
+                            for (int ib = 0; ib < 2; ++ib) {
+                                const int accn = ia + ib;
+                                const bool init = ia == 0 || accn == 2;
+                                const uint32_t a0 = st + (2 * h + ia) * PWK_A_BYTES;
+                                const uint32_t b0 =
+                                    st + PWK_NS * PWK_A_BYTES + (2 * h + ib) * PWK_B_BYTES;
+#pragma unroll
+                                for (int kk = 0; kk < PW_BK / 32; ++kk)
+                                    mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
+                                                sdesc_kmajor_sw128(a0 + kk * 32),
+                                                sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                                (acc0 | (uint32_t)kk | (init ? 0u : 1u)) != 0
+                                                    ? 1u
+                                                    : 0u);
+                            }
+                        }
+                    }
+                    mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+                    if (++stage == PWK_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                    continue;
+                }
                 const uint32_t acc0 = kb != 0 ? 1u : 0u;  // the first k-block starts every sum
                 // slot i holds plane u = hi + i (A) / v = hi + i (B); the term
                 // (u, v) belongs to output s = u + v, accumulator s - 4 hi
@@ -1123,17 +1186,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
         const int half = (warp - 2) / 4;            // columns [64 half, 64 half + 64)
         uint32_t acc_phase = 0;
         for (long long tile = pair; tile < p.num_tiles; tile += npairs) {
-            int j, pr, hi, mt, nt;
-            pwk_tile_decode(p, tile, j, pr, hi, mt, nt);
+            int kind, abase, qbase, mt, nt;
+            pwk_tile_decode(p, tile, kind, abase, qbase, mt, nt);
             if (!mbar_wait_bounded(bar_tfull, acc_phase, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
             const int row = mt * 256 + (int)rank * 128 + quarter * 32 + lane;
             const int col0 = nt * PWK_BN;
             const int colmax = p.cols - col0;
-            const int nout = hi ? 3 : 4;
+            const int nout = kind == 0 ? 4 : 3;
             for (int a = 0; a < nout; ++a) {
-                const int q = j * PWK_JOBS + pr * 7 + 4 * hi + a;
+                const int q = qbase + a;
                 int32_t* orow = p.out + (long long)q * p.out_plane + (long long)row * p.ldo + col0;
                 {
                     const int c = half;
@@ -1208,7 +1271,8 @@ static int launch_kara(const PwLaunch& L, cudaStream_t stream) {
     // their outputs are not stored)
     if (L.jobs.K != 8 || L.jobs.dA != 1 || L.jobs.dB != 1 || L.jobs.nchunk != 1 ||
         L.num_sms < 2 || L.cols < 128 || L.map_rows < 256 || L.map_rows < L.rows ||
-        L.a_planes != L.jobs.NB * PWK_OPS || L.f_planes != L.jobs.NB * PWK_OPS)
+        L.a_planes != L.jobs.NB * pw_kara_ops(L.jobs) ||
+        L.f_planes != L.jobs.NB * pw_kara_ops(L.jobs))
         return MFFTB_ERR_ARG;
     if (L.chosen) *L.chosen = 4;
     PwParams p;
@@ -1385,12 +1449,29 @@ __global__ void pointwise_simt_check_kernel(const int8_t* A, long long lda, long
     int r = (int)((idx % per_job) / cols);
     int c = (int)(idx % cols);
     long long acc = 0;
-    if (J.kara) {  // q = j*21 + p*7 + s: sum over u + v = s of A(j,p,u) * B(j,p,v)
-        const int j = q / PWK_JOBS, pr = (q % PWK_JOBS) / 7, s = q % 7;
-        if (pr > 0 && pw_kara_half(J, j)) return;  // not computed at a half point
-        for (int u = s > 3 ? s - 3 : 0; u <= (s < 3 ? s : 3); ++u) {
-            const int8_t* a = A + (j * PWK_OPS + 4 * pr + u) * a_plane + r * lda;
-            const int8_t* f = F + (j * PWK_OPS + 4 * pr + (s - u)) * f_plane + c * ldf;
+    if (J.kara) {
+        // kara = 1: q = j*21 + p*7 + s, the sum over u + v = s (u, v < 4) of
+        // A(base + u) * B(base + v), base = j*12 + 4p.  kara = 2: q = j*25 +
+        // 3g + s (g < 6) sums u + v = s (u, v < 2) from the first plane of
+        // length-2 convolution g; q = j*25 + 18 + s is P2 (base j*16 + 8).
+        const int nq = pw_kara_jobs(J), ops = pw_kara_ops(J);
+        const int j = q / nq, off = q % nq;
+        int base, s, w;
+        if (J.kara == 2 && off < 18) {
+            base = j * ops + pw_kara2_qplane(off / 3);
+            s = off % 3;
+            w = 2;
+            if (off >= 9 && pw_kara_half(J, j)) return;  // P1: not at a half point
+        } else {
+            const int pr = J.kara == 2 ? 2 : off / 7;
+            base = j * ops + 4 * pr;
+            s = J.kara == 2 ? off - 18 : off % 7;
+            w = 4;
+            if (pr > 0 && pw_kara_half(J, j)) return;  // not computed at a half point
+        }
+        for (int u = s > w - 1 ? s - (w - 1) : 0; u <= (s < w - 1 ? s : w - 1); ++u) {
+            const int8_t* a = A + (base + u) * a_plane + r * lda;
+            const int8_t* f = F + (base + (s - u)) * f_plane + c * ldf;
             for (int k = 0; k < kdim; ++k) acc += (long long)a[k] * (long long)f[k];
         }
         int32_t got = out[q * out_plane + (long long)r * ldo + c];

@@ -67,20 +67,50 @@ struct PwJobs {
     // a0[0..3], a1[0..3], (a0+a1)[0..3] (the same for B), and product p's
     // output coefficient s (s = 0..6) goes to job plane j*21 + p*7 + s; the
     // inverse combines them into Chat_j.
+    //
+    // kara = 2 applies the same split once more to P0 and P1, whose operands
+    // are single digits (|x| <= 60, so x[c] + x[c+2] still fits int8): with
+    // a0 = u0 + z^2 u1 (z = y), P0 = Q0 + z^2 (Q2 - Q0 - Q1) + z^4 Q1 for the
+    // three length-2 convolutions Q0 = u0*v0, Q1 = u1*v1,
+    // Q2 = (u0+u1)*(v0+v1), 12 plane products instead of 16 (P2's operands
+    // are already sums and stay one level deep).  The operands are 16 planes
+    // per point: the 12 above, then a0[0]+a0[2], a0[1]+a0[3], a1[0]+a1[2],
+    // a1[1]+a1[3]; the job planes are 25 per point: Q0, Q1, Q2 of P0
+    // (3 coefficients each, planes j*25 + 0..8), of P1 (9..17), then P2's 7
+    // (18..24).
     int kara;
 };
 
-constexpr int PWK_OPS = 12;   // operand planes per point in Karatsuba mode
-constexpr int PWK_JOBS = 21;  // job planes per point in Karatsuba mode
+constexpr int PWK_OPS = 12;    // operand planes per point, kara = 1
+constexpr int PWK_JOBS = 21;   // job planes per point, kara = 1
+constexpr int PWK2_OPS = 16;   // operand planes per point, kara = 2
+constexpr int PWK2_JOBS = 25;  // job planes per point, kara = 2
+
+__host__ __device__ inline int pw_kara_ops(const PwJobs& J) {
+    return J.kara == 2 ? PWK2_OPS : PWK_OPS;
+}
+__host__ __device__ inline int pw_kara_jobs(const PwJobs& J) {
+    return J.kara == 2 ? PWK2_JOBS : PWK_JOBS;
+}
+// kara = 2: the first operand plane of length-2 convolution g (g = 0..5:
+// Q0, Q1, Q2 of P0, then of P1) within a point's 16
+__host__ __device__ inline int pw_kara2_qplane(int g) {
+    return g == 2 ? 12 : (g == 5 ? 14 : (g < 2 ? 2 * g : 2 * g - 2));
+}
 
 // Karatsuba mode: the half points (j = 0, NB/2) need P0 only
 __host__ __device__ inline bool pw_kara_half(const PwJobs& J, int j) {
     return j == 0 || 2 * j == J.NB;
 }
-// tile groups (product p, output half hi) of all points: 6 per ordinary
-// point, 2 per half point
+// tile groups per point: kara = 1, (product p, output half hi), 6 per
+// ordinary point, 2 per half point; kara = 2, the six length-2 convolutions
+// and P2's two halves, 8 per ordinary point, 3 per half point
+__host__ __device__ inline int pw_kara_point_groups(const PwJobs& J, bool half) {
+    return J.kara == 2 ? (half ? 3 : 8) : (half ? 2 : 6);
+}
 __host__ __device__ inline int pw_kara_groups(const PwJobs& J) {
-    return J.NB <= 2 ? 2 * J.NB : 6 * J.NB - 8;
+    const int nhalf = J.NB <= 2 ? J.NB : 2;
+    return nhalf * pw_kara_point_groups(J, true) + (J.NB - nhalf) * pw_kara_point_groups(J, false);
 }
 
 __host__ __device__ inline bool pw_half_point(const PwJobs& J, int j) {

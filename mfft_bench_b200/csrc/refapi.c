@@ -249,6 +249,160 @@ void mfft_plan_describe(const mfft_plan *p, int n)
                (long long)pi.NB * pi.K * pi.K * pi.dA * pi.dB, pi.LbA * pi.LbB);
 }
 
+/* ------------------------------------------------------------------ recursive plan
+ * src/mfft.c:449-527,665-686.  The reference's recursive plan solves each
+ * point's negacyclic convolution of length 2^k either by Karatsuba (3^k
+ * products) or by splitting it into 2^nu blocks carried in a ring of length
+ * 2^(k+1-nu) whose block products recurse one level down (2^nu times the
+ * cost below); a choice whose int64 intermediates could pass 62 bits is
+ * refused.  The cost model and its tie rules are kept so that a recursive plan
+ * has the reference's S, NB, K and product count.  The product itself runs on
+ * the B200 path like every other plan: the exact result does not depend on
+ * the plan, and the GPU's own planner picks the int8 schedule (whose ring
+ * products are themselves split by Karatsuba on the W = 64 plan). */
+enum { NEG_KMAX = 26, NEG_MMAX = 74 }; /* the reference's table bounds, mfft.c:480-481 */
+
+typedef struct {
+    long long cost;
+    int outbits, maxbits, ok;
+} negcost;
+
+typedef struct {
+    negcost v[NEG_KMAX][NEG_MMAX];
+    unsigned char done[NEG_KMAX][NEG_MMAX];
+    int ln; /* ceil(log2 n) */
+} negmemo;
+
+static negcost neg_cost(negmemo *m, int k, int mbits)
+{
+    negcost none = {0, 0, 0, 0};
+    if (k < 0 || k >= NEG_KMAX || mbits < 0 || mbits >= NEG_MMAX) return none;
+    if (m->done[k][mbits]) return m->v[k][mbits];
+    negcost best = none;
+    /* Karatsuba on the whole convolution: the folded result needs
+     * 1 + k + ln + 2 mbits bits, its intermediates one more */
+    const int kbits = 2 + k + m->ln + 2 * mbits;
+    if (kbits <= 62) {
+        long long c = 1;
+        for (int i = 0; i < k; i++) c *= 3;
+        best.cost = c;
+        best.outbits = kbits - 1;
+        best.maxbits = kbits;
+        best.ok = 1;
+    }
+    for (int nu = 2; 2 * nu <= k + 1; nu++) {
+        negcost sub = neg_cost(m, k + 1 - nu, mbits + nu);
+        if (!sub.ok) continue;
+        const int top = sub.maxbits > nu + sub.outbits ? sub.maxbits : nu + sub.outbits;
+        if (top > 62) continue;
+        const long long c = ((long long)1 << nu) * sub.cost;
+        if (!best.ok || c < best.cost) {
+            best.cost = c;
+            best.outbits = sub.outbits + 1;
+            best.maxbits = top;
+            best.ok = 1;
+        }
+    }
+    m->done[k][mbits] = 1;
+    m->v[k][mbits] = best;
+    return best;
+}
+
+int mfft_plan_init_rec(mfft_plan *p, int L, int n, int sigma_override)
+{
+    if (!p || L < 2 || (L & (L - 1))) return -1;
+    negmemo *m = calloc(1, sizeof *m);
+    if (!m) return -1;
+    m->ln = ilog2i(n);
+    const int l = ilog2i(L);
+    long long best = -1;
+    int pick = 0;
+    for (int sigma = 1; sigma < l; sigma++) {
+        const int S = 1 << sigma, NB = 2 * L / S, K = 2 * S;
+        if (2 * S * S < L || (2 * K) % NB || NB < 2) continue;
+        if (sigma_override > 0 && sigma != sigma_override) continue;
+        const negcost c = neg_cost(m, sigma + 1, LIMB_BITS + ilog2i(NB));
+        if (!c.ok) continue;
+        const long long total = (long long)NB * c.cost;
+        if (best < 0 || total < best) {
+            best = total;
+            pick = sigma;
+        }
+    }
+    free(m);
+    if (best < 0) return -1;
+    p->L = L;
+    p->S = 1 << pick;
+    p->NB = 2 * L / p->S;
+    p->K = 2 * p->S;
+    p->g = 2 * p->K / p->NB;
+    p->rec = 1;
+    p->nprod = best;
+    return 0;
+}
+
+/* src/mfft.c:560-662: C = A * B mod (y^K + 1), A and B K int32 planes of
+ * n x n matrices, C K int64 planes.  It runs on the GPU as one limb
+ * convolution: every int32 entry x splits into signed 16-bit limbs
+ * x = 2^16 h + l, coefficient u of A (and of B) becomes limbs 3u (l) and
+ * 3u + 1 (h), with limb 3u + 2 left zero so that the limb products of
+ * different coefficient pairs never share a slot; then
+ * lin[t] = Cw[3t] + 2^16 Cw[3t+1] + 2^32 Cw[3t+2] (modulo 2^64, exact where
+ * the product fits int64, as the reference requires) and
+ * C[w] = lin[w] - lin[w + K]. */
+void ssa_negconv(int64_t *C, const int32_t *A, const int32_t *B, int K, int n, int Mbits,
+                 kernel_t kern)
+{
+    (void)Mbits;
+    (void)kern;
+    if (!C || !A || !B || K < 1 || n < 1) {
+        finish(NULL, MFFTGPU_ERR_ARG, "ssa_negconv");
+        return;
+    }
+    const size_t nn = (size_t)n * n;
+    const int Lx = 3 * K - 1, P = 2 * Lx - 1;
+    int32_t *As = calloc((size_t)Lx * nn, sizeof(int32_t));
+    int32_t *Bs = calloc((size_t)Lx * nn, sizeof(int32_t));
+    int64_t *Cw = malloc((size_t)P * nn * sizeof(int64_t));
+    mfftgpu_ctx *c = (As && Bs && Cw) ? default_ctx() : NULL;
+    int rc = !(As && Bs && Cw) ? MFFTGPU_ERR_NOMEM : (c ? 0 : g_status);
+    if (c) {
+        for (int u = 0; u < K; u++)
+            for (size_t i = 0; i < nn; i++) {
+                const int32_t a = A[(size_t)u * nn + i], b = B[(size_t)u * nn + i];
+                const int32_t al = (int16_t)(uint16_t)((uint32_t)a & 0xFFFFu);
+                const int32_t bl = (int16_t)(uint16_t)((uint32_t)b & 0xFFFFu);
+                As[(size_t)(3 * u) * nn + i] = al;
+                As[(size_t)(3 * u + 1) * nn + i] = (int32_t)(((int64_t)a - al) >> 16);
+                Bs[(size_t)(3 * u) * nn + i] = bl;
+                Bs[(size_t)(3 * u + 1) * nn + i] = (int32_t)(((int64_t)b - bl) >> 16);
+            }
+        mfftgpu_set_profile(c, g_mfft_profile ? 1 : 0);
+        rc = mfftgpu_conv_i32(c, As, Bs, n, Lx, Cw);
+    }
+    if (!finish(c, rc, "ssa_negconv")) {
+        for (int w = 0; w < K; w++)
+            for (size_t i = 0; i < nn; i++) {
+                uint64_t v = 0;
+                for (int hi = 0; hi < 2; hi++) {
+                    const int t = w + hi * K;
+                    if (t > 2 * K - 2) break;
+                    const uint64_t lin = (uint64_t)Cw[(size_t)(3 * t) * nn + i] +
+                                         ((uint64_t)Cw[(size_t)(3 * t + 1) * nn + i] << 16) +
+                                         ((uint64_t)Cw[(size_t)(3 * t + 2) * nn + i] << 32);
+                    v = hi ? v - lin : v + lin;
+                }
+                C[(size_t)w * nn + i] = (int64_t)v;
+            }
+        account(c, n, 1, Lx, Lx);
+    } else {
+        memset(C, 0, (size_t)K * nn * sizeof(int64_t));
+    }
+    free(As);
+    free(Bs);
+    free(Cw);
+}
+
 /* ------------------------------------------------------------------ products */
 void mm_mfft(const uint16_t *Apl, const uint16_t *Bpl, int n, int L, const mfft_plan *p,
              kernel_t k, uint16_t *out, int RL)

@@ -230,6 +230,8 @@ class RefLib:
         L.mfft_plan_init.argtypes = [C.POINTER(RefPlan), C.c_int, C.c_int]
         L.mm_mfft.argtypes = [_u16p, _u16p, C.c_int, C.c_int, C.POINTER(RefPlan), C.c_int,
                               _u16p, C.c_int]
+        L.mfft_plan_init_rec.argtypes = [C.POINTER(RefPlan), C.c_int, C.c_int, C.c_int]
+        L.ssa_negconv.argtypes = [_i64p, _i32p, _i32p, C.c_int, C.c_int, C.c_int, C.c_int]
         L.mm_limbplane.argtypes = [_u16p, _u16p, C.c_int, C.c_int, C.c_int, _u16p, C.c_int]
         L.conv_mfft.argtypes = [_i64p, _i32p, _i32p, C.c_int, C.c_int, C.POINTER(RefPlan),
                                 C.c_int]
@@ -253,15 +255,29 @@ class RefLib:
             return None
         return p
 
+    def plan_rec(self, L, n, sigma=0):
+        """src/mfft.c:665-686, the recursive plan."""
+        p = RefPlan()
+        if self.lib.mfft_plan_init_rec(C.byref(p), L, n, sigma) != 0:
+            return None
+        return p
+
+    def ssa_negconv(self, A32, B32, K, n, Mbits, kernel=KERNEL_PACKED):
+        """src/mfft.c:560-662: A * B mod (y^K + 1) over n x n int32 planes."""
+        out = np.zeros(K * n * n, np.int64)
+        self.lib.ssa_negconv(out, np.ascontiguousarray(A32, np.int32),
+                             np.ascontiguousarray(B32, np.int32), K, n, Mbits, kernel)
+        return out
+
     def bigmat_rand(self, n, L, seed):
         m = np.empty(n * n * L, np.uint16)
         self.lib.bigmat_rand(m, n, L, seed)
         return m
 
-    def mm_mfft(self, A, B, n, L, RL=None, kernel=KERNEL_PACKED):
+    def mm_mfft(self, A, B, n, L, RL=None, kernel=KERNEL_PACKED, plan=None):
         RL = RL or 2 * L + 1
         out = np.zeros(RL * n * n, np.uint16)
-        self.lib.mm_mfft(A, B, n, L, C.byref(self.plan(L)), kernel, out, RL)
+        self.lib.mm_mfft(A, B, n, L, C.byref(plan or self.plan(L)), kernel, out, RL)
         return out
 
     def mm_limbplane(self, A, B, n, L, RL=None, kernel=KERNEL_PACKED):

@@ -40,6 +40,18 @@ def test_plan_init_semantics(oracle):
                 assert (p.S, p.NB, p.K, p.g, p.nprod, p.rec) == (q.S, q.NB, q.K, q.g, q.nprod, 0)
 
 
+def test_plan_init_rec_known_answers():
+    """The recursive plans of the benchmark shapes, as the reference's own
+    mfft_plan_init_rec (src/mfft.c:665-686) gives them: (L, n) -> S, NB, K,
+    products."""
+    for (L, n), want in {(512, 64): (16, 64, 32, 15552), (16, 1024): (4, 8, 8, 216),
+                         (64, 4096): (8, 16, 16, 1296), (4, 16384): (2, 4, 4, 36),
+                         (32, 8192): (4, 16, 8, 432)}.items():
+        p = m.mfft_plan_init_rec(L, n)
+        assert (p.S, p.NB, p.K, p.nprod, p.rec, p.g) == want + (1, 2 * want[2] // want[1])
+    assert m.mfft_plan_init_rec(3, 64) is None and m.mfft_plan_init_rec(2, 64) is None
+
+
 def test_bigmat_rand_matches_reference_stream(oracle):
     for n, L, seed in ((5, 3, 12345), (16, 64, 12345 ^ 0xABCDEF), (1, 1, 0)):
         assert np.array_equal(m.bigmat_rand(n, L, seed), oracle.bigmat_rand(n, L, seed))
@@ -110,13 +122,17 @@ def test_plan_exactness_invariants(n, mode, w):
     if pi["kara"]:
         # Karatsuba pointwise: three full length-S convolutions per ordinary
         # point, one per half point; the sums a0 + a1 fit int8 and P2's
-        # accumulators (S terms of length n) fit int32
+        # accumulators (S terms of length n) fit int32.  The default level 2
+        # takes P0 (and P1) as three length-S/2 convolutions: their sums are
+        # of two single digits again, with at most S/2 terms per accumulator.
         NB, S = pi["NB"], pi["S"]
         assert pi["K"] == 8 and pi["dA"] == pi["dB"] == 1 and pi["nchunk"] == 1 and NB <= 8
         assert 2 * MA <= 127 and 2 * pi["ncB"] * dmax <= 127
         assert S * pi["n_int"] * (2 * MA) * (2 * pi["ncB"] * dmax) < 2 ** 31
-        assert pi["njobs"] == NB * 21
-        assert pi["int8_macs"] == (3 * S * S * (NB - 2) + 2 * S * S) * float(pi["n_int"]) ** 3
+        assert pi["kara"] == 2 and pi["njobs"] == NB * 25
+        q = 3 * (S // 2) ** 2
+        nh = min(NB, 2)
+        assert pi["int8_macs"] == ((2 * q + S * S) * (NB - nh) + q * nh) * float(pi["n_int"]) ** 3
     else:
         assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
         assert pi["int8_macs"] == (pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"]

@@ -86,7 +86,7 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
     same bits, and match the oracle's exact entries."""
     gen = oracle.signed_planes if signed else oracle.bigmat_rand
     A, B = gen(n, L, 71 + n), gen(n, L, 73 + L)
-    ctx.set_karatsuba(False)  # the t-grouped kernel's own half-point skip
+    ctx.set_karatsuba(0)  # the t-grouped kernel's own half-point skip
     ctx.set_half_points(0)
     try:
         dense = ctx.mm_u16(A, B, n, L, signed=signed).reshape(2 * L + 1, n, n)
@@ -96,7 +96,7 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
         ph = ctx.last_plan()
     finally:
         ctx.set_half_points(1)
-        ctx.set_karatsuba(True)
+        ctx.set_karatsuba(2)
     assert ph["pw_kernel"] == 3 and ph["half_points"] == 1 and pd["half_points"] == 0
     NB, K, S = ph["NB"], ph["K"], ph["S"]
     assert ph["int8_macs"] == pytest.approx(pd["int8_macs"] * ((NB - 2) * K * K + 2 * S * S)
@@ -403,19 +403,26 @@ def test_host_entry_points_chunked_readback(ctx):
     (300, 272, 1000, 8),   # ragged rows, columns and contraction
     (512, 256, 2048, 4),
     (100, 128, 256, 2),    # fewer rows than one pair tile
+    (256, 144, 640, 8),    # 5 k-blocks: level 2's last stage holds one
+    (300, 128, 100, 4),    # a single, partial k-block
 ])
-def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB):
+@pytest.mark.parametrize("level", [1, 2])
+def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
     """The Karatsuba plane-product kernel on random int8 operand planes
-    (NB * 12 per side) against a CUDA-core evaluation of its job table:
-    P0, P1, P2 of every ordinary point, P0 of the half points."""
-    assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256, variant=4) == 0
+    against a CUDA-core evaluation of its job table.  Level 1 (NB * 12 planes
+    per side): P0, P1, P2 of every ordinary point, P0 of the half points.
+    Level 2 (NB * 16): the length-2 convolutions Q0, Q1, Q2 of P0 and P1 (two
+    k-blocks per pipeline stage, an odd k-block count included) and P2."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256,
+                                  variant=3 + level) == 0
 
 
 @pytest.mark.parametrize("n,kind", [(256, "i64"), (300, "i64"), (1000, "i64"), (2112, "i64"),
                                     (512, "u16s"), (384, "u16")])
 def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
-    """Whole W=64 products with the Karatsuba pointwise (the default for this
-    plan) and without it are the same bits, and match the oracle."""
+    """Whole W=64 products with the two-level Karatsuba pointwise (the
+    default for this plan), with one level (also through the lane inverse)
+    and without it are the same bits, and match the oracle."""
     if kind == "i64":
         A, B = oracle.int64_entries(n, 5 + n), oracle.int64_entries(n, 7 + n)
         run = lambda: ctx.mm_i64(A, B, n, RL=9)  # noqa: E731
@@ -427,21 +434,24 @@ def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
         run = lambda: ctx.mm_u16(Ap, Bp, n, 4, signed=signed)  # noqa: E731
     got = run()
     pk = ctx.last_plan()
-    assert pk["kara"] == 1 and pk["pw_kernel"] == 4
-    assert pk["int8_macs"] == 320 * float(pk["n_int"]) ** 3
-    ctx.set_kernel_variant("inverse", 2)  # the lane inverse on the Karatsuba job planes
+    assert pk["kara"] == 2 and pk["pw_kernel"] == 4
+    assert pk["int8_macs"] == 264 * float(pk["n_int"]) ** 3
+    ctx.set_karatsuba(1)
     try:
+        one = run()
+        assert ctx.last_plan()["kara"] == 1
+        assert ctx.last_plan()["int8_macs"] == 320 * float(pk["n_int"]) ** 3
+        ctx.set_kernel_variant("inverse", 2)  # the lane inverse on level-1 job planes
         lane = run()
         assert ctx.last_plan()["kara"] == 1
-    finally:
-        ctx.set_kernel_variant("inverse", 0)
-    assert np.array_equal(lane, got)
-    ctx.set_karatsuba(False)
-    try:
+        ctx.set_karatsuba(0)
         ref = run()
         assert ctx.last_plan()["kara"] == 0
     finally:
-        ctx.set_karatsuba(True)
+        ctx.set_kernel_variant("inverse", 0)
+        ctx.set_karatsuba(2)
+    assert np.array_equal(one, got)
+    assert np.array_equal(lane, got)
     assert np.array_equal(got, ref)
     rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 2000)]
     cols = np.tile(np.arange(n), n)[:: max(1, n * n // 2000)]

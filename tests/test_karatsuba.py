@@ -71,6 +71,42 @@ def test_karatsuba_identity(half):
             assert P0 + [0] == want  # the half points read P0 alone
 
 
+def _expand2(Q0, Q1, Q2):
+    """A length-4 convolution from its three length-2 ones, as the register
+    inverse kernel forms it: P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1."""
+    M = [Q2[s] - Q0[s] - Q1[s] for s in range(3)]
+    return [Q0[0], Q0[1], Q0[2] + M[0], M[1], Q1[0] + M[2], Q1[1], Q1[2]]
+
+
+def _conv2(a, b):
+    return [a[0] * b[0], a[0] * b[1] + a[1] * b[0], a[1] * b[1]]
+
+
+@pytest.mark.parametrize("half", [False, True])
+def test_two_level_karatsuba_identity(half):
+    """Level 2: P0 and P1 from three length-2 convolutions each (their
+    operands are single transformed digits, |x| <= 60, so the sums fit int8);
+    P2's operands are sums already and stay one level deep."""
+    rng = random.Random(11 + half)
+    for _ in range(2000):
+        a = [rng.randint(-60, 60) for _ in range(8)]
+        b = [rng.randint(-60, 60) for _ in range(8)]
+        if half:
+            a[4:] = b[4:] = [0] * 4
+        P = []
+        for lo in (0, 4):
+            u0, u1 = a[lo:lo + 2], a[lo + 2:lo + 4]
+            v0, v1 = b[lo:lo + 2], b[lo + 2:lo + 4]
+            su = [u0[i] + u1[i] for i in range(2)]
+            sv = [v0[i] + v1[i] for i in range(2)]
+            assert max(map(abs, su + sv)) <= 120  # the int8 operands of Q2
+            P.append(_expand2(_conv2(u0, v0), _conv2(u1, v1), _conv2(su, sv)))
+            assert P[-1] == _conv4(a[lo:lo + 4], b[lo:lo + 4])
+        sa = [a[i] + a[i + 4] for i in range(4)]
+        sb = [b[i] + b[i + 4] for i in range(4)]
+        assert _recombine(P[0], P[1], _conv4(sa, sb)) == _negacyclic(a, b)
+
+
 def test_karatsuba_extremes():
     """All-extreme operands: every job value and the recombined coefficients
     stay within the int32 accumulator and int64 inverse bounds the planner
@@ -90,9 +126,10 @@ def test_karatsuba_extremes():
 def test_planner_uses_karatsuba_on_the_w64_plan():
     pi = m.plan_info(16384, 0, 64)
     assert (pi["b"], pi["S"], pi["NB"], pi["K"], pi["dA"]) == (4, 4, 8, 8, 1)
-    assert pi["kara"] == 1 and pi["njobs"] == 8 * 21
-    # 6 ordinary points x 3 x 16 + 2 half points x 16 = 320 plane products
-    assert pi["int8_macs"] == 320 * 16384.0 ** 3
+    assert pi["kara"] == 2 and pi["njobs"] == 8 * 25
+    # 6 ordinary points x (2 x 12 + 16) + 2 half points x 12 = 264 plane
+    # products (one level: 6 x 48 + 2 x 16 = 320; none: 8 x 64 = 512)
+    assert pi["int8_macs"] == 264 * 16384.0 ** 3
     # past n ~ 37000 the P2 accumulators (4 * n * 120^2) would pass 2^31
     assert m.plan_info(40000, 0, 64)["kara"] == 0
     # plans whose transformed sums do not leave room for a0 + a1 keep the

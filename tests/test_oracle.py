@@ -134,6 +134,21 @@ def test_plan_init_matches_reference(oracle, reflib):
                 assert (a.S, a.NB, a.K, a.g, a.nprod) == (b.S, b.NB, b.K, b.g, b.nprod)
 
 
+def test_plan_init_rec_matches_reference(reflib):
+    """The drop-in recursive planner against the reference's (its Karatsuba /
+    block-split cost model and int64 refusals), over powers of two and
+    non-powers, matrix sizes from 1 to 2^20 and every sigma override."""
+    import mfft_bench_b200 as m
+    for L in (1, 2, 3, 4, 8, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096):
+        for n in (1, 2, 3, 64, 100, 1024, 4096, 16384, 65536, 1 << 20):
+            for sigma in range(0, 13):
+                a, b = m.mfft_plan_init_rec(L, n, sigma), reflib.plan_rec(L, n, sigma)
+                assert (a is None) == (b is None), (L, n, sigma)
+                if a is not None:
+                    assert (a.S, a.NB, a.K, a.g, a.nprod, a.rec) == \
+                        (b.S, b.NB, b.K, b.g, b.nprod, b.rec), (L, n, sigma)
+
+
 def test_oracle_vs_reference_unsigned_random(oracle, reflib):
     """mm_mfft of the restatement against the reference's mm_mfft and
     mm_limbplane on the reference's own generator, including outputs shorter
