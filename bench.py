@@ -76,27 +76,35 @@ def env_int(k, d):
 
 # DRAM bytes (read + write) of one plane-product launch (one row block), from
 # a one-pass ncu capture of dram__bytes_read.sum / dram__bytes_write.sum on
-# the full workload (one pass checked on n = 4096 first), keyed by workload
-# and kernel (3 t-grouped, 4 Karatsuba).
+# the full workload (one pass checked on n = 4096 first), keyed by workload,
+# kernel (3 t-grouped, 4 Karatsuba) and Karatsuba level.
 POINTWISE_TRAFFIC = {
-    ("c5", 4): {"bytes_per_launch": 310.06e9 + 52.87e9,
-                "note": ("ncu, the second launch of a 1-GPU product (a row block of the plan's "
-                         "rblock rows x 16384 columns), Karatsuba kernel: 310.1 GB read + 52.9 GB "
-                         "written in 363 ms; algorithmic: 96 A operand planes of the block + 96 B "
-                         "operand planes (about 34 GB) read, 140 int32 job planes per element of "
-                         "the block written")},
-    ("c5", 3): {"bytes_per_launch": 848.51e9 + 52.15e9,
-                "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows), "
-                         "t-grouped kernel with the half-point terms skipped: 848.5 GB read + "
-                         "52.2 GB written; algorithmic operand bytes of that launch 43.9 GB read "
-                         "+ 46.7 GB of int32 job planes written")},
+    ("c5", 4, 2): {"bytes_per_launch": 197.62e9 + 45.51e9,
+                   "note": ("ncu, the second launch of a 1-GPU product (a row block of 4096 rows "
+                            "x 16384 columns), two-level Karatsuba kernel: 197.6 GB read + "
+                            "45.5 GB written in 210.5 ms; algorithmic: 128 A operand planes of "
+                            "the block + 128 B operand planes (43.0 GB) read, 168 int32 job "
+                            "planes per element of the block (45.1 GB) written")},
+    ("c5", 4, 1): {"bytes_per_launch": 310.06e9 + 52.87e9,
+                   "note": ("ncu, the second launch of a 1-GPU product (a row block of the "
+                            "plan's rblock rows x 16384 columns), one-level Karatsuba kernel: "
+                            "310.1 GB read + "
+                            "52.9 GB written in 363 ms; algorithmic: 96 A operand planes of the "
+                            "block + 96 B operand planes (about 34 GB) read, 140 int32 job "
+                            "planes per element of the block written")},
+    ("c5", 3, 0): {"bytes_per_launch": 848.51e9 + 52.15e9,
+                   "note": ("ncu, first row block of a 1-GPU product (11136 of 16384 rows), "
+                            "t-grouped kernel with the half-point terms skipped: 848.5 GB read + "
+                            "52.2 GB written; algorithmic operand bytes of that launch 43.9 GB "
+                            "read + 46.7 GB of int32 job planes written")},
 }
 
 PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
               2: "pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)",
               3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)",
-              4: "pointwise_kara_i8_kernel (tcgen05 cta_group::2 kind::i8, Karatsuba: 3 full "
-                 "length-4 convolutions per point)"}
+              4: "pointwise_kara_i8_kernel (tcgen05 cta_group::2 kind::i8, Karatsuba: 3 "
+                 "length-4 convolutions per point, at level 2 the first two as 3 length-2 "
+                 "convolutions each)"}
 
 
 def load_peaks():
@@ -813,7 +821,7 @@ def main():
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share
-    tr = POINTWISE_TRAFFIC.get((args.workload, pi.get("pw_kernel")))
+    tr = POINTWISE_TRAFFIC.get((args.workload, pi.get("pw_kernel"), pi.get("kara", 0)))
     if ("roofline" in line and tr and world == 1 and n == DEFAULT_N[args.workload]
             and pi.get("kind") == 0):
         line["roofline"]["traffic"] = tr["bytes_per_launch"]

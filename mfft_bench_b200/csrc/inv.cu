@@ -223,7 +223,9 @@ __device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane
     P[6] = q1[2];
 }
 
-template <int NB, int K>
+// KARA: the Karatsuba level of the job planes (0: NB*K negacyclic planes),
+// a template argument so that every load of a point is issued back to back
+template <int NB, int K, int KARA>
 __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
     constexpr int S = K / 2, LGNB = NB == 2 ? 1 : (NB == 4 ? 2 : 3);
     const long long e = blockIdx.x * 128LL + threadIdx.x;
@@ -240,19 +242,18 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
         return LGNB == 1 ? j : (LGNB == 2 ? (((j & 1) << 1) | (j >> 1))
                                           : (((j & 1) << 2) | (j & 2) | (j >> 2)));
     };
-    if constexpr (K == 8) {
-        if (a.kara) {
+    if constexpr (K == 8 && KARA > 0) {
+        {
             // Chat_j = P0 - P1 + y^4 (P2 - P0 - P1) mod y^8 + 1, with
             // M = P2 - P0 - P1: Chat[t] = D[t] - M[t+4] (t < 3), D[3] (t = 3),
-            // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1.  kara = 2
+            // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1.  Level 2
             // first forms P0 and P1 from their length-2 convolutions.
-            const bool two = a.kara == 2;
-            const int nq = two ? 25 : 21, p2 = two ? 18 : 14;
+            constexpr int NQ = KARA == 2 ? 25 : 21, P2 = KARA == 2 ? 18 : 14;
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
-                const int32_t* src = a.acc + (long long)j * nq * a.acc_plane + e;
+                const int32_t* src = a.acc + (long long)j * NQ * a.acc_plane + e;
                 int64_t P0[7];
-                if (two) {
+                if constexpr (KARA == 2) {
                     kara2_expand(src, a.acc_plane, P0);
                 } else {
 #pragma unroll
@@ -265,7 +266,7 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
                     continue;
                 }
                 int64_t P1[7], M[7];
-                if (two) {
+                if constexpr (KARA == 2) {
                     kara2_expand(src + 9 * a.acc_plane, a.acc_plane, P1);
                 } else {
 #pragma unroll
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
                 }
 #pragma unroll
                 for (int s = 0; s < 7; ++s)
-                    M[s] = (int64_t)__ldg(src + (long long)(p2 + s) * a.acc_plane) - P0[s] - P1[s];
+                    M[s] = (int64_t)__ldg(src + (long long)(P2 + s) * a.acc_plane) - P0[s] - P1[s];
                 int64_t(&y)[K] = x[bitrev(j)];
 #pragma unroll
                 for (int t = 0; t < 3; ++t) y[t] = P0[t] - P1[t] - M[t + 4];
@@ -788,12 +789,17 @@ static int try_lane(const InvArgs& a, cudaStream_t stream) {
     return MFFTB_ERR_UNSUPPORTED;
 }
 
-template <int NB, int K>
+template <int NB, int K, int KARA = 0>
 static int launch_reg(const InvArgs& a, cudaStream_t stream) {
     const long long total = (long long)a.rows * a.lda;
     const long long blocks = (total + 127) / 128;
-    if (blocks > 0) inverse_reg_kernel<NB, K><<<(unsigned)blocks, 128, 0, stream>>>(a);
+    if (blocks > 0) inverse_reg_kernel<NB, K, KARA><<<(unsigned)blocks, 128, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
+}
+
+template <int NB>
+static int launch_reg_kara(const InvArgs& a, cudaStream_t stream) {
+    return a.kara == 2 ? launch_reg<NB, 8, 2>(a, stream) : launch_reg<NB, 8, 1>(a, stream);
 }
 
 static int school_carry_launch(const InvArgs& a, cudaStream_t stream);
@@ -808,9 +814,9 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
             const int rc = try_lane(a, stream);
             if (rc != MFFTB_ERR_UNSUPPORTED) return rc;
         }
-        if (a.NB == 8) return launch_reg<8, 8>(a, stream);
-        if (a.NB == 4) return launch_reg<4, 8>(a, stream);
-        if (a.NB == 2) return launch_reg<2, 8>(a, stream);
+        if (a.NB == 8) return launch_reg_kara<8>(a, stream);
+        if (a.NB == 4) return launch_reg_kara<4>(a, stream);
+        if (a.NB == 2) return launch_reg_kara<2>(a, stream);
         return MFFTB_ERR_ARG;
     }
     const int NK = a.NB * a.K;
