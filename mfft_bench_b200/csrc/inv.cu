@@ -224,9 +224,12 @@ __device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane
 }
 
 // KARA: the Karatsuba level of the job planes (0: NB*K negacyclic planes),
-// a template argument so that every load of a point is issued back to back
+// a template argument so that every load of a point is issued back to back.
+// Level 2 (25 planes per point) is held to three blocks per SM (168
+// registers, a 32-byte spill): the loads in flight per SM matter more than
+// the spill (c5: 44.6 ms against 53.8 ms at two blocks per SM).
 template <int NB, int K, int KARA>
-__global__ void __launch_bounds__(128) inverse_reg_kernel(const InvArgs a) {
+__global__ void __launch_bounds__(128, KARA == 2 ? 3 : 1) inverse_reg_kernel(const InvArgs a) {
     constexpr int S = K / 2, LGNB = NB == 2 ? 1 : (NB == 4 ? 2 : 3);
     const long long e = blockIdx.x * 128LL + threadIdx.x;
     const long long total = (long long)a.rows * a.lda;
