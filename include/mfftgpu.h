@@ -64,7 +64,8 @@ typedef struct {
                                 product, counted as a schoolbook over 7-bit digits */
     int kara;                /* Karatsuba level: 1, three full length-4 convolutions per
                                 point (njobs = NB * 21 job planes); 2, the first two of them
-                                as three length-2 convolutions each (NB * 25); 0 off */
+                                as three length-2 convolutions each (NB * 25); 3, all three
+                                (NB * 27); 0 off */
     int rblock;              /* rows per row block of the last product (each block is one
                                 launch of every A-side kernel); 0 from mfftgpu_plan_info_get */
 } mfftgpu_plan_info;
@@ -118,15 +119,16 @@ int mfftgpu_ipc_free(void *ptr);
  *   2 the lane kernel wherever it covers the plan (also NB*K <= 64 plans,
  *   which auto gives the register kernel). */
 int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
-/* Karatsuba pointwise level (0, 1 or 2; the default 2, or $MFFTGPU_KARA).
+/* Karatsuba pointwise level (0 to 3; the default 3, or $MFFTGPU_KARA).
  * Plans with K = 8 and one int8 digit whose sums a0 + a1 still fit int8 (the
  * W = 64 configuration) take each point's ring product as three full
  * convolutions of length 4, P0 = a0 b0, P1 = a1 b1, P2 = (a0 + a1)(b0 + b1)
  * with a = a0 + y^4 a1: 48 plane products per point instead of 64, 16 at the
  * points 0 and NB/2 (level 1).  Level 2 splits P0 and P1 the same way into
- * three length-2 convolutions each (their operands are single digits, so
- * the sums still fit int8; P2's are sums already): 40 plane products per
- * point, 12 at the points 0 and NB/2.  Results are identical at every
+ * three length-2 convolutions each (their sums of two transformed values
+ * still fit int8): 40 plane products per point, 12 at the points 0 and NB/2.
+ * Level 3 splits P2 as well (a0 + a1 takes one digit per transform block,
+ * like a single value): 36 per point.  Results are identical at every
  * level; other values return MFFTGPU_ERR_ARG. */
 int mfftgpu_set_karatsuba(mfftgpu_ctx *ctx, int level);
 /* At the evaluation points 0 and NB/2 the transformed blocks keep only their
@@ -243,7 +245,7 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs, 4 the Karatsuba job
  * table (K = 8, one digit, one chunk: NB * 12 operand planes per side, NB * 21
  * job planes) on its CTA-pair kernel, 5 the same at level 2 (NB * 16 operand
- * planes, NB * 25 job planes).  *mismatches receives the number of
+ * planes, NB * 25 job planes), 6 at level 3 (NB * 18, NB * 27).  *mismatches receives the number of
  * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,

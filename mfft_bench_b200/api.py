@@ -127,7 +127,8 @@ class Context:
 
     def set_karatsuba(self, level):
         """Karatsuba pointwise level on plans that allow it: 0 off, 1 one
-        level (True), 2 P0 and P1 split again (the default); same bits."""
+        level (True), 2 P0 and P1 split again, 3 P2 as well (the default);
+        same bits."""
         self._check(lib.mfftgpu_set_karatsuba(self._h, int(level)), "set_karatsuba")
 
     def set_kernel_variant(self, stage, variant):

@@ -29,8 +29,8 @@
 using namespace mfftb;
 
 // Karatsuba level of the pointwise step where a plan allows it (the W = 64
-// plans): 2 splits P0 and P1 into length-2 convolutions as well
-constexpr int kDefaultKara = 2;
+// plans): 2 splits P0 and P1 into length-2 convolutions as well, 3 also P2
+constexpr int kDefaultKara = 3;
 
 struct mfftgpu_ctx {
     int device = 0;
@@ -177,7 +177,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     // row block R from the workspace limit: B's digit planes and operand
     // planes whole, A's digit and operand planes and the job planes per row
     auto size_blocks = [&]() {
-        const int kops = P.kara == 2 ? PWK2_OPS : PWK_OPS;
+        const int kops = pw_kara_level_ops(P.kara);
         fpl = school ? 0 : (P.kara ? P.NB * kops : P.NB * P.dB * (2 * P.K - 1));
         apl = school ? 0 : (P.kara ? P.NB * kops : P.NB * P.dA * P.K);
         szDB = align256((size_t)P.LbB * nn_int * dbytes);
@@ -559,7 +559,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_METHOD")) C->method = atoi(s);
     if (const char* s = getenv("MFFTGPU_KARA")) {
         const int v = atoi(s);
-        C->kara = v < 0 ? 0 : (v > 2 ? 2 : v);
+        C->kara = v < 0 ? 0 : (v > 3 ? 3 : v);
     }
     cudaMemset(C->d_err, 0, 256);
     *out = C;
@@ -669,7 +669,7 @@ int mfftgpu_set_half_points(mfftgpu_ctx* C, int on) {
 }
 
 int mfftgpu_set_karatsuba(mfftgpu_ctx* C, int level) {
-    if (!C || level < 0 || level > 2) return MFFTB_ERR_ARG;
+    if (!C || level < 0 || level > 3) return MFFTB_ERR_ARG;
     C->kara = level;
     return MFFTB_OK;
 }
@@ -1123,10 +1123,10 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     cudaSetDevice(C->device);
     const int ld = (kdim + 15) / 16 * 16;
     PwJobs J{K, dA, dB, dA + dB - 1, nchunk, NB * K * (dA + dB - 1) * nchunk};
-    // variants 4 and 5: the Karatsuba kernel (K = 8, one digit, one chunk)
-    // at level 1 / 2 on random operand planes, NB * 12 / NB * 16 per side; A
-    // planes span at least 256 rows
-    const bool kara = variant == 4 || variant == 5;
+    // variants 4, 5, 6: the Karatsuba kernel (K = 8, one digit, one chunk)
+    // at level 1 / 2 / 3 on random operand planes, NB * 12 / 16 / 18 per
+    // side; A planes span at least 256 rows
+    const bool kara = variant >= 4 && variant <= 6;
     if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;

@@ -23,7 +23,9 @@
 // (f_stack = 2, one digit) both operands are written as K + S planes per
 // point: Xhat[0..K-1], then Xhat[c] + Xhat[c+S] for c < S; with the second
 // Karatsuba level (f_stack = 3) S more follow: Xhat[c] + Xhat[c+S/2] for the
-// first S/2 coefficients c of each half (c = 0..S/2-1, then S..S+S/2-1).
+// first S/2 coefficients c of each half (c = 0..S/2-1, then S..S+S/2-1); with
+// f_stack = 4 S/2 more: s[c] + s[c+S/2] (c < S/2) of the sums s[c] =
+// Xhat[c] + Xhat[c+S].
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -96,7 +98,9 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                     for (int q = 0; q < 4; ++q) x[q] += sgn * v[q];
                 }
             };
-            const int per_j = a.f_stack == 3 ? a.K + 2 * a.S : a.K + a.S;
+            const int per_j = a.f_stack == 4   ? a.K + 2 * a.S + a.S / 2
+                              : a.f_stack == 3 ? a.K + 2 * a.S
+                                               : a.K + a.S;
             const long long base = (long long)j * per_j;
             for (int c = 0; c < a.S; ++c) {
                 int lo[4], hi[4];
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                 store4(a.out + (base + a.K + c) * a.oplane + e0, lo[0] + hi[0], lo[1] + hi[1],
                        lo[2] + hi[2], lo[3] + hi[3]);
             }
-            if (a.f_stack == 3) {
+            if (a.f_stack >= 3) {
                 const int h = a.S / 2;
                 for (int i = 0; i < a.S; ++i) {
                     const int c = (i / h) * a.S + i % h;  // first coefficient of the pair
@@ -116,6 +120,19 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                     coef(c + h, x1);
                     store4(a.out + (base + a.K + a.S + i) * a.oplane + e0, x0[0] + x1[0],
                            x0[1] + x1[1], x0[2] + x1[2], x0[3] + x1[3]);
+                }
+            }
+            if (a.f_stack == 4) {
+                const int h = a.S / 2;
+                for (int c = 0; c < h; ++c) {
+                    int t[4] = {0, 0, 0, 0}, v[4];
+                    const int idx[4] = {c, c + a.S, c + h, c + h + a.S};
+                    for (int q = 0; q < 4; ++q) {
+                        coef(idx[q], v);
+                        for (int e = 0; e < 4; ++e) t[e] += v[e];
+                    }
+                    store4(a.out + (base + a.K + 2 * a.S + c) * a.oplane + e0, t[0], t[1], t[2],
+                           t[3]);
                 }
             }
             continue;
@@ -207,7 +224,9 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
                 }
                 xs[c] = x;
             }
-            const long long base = (long long)j * (a.f_stack == 3 ? K + 2 * S : K + S);
+            const long long base =
+                (long long)j * (a.f_stack == 4 ? K + 2 * S + S / 2
+                                               : (a.f_stack == 3 ? K + 2 * S : K + S));
 #pragma unroll
             for (int c = 0; c < K; ++c)
                 *reinterpret_cast<uint32_t*>(a.out + (base + c) * a.oplane + e0) = xs[c];
@@ -215,7 +234,7 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
             for (int c = 0; c < S; ++c)
                 *reinterpret_cast<uint32_t*>(a.out + (base + K + c) * a.oplane + e0) =
                     __vadd4(xs[c], xs[c + S]);
-            if (a.f_stack == 3) {
+            if (a.f_stack >= 3) {
                 constexpr int H = S / 2 > 0 ? S / 2 : 1;
 #pragma unroll
                 for (int i = 0; i < S; ++i) {
@@ -223,6 +242,13 @@ __global__ void __launch_bounds__(256) forward_simd_kernel(const FwdArgs a) {
                     *reinterpret_cast<uint32_t*>(a.out + (base + K + S + i) * a.oplane + e0) =
                         __vadd4(xs[c], xs[c + H]);
                 }
+            }
+            if (a.f_stack == 4) {
+                constexpr int H = S / 2 > 0 ? S / 2 : 1;
+#pragma unroll
+                for (int c = 0; c < H; ++c)
+                    *reinterpret_cast<uint32_t*>(a.out + (base + K + 2 * S + c) * a.oplane + e0) =
+                        __vadd4(__vadd4(xs[c], xs[c + S]), __vadd4(xs[c + H], xs[c + H + S]));
             }
             continue;
         }
@@ -438,7 +464,7 @@ int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     if (a.nelem % 4 || a.d < 1 || a.d > 4) return MFFTB_ERR_ARG;
     // Karatsuba operands: one int8 digit per value, blocks of S = K/2
     if (a.f_stack >= 2 && (a.d != 1 || 2 * a.S != a.K)) return MFFTB_ERR_ARG;
-    if (a.f_stack == 3 && a.S < 2) return MFFTB_ERR_ARG;
+    if (a.f_stack >= 3 && a.S < 2) return MFFTB_ERR_ARG;
     const int threads = 256;
     long long blocks = (a.nelem / 4 + threads - 1) / threads;
     if (blocks <= 0) return MFFTB_OK;

@@ -225,11 +225,11 @@ __device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane
 
 // KARA: the Karatsuba level of the job planes (0: NB*K negacyclic planes),
 // a template argument so that every load of a point is issued back to back.
-// Level 2 (25 planes per point) is held to three blocks per SM (168
-// registers, a 32-byte spill): the loads in flight per SM matter more than
-// the spill (c5: 44.6 ms against 53.8 ms at two blocks per SM).
+// Levels 2 and 3 (25 / 27 planes per point) are held to three blocks per SM
+// (168 registers, a small spill): the loads in flight per SM matter more
+// than the spill (c5, level 2: 44.6 ms against 53.8 ms at two blocks per SM).
 template <int NB, int K, int KARA>
-__global__ void __launch_bounds__(128, KARA == 2 ? 3 : 1) inverse_reg_kernel(const InvArgs a) {
+__global__ void __launch_bounds__(128, KARA >= 2 ? 3 : 1) inverse_reg_kernel(const InvArgs a) {
     constexpr int S = K / 2, LGNB = NB == 2 ? 1 : (NB == 4 ? 2 : 3);
     const long long e = blockIdx.x * 128LL + threadIdx.x;
     const long long total = (long long)a.rows * a.lda;
@@ -251,12 +251,13 @@ __global__ void __launch_bounds__(128, KARA == 2 ? 3 : 1) inverse_reg_kernel(con
             // M = P2 - P0 - P1: Chat[t] = D[t] - M[t+4] (t < 3), D[3] (t = 3),
             // D[t] + M[t-4] (t = 4..6), M[3] (t = 7), D = P0 - P1.  Level 2
             // first forms P0 and P1 from their length-2 convolutions.
-            constexpr int NQ = KARA == 2 ? 25 : 21, P2 = KARA == 2 ? 18 : 14;
+            constexpr int NQ = KARA == 3 ? 27 : (KARA == 2 ? 25 : 21);
+            constexpr int P2 = KARA == 1 ? 14 : 18;
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
                 const int32_t* src = a.acc + (long long)j * NQ * a.acc_plane + e;
                 int64_t P0[7];
-                if constexpr (KARA == 2) {
+                if constexpr (KARA >= 2) {
                     kara2_expand(src, a.acc_plane, P0);
                 } else {
 #pragma unroll
@@ -269,16 +270,23 @@ __global__ void __launch_bounds__(128, KARA == 2 ? 3 : 1) inverse_reg_kernel(con
                     continue;
                 }
                 int64_t P1[7], M[7];
-                if constexpr (KARA == 2) {
+                if constexpr (KARA >= 2) {
                     kara2_expand(src + 9 * a.acc_plane, a.acc_plane, P1);
                 } else {
 #pragma unroll
                     for (int s = 0; s < 7; ++s)
                         P1[s] = __ldg(src + (long long)(7 + s) * a.acc_plane);
                 }
+                if constexpr (KARA == 3) {
+                    kara2_expand(src + 18 * a.acc_plane, a.acc_plane, M);
 #pragma unroll
-                for (int s = 0; s < 7; ++s)
-                    M[s] = (int64_t)__ldg(src + (long long)(P2 + s) * a.acc_plane) - P0[s] - P1[s];
+                    for (int s = 0; s < 7; ++s) M[s] -= P0[s] + P1[s];
+                } else {
+#pragma unroll
+                    for (int s = 0; s < 7; ++s)
+                        M[s] = (int64_t)__ldg(src + (long long)(P2 + s) * a.acc_plane) - P0[s] -
+                               P1[s];
+                }
                 int64_t(&y)[K] = x[bitrev(j)];
 #pragma unroll
                 for (int t = 0; t < 3; ++t) y[t] = P0[t] - P1[t] - M[t + 4];
@@ -802,6 +810,7 @@ static int launch_reg(const InvArgs& a, cudaStream_t stream) {
 
 template <int NB>
 static int launch_reg_kara(const InvArgs& a, cudaStream_t stream) {
+    if (a.kara == 3) return launch_reg<NB, 8, 3>(a, stream);
     return a.kara == 2 ? launch_reg<NB, 8, 2>(a, stream) : launch_reg<NB, 8, 1>(a, stream);
 }
 
@@ -811,7 +820,7 @@ int inverse_launch(const InvArgs& a, cudaStream_t stream) {
     if (a.school) return school_carry_launch(a, stream);
     if (a.kara) {
         if (a.K != 8 || a.nW != 1 || a.nchunk != 1 || a.positions > (a.NB + 1) * a.S ||
-            a.kara > 2)
+            a.kara > 3)
             return MFFTB_ERR_ARG;
         if (a.variant == 2) {
             const int rc = try_lane(a, stream);

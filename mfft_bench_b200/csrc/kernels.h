@@ -48,7 +48,9 @@ struct FwdArgs {
     int f_stack;       // 0: write Ahat [j][da][c]; 1: write F [j][db][r] (2K-1 planes);
                        // 2: Karatsuba operands [j][K + S]: Xhat[c], then Xhat[c] + Xhat[c+S];
                        // 3: two levels [j][K + 2S]: those, then Xhat[c] + Xhat[c+S/2] for
-                       //    c = 0..S/2-1 and S..S+S/2-1
+                       //    c = 0..S/2-1 and S..S+S/2-1;
+                       // 4: [j][K + 2S + S/2]: those, then s[c] + s[c+S/2] (c < S/2) of
+                       //    s[c] = Xhat[c] + Xhat[c+S]
     int8_t* out;
     long long oplane;  // bytes per output plane
     int* err;
@@ -94,8 +96,9 @@ struct InvArgs {
     // y^4 a1); the half points (j = 0, NB/2) hold P0 only.  kara = 2: 25
     // job planes per point, q = j*25 + ...: the length-2 convolutions Q0, Q1,
     // Q2 of P0 (3 coefficients each, 0..8) and of P1 (9..17), from which
-    // P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1, then P2 (18..24).  The register
-    // kernel reads both layouts, the lane kernel kara = 1 only.
+    // P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1, then P2 (18..24).  kara = 3: 27,
+    // the Q's of P2 at 18..26.  The register kernel reads every layout, the
+    // lane kernel kara = 1 only.
     int kara;
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);

@@ -141,7 +141,7 @@ bool plan_kara_ok(const Plan& p) {
 }
 
 void plan_set_kara(Plan& p, int level) {
-    if (level < 0 || level > 2 || (level && !plan_kara_ok(p))) level = 0;
+    if (level < 0 || level > 3 || (level && !plan_kara_ok(p))) level = 0;
     p.kara = level;
     const double S2 = (double)p.S * p.S;
     const double pts = p.NB <= 2 ? 0.0 : (double)p.NB - 2.0;  // ordinary points
@@ -153,6 +153,10 @@ void plan_set_kara(Plan& p, int level) {
         const double q = 3.0 * S2 / 4.0;
         p.njobs = p.NB * 25;
         p.macs_per_elem = ((2.0 * q + S2) * pts + q * half) * p.n_int;
+    } else if (level == 3) {  // P0, P1 and P2 as three length-S/2 convolutions each
+        const double q = 3.0 * S2 / 4.0;
+        p.njobs = p.NB * 27;
+        p.macs_per_elem = (3.0 * q * pts + q * half) * p.n_int;
     } else {
         p.njobs = p.NB * p.K * p.nW * p.nchunk;
         p.macs_per_elem = (double)p.NB * p.K * p.K * p.dA * p.dB * p.n_int;

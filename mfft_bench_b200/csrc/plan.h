@@ -59,7 +59,8 @@ struct Plan {
     // terms -- 48 plane products per point, 16 at the half points; njobs is
     // then the NB * 21 job planes, macs_per_elem the issued MACs.  kara = 2
     // splits P0 and P1 once more into three length-2 convolutions each (40
-    // plane products per point, 12 at the half points, NB * 25 job planes).
+    // plane products per point, 12 at the half points, NB * 25 job planes);
+    // kara = 3 splits P2 as well (36 per point, NB * 27 job planes).
     int kara;
 };
 
@@ -81,12 +82,18 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced
 // Whether the Karatsuba pointwise keeps the plan exact: one int8 digit per
 // transformed value with room for the sums a0 + a1 (2 |x| <= 127), K = 8,
 // one contraction chunk, and every int32 accumulator of P2 = (a0+a1)(b0+b1)
-// (4 terms of length n) below 2^31.  The second level needs nothing more:
-// its sums u0 + u1 are sums of two single digits like a0 + a1, and its
+// (4 terms of length n) below 2^31.  The further levels need nothing more.
+// A block of the transform holds S coefficients in a ring of K = 2S, so a
+// signed permutation y^e puts each block's digit in exactly one of the
+// positions c and c+S: (a0 + a1)[c] = x[c] + x[c+S] has one digit term per
+// block, as x[c] has, and |a0 + a1| <= boundA.  Every sum the second level
+// forms -- x[c] + x[c+2] (P0, P1) or (a0+a1)[c] + (a0+a1)[c+2] (P2) -- then
+// has at most two per block, |sum| <= 2 boundA <= 127, and its
 // accumulators have at most 2 terms.
 bool plan_kara_ok(const Plan& p);
-// Set a plan's Karatsuba level (0 = negacyclic, 1, 2; job planes and issued
-// MACs); a level the plan cannot take falls back to 0.
+// Set a plan's Karatsuba level (0 = negacyclic; 1; 2, P0 and P1 split once
+// more; 3, P2 as well; job planes and issued MACs); a level the plan cannot
+// take falls back to 0.
 void plan_set_kara(Plan& p, int level);
 // Whether job (t, ch) of a schoolbook plan has any term.
 inline bool school_job_live(const Plan& p, int t, int ch) {

@@ -967,15 +967,16 @@ __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long til
         if (sj < ng) break;
         sj -= ng;
     }
-    if (p.jobs.kara == 2) {
-        if (sj < 6) {
+    if (p.jobs.kara >= 2) {
+        const int ops = pw_kara_ops(p.jobs), nq = pw_kara_jobs(p.jobs);
+        if (sj < 6 || p.jobs.kara == 3) {
             kind = 2;
-            abase = j * PWK2_OPS + pw_kara2_qplane(sj);
-            qbase = j * PWK2_JOBS + 3 * sj;
+            abase = j * ops + pw_kara2_qplane(sj);
+            qbase = j * nq + 3 * sj;
         } else {
             kind = sj - 6;
-            abase = j * PWK2_OPS + 8 + kind;
-            qbase = j * PWK2_JOBS + 18 + 4 * kind;
+            abase = j * ops + 8 + kind;
+            qbase = j * nq + 18 + 4 * kind;
         }
     } else {
         kind = sj & 1;
@@ -1454,14 +1455,15 @@ __global__ void pointwise_simt_check_kernel(const int8_t* A, long long lda, long
         // A(base + u) * B(base + v), base = j*12 + 4p.  kara = 2: q = j*25 +
         // 3g + s (g < 6) sums u + v = s (u, v < 2) from the first plane of
         // length-2 convolution g; q = j*25 + 18 + s is P2 (base j*16 + 8).
+        // kara = 3: q = j*27 + 3g + s for all nine g.
         const int nq = pw_kara_jobs(J), ops = pw_kara_ops(J);
         const int j = q / nq, off = q % nq;
         int base, s, w;
-        if (J.kara == 2 && off < 18) {
+        if ((J.kara == 2 && off < 18) || J.kara == 3) {
             base = j * ops + pw_kara2_qplane(off / 3);
             s = off % 3;
             w = 2;
-            if (off >= 9 && pw_kara_half(J, j)) return;  // P1: not at a half point
+            if (off >= 9 && pw_kara_half(J, j)) return;  // P1, P2: not at a half point
         } else {
             const int pr = J.kara == 2 ? 2 : off / 7;
             base = j * ops + 4 * pr;

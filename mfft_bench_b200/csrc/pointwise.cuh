@@ -78,6 +78,16 @@ struct PwJobs {
     // a1[1]+a1[3]; the job planes are 25 per point: Q0, Q1, Q2 of P0
     // (3 coefficients each, planes j*25 + 0..8), of P1 (9..17), then P2's 7
     // (18..24).
+    //
+    // kara = 3 splits P2 the same way.  Its operands (a0+a1)[c] are no larger
+    // than a single transformed value: every block of the transform holds S
+    // coefficients in a ring of K = 2S, so of the two positions c and c+S a
+    // signed permutation y^e fills exactly one from each block, and
+    // (a0+a1)[c] = x[c] + x[c+S] has one digit term per block, like x[c];
+    // (a0+a1)[c] + (a0+a1)[c+2] then has two per block, like x[c] + x[c+2].
+    // 18 operand planes per point: the 16 above, then (a0+a1)[0]+(a0+a1)[2],
+    // (a0+a1)[1]+(a0+a1)[3]; 27 job planes: the Q0, Q1, Q2 of P0 (0..8), of
+    // P1 (9..17) and of P2 (18..26).
     int kara;
 };
 
@@ -85,17 +95,31 @@ constexpr int PWK_OPS = 12;    // operand planes per point, kara = 1
 constexpr int PWK_JOBS = 21;   // job planes per point, kara = 1
 constexpr int PWK2_OPS = 16;   // operand planes per point, kara = 2
 constexpr int PWK2_JOBS = 25;  // job planes per point, kara = 2
+constexpr int PWK3_OPS = 18;   // operand planes per point, kara = 3
+constexpr int PWK3_JOBS = 27;  // job planes per point, kara = 3
 
-__host__ __device__ inline int pw_kara_ops(const PwJobs& J) {
-    return J.kara == 2 ? PWK2_OPS : PWK_OPS;
+__host__ __device__ inline int pw_kara_level_ops(int level) {
+    return level == 3 ? PWK3_OPS : (level == 2 ? PWK2_OPS : PWK_OPS);
 }
+__host__ __device__ inline int pw_kara_ops(const PwJobs& J) { return pw_kara_level_ops(J.kara); }
 __host__ __device__ inline int pw_kara_jobs(const PwJobs& J) {
-    return J.kara == 2 ? PWK2_JOBS : PWK_JOBS;
+    return J.kara == 3 ? PWK3_JOBS : (J.kara == 2 ? PWK2_JOBS : PWK_JOBS);
 }
-// kara = 2: the first operand plane of length-2 convolution g (g = 0..5:
-// Q0, Q1, Q2 of P0, then of P1) within a point's 16
+// kara >= 2: the first operand plane of length-2 convolution g within a
+// point's operand planes (g = 0..2: Q0, Q1, Q2 of P0; 3..5: of P1; 6..8, at
+// kara = 3: of P2)
 __host__ __device__ inline int pw_kara2_qplane(int g) {
-    return g == 2 ? 12 : (g == 5 ? 14 : (g < 2 ? 2 * g : 2 * g - 2));
+    switch (g) {
+        case 0: return 0;
+        case 1: return 2;
+        case 2: return 12;
+        case 3: return 4;
+        case 4: return 6;
+        case 5: return 14;
+        case 6: return 8;
+        case 7: return 10;
+        default: return 16;
+    }
 }
 
 // Karatsuba mode: the half points (j = 0, NB/2) need P0 only
@@ -104,9 +128,11 @@ __host__ __device__ inline bool pw_kara_half(const PwJobs& J, int j) {
 }
 // tile groups per point: kara = 1, (product p, output half hi), 6 per
 // ordinary point, 2 per half point; kara = 2, the six length-2 convolutions
-// and P2's two halves, 8 per ordinary point, 3 per half point
+// and P2's two halves, 8 per ordinary point, 3 per half point; kara = 3,
+// nine length-2 convolutions per ordinary point, 3 per half point
 __host__ __device__ inline int pw_kara_point_groups(const PwJobs& J, bool half) {
-    return J.kara == 2 ? (half ? 3 : 8) : (half ? 2 : 6);
+    if (half) return J.kara >= 2 ? 3 : 2;
+    return J.kara == 3 ? 9 : (J.kara == 2 ? 8 : 6);
 }
 __host__ __device__ inline int pw_kara_groups(const PwJobs& J) {
     const int nhalf = J.NB <= 2 ? J.NB : 2;

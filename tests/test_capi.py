@@ -122,17 +122,18 @@ def test_plan_exactness_invariants(n, mode, w):
     if pi["kara"]:
         # Karatsuba pointwise: three full length-S convolutions per ordinary
         # point, one per half point; the sums a0 + a1 fit int8 and P2's
-        # accumulators (S terms of length n) fit int32.  The default level 2
-        # takes P0 (and P1) as three length-S/2 convolutions: their sums are
-        # of two single digits again, with at most S/2 terms per accumulator.
+        # accumulators (S terms of length n) fit int32.  The default level 3
+        # takes P0, P1 and P2 as three length-S/2 convolutions each: their
+        # sums have two digit terms per block, with at most S/2 terms per
+        # accumulator.
         NB, S = pi["NB"], pi["S"]
         assert pi["K"] == 8 and pi["dA"] == pi["dB"] == 1 and pi["nchunk"] == 1 and NB <= 8
         assert 2 * MA <= 127 and 2 * pi["ncB"] * dmax <= 127
         assert S * pi["n_int"] * (2 * MA) * (2 * pi["ncB"] * dmax) < 2 ** 31
-        assert pi["kara"] == 2 and pi["njobs"] == NB * 25
+        assert pi["kara"] == 3 and pi["njobs"] == NB * 27
         q = 3 * (S // 2) ** 2
         nh = min(NB, 2)
-        assert pi["int8_macs"] == ((2 * q + S * S) * (NB - nh) + q * nh) * float(pi["n_int"]) ** 3
+        assert pi["int8_macs"] == (3 * q * (NB - nh) + q * nh) * float(pi["n_int"]) ** 3
     else:
         assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
         assert pi["int8_macs"] == (pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"]

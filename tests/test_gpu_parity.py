@@ -96,7 +96,7 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
         ph = ctx.last_plan()
     finally:
         ctx.set_half_points(1)
-        ctx.set_karatsuba(2)
+        ctx.set_karatsuba(3)
     assert ph["pw_kernel"] == 3 and ph["half_points"] == 1 and pd["half_points"] == 0
     NB, K, S = ph["NB"], ph["K"], ph["S"]
     assert ph["int8_macs"] == pytest.approx(pd["int8_macs"] * ((NB - 2) * K * K + 2 * S * S)
@@ -406,13 +406,14 @@ def test_host_entry_points_chunked_readback(ctx):
     (256, 144, 640, 8),    # 5 k-blocks: level 2's last stage holds one
     (300, 128, 100, 4),    # a single, partial k-block
 ])
-@pytest.mark.parametrize("level", [1, 2])
+@pytest.mark.parametrize("level", [1, 2, 3])
 def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
     """The Karatsuba plane-product kernel on random int8 operand planes
     against a CUDA-core evaluation of its job table.  Level 1 (NB * 12 planes
     per side): P0, P1, P2 of every ordinary point, P0 of the half points.
     Level 2 (NB * 16): the length-2 convolutions Q0, Q1, Q2 of P0 and P1 (two
-    k-blocks per pipeline stage, an odd k-block count included) and P2."""
+    k-blocks per pipeline stage, an odd k-block count included) and P2.
+    Level 3 (NB * 18): those of P2 as well."""
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256,
                                   variant=3 + level) == 0
 
@@ -420,9 +421,9 @@ def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
 @pytest.mark.parametrize("n,kind", [(256, "i64"), (300, "i64"), (1000, "i64"), (2112, "i64"),
                                     (512, "u16s"), (384, "u16")])
 def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
-    """Whole W=64 products with the two-level Karatsuba pointwise (the
-    default for this plan), with one level (also through the lane inverse)
-    and without it are the same bits, and match the oracle."""
+    """Whole W=64 products with the Karatsuba pointwise at level 3 (the
+    default for this plan), 2, 1 (also through the lane inverse) and without
+    it are the same bits, and match the oracle."""
     if kind == "i64":
         A, B = oracle.int64_entries(n, 5 + n), oracle.int64_entries(n, 7 + n)
         run = lambda: ctx.mm_i64(A, B, n, RL=9)  # noqa: E731
@@ -434,10 +435,14 @@ def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
         run = lambda: ctx.mm_u16(Ap, Bp, n, 4, signed=signed)  # noqa: E731
     got = run()
     pk = ctx.last_plan()
-    assert pk["kara"] == 2 and pk["pw_kernel"] == 4
-    assert pk["int8_macs"] == 264 * float(pk["n_int"]) ** 3
-    ctx.set_karatsuba(1)
+    assert pk["kara"] == 3 and pk["pw_kernel"] == 4
+    assert pk["int8_macs"] == 240 * float(pk["n_int"]) ** 3
+    ctx.set_karatsuba(2)
     try:
+        two = run()
+        assert ctx.last_plan()["kara"] == 2
+        assert ctx.last_plan()["int8_macs"] == 264 * float(pk["n_int"]) ** 3
+        ctx.set_karatsuba(1)
         one = run()
         assert ctx.last_plan()["kara"] == 1
         assert ctx.last_plan()["int8_macs"] == 320 * float(pk["n_int"]) ** 3
@@ -449,7 +454,8 @@ def test_karatsuba_products_are_exact(ctx, oracle, n, kind):
         assert ctx.last_plan()["kara"] == 0
     finally:
         ctx.set_kernel_variant("inverse", 0)
-        ctx.set_karatsuba(2)
+        ctx.set_karatsuba(3)
+    assert np.array_equal(two, got)
     assert np.array_equal(one, got)
     assert np.array_equal(lane, got)
     assert np.array_equal(got, ref)

@@ -107,6 +107,78 @@ def test_two_level_karatsuba_identity(half):
         assert _recombine(P[0], P[1], _conv4(sa, sb)) == _negacyclic(a, b)
 
 
+def test_three_way_split_identity():
+    """Level 3: P2 as three length-2 convolutions too (its operands a0 + a1
+    are single-term sums per block, so (a0+a1)[c] + (a0+a1)[c+2] fits int8
+    like x[c] + x[c+2])."""
+    rng = random.Random(13)
+    for _ in range(2000):
+        a = [rng.randint(-60, 60) for _ in range(8)]
+        b = [rng.randint(-60, 60) for _ in range(8)]
+        sa = [a[i] + a[i + 4] for i in range(4)]
+        sb = [b[i] + b[i + 4] for i in range(4)]
+        P = []
+        for u, v in ((a[:4], b[:4]), (a[4:], b[4:]), (sa, sb)):
+            su, sv = [u[0] + u[2], u[1] + u[3]], [v[0] + v[2], v[1] + v[3]]
+            P.append(_expand2(_conv2(u[:2], v[:2]), _conv2(u[2:], v[2:]), _conv2(su, sv)))
+            assert P[-1] == _conv4(u, v)
+        assert _recombine(*P) == _negacyclic(a, b)
+
+
+def _point_terms(K, S, NB, nc, j):
+    """Digit terms of the transformed coefficients x[0..K-1] at point j:
+    block beta (beta < nc) holds digits at ring positions 0..S-1 and is
+    multiplied by y^(g j beta), a signed permutation of Z[y]/(y^K + 1)."""
+    g = 2 * K // NB
+    xs = []
+    for k in range(K):
+        t = {}
+        for beta in range(nc):
+            r, sgn = (k - g * j * beta) % (2 * K), 1
+            if r >= K:
+                r, sgn = r - K, -1
+            if r < S:
+                t[(beta, r)] = t.get((beta, r), 0) + sgn
+        xs.append(t)
+    return xs
+
+
+def _nterms(*ts):
+    out = {}
+    for t in ts:
+        for key, v in t.items():
+            out[key] = out.get(key, 0) + v
+    return sum(abs(v) for v in out.values())
+
+
+@pytest.mark.parametrize("NB", [2, 4, 8])
+def test_karatsuba_operand_bounds(NB):
+    """The bounds every Karatsuba level relies on, counted from the transform
+    itself at every evaluation point: x[c] and (a0+a1)[c] = x[c] + x[c+4]
+    take one digit per block (|.| <= nc * dmax = boundA); the second-level
+    sums x[c] + x[c+2] and (a0+a1)[c] + (a0+a1)[c+2] take two (<= 2 boundA,
+    the int8 check of the planner); a third level on Q2 would need four."""
+    K, S = 8, 4
+    nc = NB // 2 if NB > 2 else 1
+    for j in range(NB):
+        x = _point_terms(K, S, NB, nc, j)
+        s = [_merge(x[c], x[c + 4]) for c in range(4)]
+        assert max(_nterms(v) for v in x) <= nc
+        assert max(_nterms(v) for v in s) <= nc
+        assert max(_nterms(x[c], x[c + 2]) for c in (0, 1, 4, 5)) <= 2 * nc
+        assert max(_nterms(s[c], s[c + 2]) for c in (0, 1)) <= 2 * nc
+    if NB == 8:  # the reason a Q2 stays a length-2 convolution
+        x = _point_terms(K, S, NB, nc, 0)
+        assert _nterms(x[0], x[1], x[2], x[3]) == 4 * nc
+
+
+def _merge(a, b):
+    out = dict(a)
+    for key, v in b.items():
+        out[key] = out.get(key, 0) + v
+    return out
+
+
 def test_karatsuba_extremes():
     """All-extreme operands: every job value and the recombined coefficients
     stay within the int32 accumulator and int64 inverse bounds the planner
@@ -126,10 +198,10 @@ def test_karatsuba_extremes():
 def test_planner_uses_karatsuba_on_the_w64_plan():
     pi = m.plan_info(16384, 0, 64)
     assert (pi["b"], pi["S"], pi["NB"], pi["K"], pi["dA"]) == (4, 4, 8, 8, 1)
-    assert pi["kara"] == 2 and pi["njobs"] == 8 * 25
-    # 6 ordinary points x (2 x 12 + 16) + 2 half points x 12 = 264 plane
-    # products (one level: 6 x 48 + 2 x 16 = 320; none: 8 x 64 = 512)
-    assert pi["int8_macs"] == 264 * 16384.0 ** 3
+    assert pi["kara"] == 3 and pi["njobs"] == 8 * 27
+    # 6 ordinary points x 3 x 12 + 2 half points x 12 = 240 plane products
+    # (P2 one level deep: 264; one level: 6 x 48 + 2 x 16 = 320; none: 512)
+    assert pi["int8_macs"] == 240 * 16384.0 ** 3
     # past n ~ 37000 the P2 accumulators (4 * n * 120^2) would pass 2^31
     assert m.plan_info(40000, 0, 64)["kara"] == 0
     # plans whose transformed sums do not leave room for a0 + a1 keep the
