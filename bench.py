@@ -79,6 +79,12 @@ def env_int(k, d):
 # the full workload (one pass checked on n = 4096 first), keyed by workload,
 # kernel (3 t-grouped, 4 Karatsuba) and Karatsuba level.
 POINTWISE_TRAFFIC = {
+    ("c5", 4, 3): {"bytes_per_launch": 152.18e9 + 39.55e9,
+                   "note": ("ncu, the second launch of a 1-GPU product (a row block of 3328 rows "
+                            "x 16384 columns), level-3 Karatsuba kernel (two 96 KB stages): "
+                            "152.2 GB read + 39.6 GB written in 148.0 ms; algorithmic: 144 A "
+                            "operand planes of the block + 144 B operand planes (46.5 GB) read, "
+                            "180 int32 job planes per element of the block (39.3 GB) written")},
     ("c5", 4, 2): {"bytes_per_launch": 197.62e9 + 45.51e9,
                    "note": ("ncu, the second launch of a 1-GPU product (a row block of 4096 rows "
                             "x 16384 columns), two-level Karatsuba kernel: 197.6 GB read + "

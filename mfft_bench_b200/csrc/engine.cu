@@ -70,6 +70,7 @@ struct mfftgpu_ctx {
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     int kara = kDefaultKara;      // Karatsuba level where the plan allows it
+    int kara_stages = 0;          // level-3 pipeline: 4 four 48 KB stages; 0 / 2 two of 96 KB
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
     int reuse_b = 0;
@@ -375,6 +376,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
                         P.NB, (!school && !P.kara && C->half_points && P.K == 2 * P.S) ? P.S : 0,
                         P.kara};
         L.map_rows = (int)std::max<long long>(rb, 256);
+        L.kara_stages = C->kara_stages;
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
         L.out = acc;
         L.out_plane = R * n_int;
@@ -553,6 +555,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_GROUP_M")) C->group_m = atoi(s);
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
+    if (const char* s = getenv("MFFTGPU_KARA_STAGES")) C->kara_stages = atoi(s);
     if (const char* s = getenv("MFFTGPU_HALF_POINTS")) C->half_points = atoi(s) != 0;
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
@@ -1187,6 +1190,7 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     L.kdim = kdim;
     L.jobs = J;
     L.map_rows = arows;
+    L.kara_stages = C->kara_stages;
     L.block_n = block_n;
     L.out = out;
     L.out_plane = (long long)rows * cols;

@@ -927,21 +927,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
 // multiply of a stage holds a term: a stage loads the 4 (lo) or 3 (hi) A
 // planes and as many B planes of the product and issues all of its terms,
 // one 256 x 128 accumulator per output coefficient.
-constexpr int PWK_NS = 4;             // operand plane slots per side and stage
 constexpr int PWK_BN = 128;           // output columns per pair tile (MMA N)
 // warp 0 TMA producer, warp 1 MMA issuer, warps 2-9 epilogue: two warps per
 // 32-lane TMEM quarter, each draining 64 of an accumulator's 128 columns, so
 // the tensor pipe waits half as long between tiles
 constexpr int PWK_EPI_WARPS = 8;
 constexpr int PWK_THREADS = 32 * (2 + PWK_EPI_WARPS);
-// A stage: 4 A plane tiles (128 rows) and 4 B half-tiles (64 columns) of
-// 128 contraction bytes per CTA, 96 KB, two of them.  (Four 48 KB stages of
-// 64 contraction bytes with 64-byte swizzling were measured slower.)
-constexpr int PWK_STAGES = 2;
+// 192 KB of stages per CTA: two of 4 A plane tiles (128 rows) and 4 B
+// half-tiles (64 columns) of 128 contraction bytes, or, for tiles of
+// length-2 convolutions only, four of 2 + 2.  (Four 48 KB stages of 64
+// contraction bytes with 64-byte swizzling were measured slower for the
+// mixed tile kinds.)
 constexpr int PWK_A_BYTES = 128 * PW_BK;
 constexpr int PWK_B_BYTES = (PWK_BN / 2) * PW_BK;
-constexpr int PWK_STAGE_BYTES = PWK_NS * (PWK_A_BYTES + PWK_B_BYTES);
-constexpr int PWK_SMEM_BYTES = 1024 + PWK_STAGES * PWK_STAGE_BYTES + 256;
+constexpr int PWK_SMEM_BYTES = 1024 + 8 * (PWK_A_BYTES + PWK_B_BYTES) + 256;
 
 // A tile group of the Karatsuba kernel: kind 0 ("lo", 4 + 4 planes, output
 // coefficients 0..3 of a length-4 convolution), 1 ("hi", 3 + 3 planes,
@@ -985,19 +984,27 @@ __device__ __forceinline__ void pwk_tile_decode(const PwParams& p, long long til
     }
 }
 
+// NSTAGE = 2: stages of 4 + 4 plane slots (96 KB), every tile kind (the
+// default); NSTAGE = 4: stages of 2 + 2 slots (48 KB, one k-block), length-2
+// convolution tiles only (kara = 3): three stages in flight while one is
+// multiplied, but half the MMAs per barrier round trip.
+template <int NSTAGE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
     pointwise_kara_i8_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB, const PwParams p) {
+    constexpr int NS = 8 / NSTAGE;                                // slots per side and stage
+    constexpr int STAGE_BYTES = NS * (PWK_A_BYTES + PWK_B_BYTES);
+    constexpr int QK = NS / 2;  // k-blocks per stage of a length-2 convolution tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PWK_STAGES * PWK_STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + NSTAGE * STAGE_BYTES);
     const uint32_t bar_full = smem_u32(bars);
-    const uint32_t bar_empty = smem_u32(bars + PWK_STAGES);
-    const uint32_t bar_tfull = smem_u32(bars + 2 * PWK_STAGES);
-    const uint32_t bar_tempty = smem_u32(bars + 2 * PWK_STAGES + 1);
-    const uint32_t bar_drain = smem_u32(bars + 2 * PWK_STAGES + 2);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * PWK_STAGES + 3);
+    const uint32_t bar_empty = smem_u32(bars + NSTAGE);
+    const uint32_t bar_tfull = smem_u32(bars + 2 * NSTAGE);
+    const uint32_t bar_tempty = smem_u32(bars + 2 * NSTAGE + 1);
+    const uint32_t bar_drain = smem_u32(bars + 2 * NSTAGE + 2);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * NSTAGE + 3);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -1008,7 +1015,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
     const long long npairs = gridDim.x >> 1;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < PWK_STAGES; ++s) {
+        for (int s = 0; s < NSTAGE; ++s) {
             mbar_init(bar_full + 8 * s, 1);
             mbar_init(bar_empty + 8 * s, 1);
         }
@@ -1034,8 +1041,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
         // ------------------------------------------------------ TMA producer (both CTAs)
         int stage = 0;
         uint32_t phase = 0;
-        int issued_parity[PWK_STAGES];
-        for (int s = 0; s < PWK_STAGES; ++s) issued_parity[s] = -1;
+        int issued_parity[NSTAGE];
+        for (int s = 0; s < NSTAGE; ++s) issued_parity[s] = -1;
         const long long first_tile = p.stall_producer ? p.num_tiles : pair;
         bool align = p.wave_counter != nullptr;
         long long wave = 0;
@@ -1058,7 +1065,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
             // hi u, v in [1, 3]; a length-2 convolution, u, v in [0, 1] for
             // two consecutive k-blocks
             const int nsl = kind == 2 ? 2 : (kind ? 3 : 4);
-            const int ksub = kind == 2 ? 2 : 1;
+            const int ksub = kind == 2 ? QK : 1;
             for (int kb = 0; kb < p.kblocks; kb += ksub) {
                 const int nk = kb + ksub <= p.kblocks ? ksub : 1;
                 const uint32_t stage_tx =
@@ -1068,25 +1075,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                     goto producer_done;
                 const uint32_t full_leader = mapa_shared(bar_full + 8 * stage, 0);
                 if (leader) mbar_arrive_expect_tx(bar_full + 8 * stage, stage_tx);
-                uint8_t* st = smem + stage * PWK_STAGE_BYTES;
+                uint8_t* st = smem + stage * STAGE_BYTES;
                 for (int h = 0; h < nk; ++h)
                     for (int i = 0; i < nsl; ++i) {
                         const int slot = h * nsl + i;
                         tma_load_3d_pair(smem_u32(st + slot * PWK_A_BYTES), &tmA, full_leader,
                                          (kb + h) * PW_BK, mt * 256 + (int)rank * 128, abase + i);
-                        tma_load_3d_pair(smem_u32(st + PWK_NS * PWK_A_BYTES + slot * PWK_B_BYTES),
+                        tma_load_3d_pair(smem_u32(st + NS * PWK_A_BYTES + slot * PWK_B_BYTES),
                                          &tmB, full_leader, (kb + h) * PW_BK,
                                          nt * PWK_BN + (int)rank * (PWK_BN / 2), abase + i);
                     }
                 issued_parity[stage] = (int)phase;
-                if (++stage == PWK_STAGES) {
+                if (++stage == NSTAGE) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
         }
     producer_done:
-        for (int s = 0; s < PWK_STAGES; ++s)
+        for (int s = 0; s < NSTAGE; ++s)
             if (issued_parity[s] >= 0)
                 if (!mbar_wait_deadline(bar_empty + 8 * s, (uint32_t)issued_parity[s],
                                         global_timer_ns() + tmo))
@@ -1101,7 +1108,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
             int kind, abase, qbase, mt, nt;
             pwk_tile_decode(p, tile, kind, abase, qbase, mt, nt);
             const int hi = kind & 1;
-            const int ksub = kind == 2 ? 2 : 1;
+            const int ksub = kind == 2 ? QK : 1;
             if (!mbar_wait_bounded(bar_tempty, acc_phase ^ 1, abort_flag, global_timer_ns() + tmo))
                 break;
             tc_fence_after();
@@ -1110,13 +1117,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                                        global_timer_ns() + tmo))
                     goto mma_done;
                 tc_fence_after();
-                const uint32_t st = smem_u32(smem + stage * PWK_STAGE_BYTES);
+                const uint32_t st = smem_u32(smem + stage * STAGE_BYTES);
                 if (kind == 2) {
                     // slots 2h + u (A) / 2h + v (B) hold k-block kb + h; the
                     // term (u, v) belongs to accumulator u + v, started by
                     // its first term in loop order -- (0,0), (0,1), (1,1) --
                     // in k-block 0
-                    const int nk = kb + 2 <= p.kblocks ? 2 : 1;
+                    const int nk = kb + QK <= p.kblocks ? QK : 1;
                     for (int h = 0; h < nk; ++h) {
                         const uint32_t acc0 = kb + h != 0 ? 1u : 0u;
 #pragma unroll
@@ -1127,7 +1134,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                                 const bool init = ia == 0 || accn == 2;
                                 const uint32_t a0 = st + (2 * h + ia) * PWK_A_BYTES;
                                 const uint32_t b0 =
-                                    st + PWK_NS * PWK_A_BYTES + (2 * h + ib) * PWK_B_BYTES;
+                                    st + NS * PWK_A_BYTES + (2 * h + ib) * PWK_B_BYTES;
 #pragma unroll
                                 for (int kk = 0; kk < PW_BK / 32; ++kk)
                                     mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
@@ -1140,37 +1147,42 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PWK_THREADS, 1)
                         }
                     }
                     mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
-                    if (++stage == PWK_STAGES) {
+                    if (++stage == NSTAGE) {
                         stage = 0;
                         phase ^= 1;
                     }
                     continue;
                 }
-                const uint32_t acc0 = kb != 0 ? 1u : 0u;  // the first k-block starts every sum
-                // slot i holds plane u = hi + i (A) / v = hi + i (B); the term
-                // (u, v) belongs to output s = u + v, accumulator s - 4 hi
+                if constexpr (NS == 4) {
+                    const uint32_t acc0 = kb != 0 ? 1u : 0u;  // the first k-block starts every sum
+                    // slot i holds plane u = hi + i (A) / v = hi + i (B); the
+                    // term (u, v) belongs to output s = u + v, accumulator
+                    // s - 4 hi
 #pragma unroll
-                for (int ia = 0; ia < PWK_NS; ++ia) {
+                    for (int ia = 0; ia < NS; ++ia) {
 #pragma unroll
-                    for (int ib = 0; ib < PWK_NS; ++ib) {
-                        const int s = ia + ib + 2 * hi;  // u + v
-                        if (hi ? (ia == 3 || ib == 3 || s < 4) : s > 3) continue;
-                        const int accn = hi ? s - 4 : s;
-                        // the first term of each accumulator in loop order --
-                        // ia = 0 (lo), ia = accn (hi) -- starts it in k-block 0
-                        const bool init = ia == (hi ? accn : 0);
-                        const uint32_t a0 = st + ia * PWK_A_BYTES;
-                        const uint32_t b0 = st + PWK_NS * PWK_A_BYTES + ib * PWK_B_BYTES;
+                        for (int ib = 0; ib < NS; ++ib) {
+                            const int s = ia + ib + 2 * hi;  // u + v
+                            if (hi ? (ia == 3 || ib == 3 || s < 4) : s > 3) continue;
+                            const int accn = hi ? s - 4 : s;
+                            // the first term of each accumulator in loop order
+                            // -- ia = 0 (lo), ia = accn (hi) -- starts it in
+                            // k-block 0
+                            const bool init = ia == (hi ? accn : 0);
+                            const uint32_t a0 = st + ia * PWK_A_BYTES;
+                            const uint32_t b0 = st + NS * PWK_A_BYTES + ib * PWK_B_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < PW_BK / 32; ++kk)
-                            mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
-                                        sdesc_kmajor_sw128(a0 + kk * 32),
-                                        sdesc_kmajor_sw128(b0 + kk * 32), idesc,
-                                        (acc0 | (uint32_t)kk | (init ? 0u : 1u)) != 0 ? 1u : 0u);
+                            for (int kk = 0; kk < PW_BK / 32; ++kk)
+                                mma_i8_pair(tmem_base + (uint32_t)(accn * PWK_BN),
+                                            sdesc_kmajor_sw128(a0 + kk * 32),
+                                            sdesc_kmajor_sw128(b0 + kk * 32), idesc,
+                                            (acc0 | (uint32_t)kk | (init ? 0u : 1u)) != 0 ? 1u
+                                                                                          : 0u);
+                        }
                     }
                 }
                 mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
-                if (++stage == PWK_STAGES) {
+                if (++stage == NSTAGE) {
                     stage = 0;
                     phase ^= 1;
                 }
@@ -1303,21 +1315,29 @@ static int launch_kara(const PwLaunch& L, cudaStream_t stream) {
     if (rc) return rc;
     rc = make_map(&tmB, L.F, L.kdim, L.cols, L.f_planes, L.ldf, L.f_plane_bytes, PWK_BN / 2);
     if (rc) return rc;
-    static int attr_dev = -1;
+    // four 48 KB stages only on request (kara_stages = 4, level 3): at c5
+    // they ran 10 % slower per clock than two 96 KB stages (half the MMAs
+    // per barrier round trip)
+    const bool four = L.jobs.kara == 3 && L.kara_stages == 4;
+    static int attr_dev[2] = {-1, -1};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (attr_dev != dev) {
-        if (cudaFuncSetAttribute(pointwise_kara_i8_kernel,
+    if (attr_dev[four] != dev) {
+        if (cudaFuncSetAttribute(four ? pointwise_kara_i8_kernel<4> : pointwise_kara_i8_kernel<2>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  PWK_SMEM_BYTES) != cudaSuccess)
             return MFFTB_ERR_CUDA;
-        attr_dev = dev;
+        attr_dev[four] = dev;
     }
     long long pairs = L.num_sms / 2;
     if (pairs > p.num_tiles) pairs = p.num_tiles;
     if (pairs <= 0) return MFFTB_OK;
-    pointwise_kara_i8_kernel<<<(unsigned)(2 * pairs), PWK_THREADS, PWK_SMEM_BYTES, stream>>>(tmA, tmB,
-                                                                                          p);
+    if (four)
+        pointwise_kara_i8_kernel<4>
+            <<<(unsigned)(2 * pairs), PWK_THREADS, PWK_SMEM_BYTES, stream>>>(tmA, tmB, p);
+    else
+        pointwise_kara_i8_kernel<2>
+            <<<(unsigned)(2 * pairs), PWK_THREADS, PWK_SMEM_BYTES, stream>>>(tmA, tmB, p);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 

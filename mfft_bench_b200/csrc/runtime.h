@@ -47,6 +47,7 @@ struct PwLaunch {
                               // 4 Karatsuba)
     int map_rows;             // Karatsuba mode: rows the A tensor map spans (>= rows, >= 256;
                               // the rows past `rows` lie inside the plane stride)
+    int kara_stages;          // Karatsuba level 3: 4 four 48 KB stages; 0 / 2 two of 96 KB
 };
 
 int pointwise_launch(const PwLaunch& L, cudaStream_t stream);
