@@ -109,8 +109,8 @@ PW_KERNELS = {1: "pointwise_i8_kernel (tcgen05 kind::i8, one CTA per tile)",
               2: "pointwise2_i8_kernel (tcgen05 cta_group::2 kind::i8)",
               3: "pointwise3_i8_kernel (tcgen05 cta_group::2 kind::i8, 4 t-jobs per tile)",
               4: "pointwise_kara_i8_kernel (tcgen05 cta_group::2 kind::i8, Karatsuba: 3 "
-                 "length-4 convolutions per point, at level 2 the first two as 3 length-2 "
-                 "convolutions each)"}
+                 "length-4 convolutions per point, at levels 2 and 3 each of the first two, "
+                 "or all three, as 3 length-2 convolutions)"}
 
 
 def load_peaks():
@@ -823,7 +823,7 @@ def main():
             line["int8_tops_issued"] = 2 * macs / (ms * 1e-3) / 1e12
             line["useful_tops"] = 2 * pi["schoolbook7_macs"] / (ms * 1e-3) / 1e12
             line["plan"] = {k: pi[k] for k in ("b", "S", "NB", "K", "dA", "dB", "nchunk", "njobs",
-                                               "half_points", "kara", "rblock")}
+                                               "half_points", "kara", "dsum", "rblock")}
         line["phase_ms_per_step"] = {k: v / args.steps for k, v in ph.items() if k != "total"}
         share = ph["pointwise"] / max(1e-9, sum(v for k, v in ph.items() if k != "total"))
         line["pointwise_share"] = share

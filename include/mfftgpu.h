@@ -68,6 +68,9 @@ typedef struct {
                                 (NB * 27); 0 off */
     int rblock;              /* rows per row block of the last product (each block is one
                                 launch of every A-side kernel); 0 from mfftgpu_plan_info_get */
+    int dsum;                /* 1: digit sums -- the two int8 digits lo, hi of a transformed
+                                value plus lo + hi, three digit-pair classes (lo*lo, hi*hi,
+                                sum*sum) instead of four digit pairs; dA = dB = 3, nW = 3 */
 } mfftgpu_plan_info;
 
 /* --- context --------------------------------------------------------------
@@ -131,6 +134,13 @@ int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
  * like a single value): 36 per point.  Results are identical at every
  * level; other values return MFFTGPU_ERR_ARG. */
 int mfftgpu_set_karatsuba(mfftgpu_ctx *ctx, int level);
+/* Digit sums, on = 1 (the default, or $MFFTGPU_DSUM): plans that split each
+ * transformed value into two int8 digits x = lo + 2^7 hi (c1, c3) also form
+ * lo + hi, which stays in int8 when |hi| <= 64, and take the middle digit
+ * class lo_A hi_B + hi_A lo_B as (lo_A + hi_A)(lo_B + hi_B) - lo_A lo_B -
+ * hi_A hi_B: three int8 plane products per term instead of four.  Results
+ * are identical either way. */
+int mfftgpu_set_digit_sums(mfftgpu_ctx *ctx, int on);
 /* At the evaluation points 0 and NB/2 the transformed blocks keep only their
  * low K/2 coefficients, so three quarters of those points' plane products
  * are zero; on = 1 (the default, or $MFFTGPU_HALF_POINTS) lets the t-grouped
@@ -245,7 +255,9 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * tiles, tcgen05 cta_group::2), 3 t-grouped CTA pairs, 4 the Karatsuba job
  * table (K = 8, one digit, one chunk: NB * 12 operand planes per side, NB * 21
  * job planes) on its CTA-pair kernel, 5 the same at level 2 (NB * 16 operand
- * planes, NB * 25 job planes), 6 at level 3 (NB * 18, NB * 27).  *mismatches receives the number of
+ * planes, NB * 25 job planes), 6 at level 3 (NB * 18, NB * 27), 7 the
+ * t-grouped kernel on a digit-sum job table (dA = dB = 3: class w multiplies
+ * digit w of A by digit w of B).  *mismatches receives the number of
  * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,

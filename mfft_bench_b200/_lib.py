@@ -34,7 +34,7 @@ class PlanInfo(C.Structure):
         ("int8_macs", C.c_double), ("schoolbook_macs", C.c_double), ("pw_kernel", C.c_int),
         ("kind", C.c_int), ("U", C.c_int), ("balanced", C.c_int), ("half_points", C.c_int),
         ("wA", C.c_int), ("wB", C.c_int), ("schoolbook7_macs", C.c_double), ("kara", C.c_int),
-        ("rblock", C.c_int)]
+        ("rblock", C.c_int), ("dsum", C.c_int)]
 
     def as_dict(self):
         return {f: getattr(self, f) for f, _ in self._fields_}
@@ -72,6 +72,7 @@ _sig("mfftgpu_sync", i32, vp)
 _sig("mfftgpu_set_reuse_b", i32, vp, i32)
 _sig("mfftgpu_set_kernel_variant", i32, vp, i32, i32)
 _sig("mfftgpu_set_karatsuba", i32, vp, i32)
+_sig("mfftgpu_set_digit_sums", i32, vp, i32)
 _sig("mfftgpu_set_half_points", i32, vp, i32)
 _sig("mfftgpu_set_method", i32, vp, i32)
 _sig("mfftgpu_set_output_plane_stride", i32, vp, C.c_longlong)

@@ -125,6 +125,11 @@ class Context:
         at the evaluation points 0 and NB/2; identical results."""
         self._check(lib.mfftgpu_set_half_points(self._h, int(bool(on))), "set_half_points")
 
+    def set_digit_sums(self, on):
+        """Digit sums on the two-digit plans (default on): three int8 plane
+        products per term instead of four; same bits."""
+        self._check(lib.mfftgpu_set_digit_sums(self._h, int(bool(on))), "set_digit_sums")
+
     def set_karatsuba(self, level):
         """Karatsuba pointwise level on plans that allow it: 0 off, 1 one
         level (True), 2 P0 and P1 split again, 3 P2 as well (the default);

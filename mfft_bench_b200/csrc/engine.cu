@@ -70,6 +70,7 @@ struct mfftgpu_ctx {
     int fwd_variant = 0;          // forward kernel: 0 auto, 1 generic kernel
     int method = 0;               // 0 MFFT, 1 limb-plane schoolbook (value-mode products)
     int kara = kDefaultKara;      // Karatsuba level where the plan allows it
+    int dsum = 1;                 // digit sums on the two-digit plans
     int kara_stages = 0;          // level-3 pipeline: 4 four 48 KB stages; 0 / 2 two of 96 KB
     long long out_plane_stride = 0;  // _dev integer outputs: elements between planes (0: compact)
     // transformed-B cache: valid while the workspace is not reallocated
@@ -77,7 +78,7 @@ struct mfftgpu_ctx {
     bool b_valid = false;
     const void* b_ptr = nullptr;
     int b_fmt = -1, b_n = 0, b_b = 0, b_Lb = 0, b_S = 0, b_NB = 0, b_dB = 0, b_lo = 0, b_sgrid = 0,
-        b_trunc = 0, b_kind = 0, b_kara = 0;
+        b_trunc = 0, b_kind = 0, b_kara = 0, b_dsum = 0;
     Plan last_plan{};
     bool have_plan = false;
     int last_pw_kernel = 0;
@@ -217,7 +218,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
                           C->b_n == P.n && C->b_b == P.b && C->b_Lb == P.LbB && C->b_S == P.S &&
                           C->b_NB == P.NB && C->b_dB == P.dB && C->b_lo == B.lo_bit &&
                           C->b_sgrid == B.S_grid && C->b_trunc == B.trunc_rel &&
-                          C->b_kara == P.kara;
+                          C->b_kara == P.kara && C->b_dsum == P.dsum;
     char* DB = C->ws;
     int8_t* F = reinterpret_cast<int8_t*>(DB + szDB);
     char* DA = DB + szDB + szF;
@@ -292,6 +293,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
     fb.err = C->d_err;
     fb.b = P.b;
     fb.variant = C->fwd_variant;
+    fb.dsum = P.dsum;
     if (!b_cached) {
         C->b_valid = false;
         tick(0);
@@ -318,6 +320,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
         C->b_sgrid = B.S_grid;
         C->b_trunc = B.trunc_rel;
         C->b_kara = P.kara;
+        C->b_dsum = P.dsum;
     }
 
     // ---- A row blocks
@@ -374,7 +377,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
         L.kdim = n_int;
         L.jobs = PwJobs{P.K, P.dA, P.dB, P.nW, P.nchunk, P.njobs, school ? 1 : 0, P.LbA, P.LbB, P.U,
                         P.NB, (!school && !P.kara && C->half_points && P.K == 2 * P.S) ? P.S : 0,
-                        P.kara};
+                        P.kara, P.dsum};
         L.map_rows = (int)std::max<long long>(rb, 256);
         L.kara_stages = C->kara_stages;
         L.block_n = n_int <= 64 ? 64 : (n_int <= 128 ? 128 : 256);
@@ -428,6 +431,7 @@ int run_product(mfftgpu_ctx* C, const Plan& plan, const Operand& A, const Operan
         ia.LbB = P.LbB;
         ia.U = P.U;
         ia.kara = P.kara;
+        ia.dsum = P.dsum;
         tick(3);
         if ((rc = inverse_launch(ia, st))) return set_err(C, rc, "inverse launch failed (%d)", rc);
         ++C->launches;
@@ -460,6 +464,7 @@ int plan_or_err(mfftgpu_ctx* C, int n, int mode, int wA, int wB, Plan* P,
         return set_err(C, MFFTB_ERR_PLAN, "no exact int8 plan for n=%d mode=%d widths %d/%d", n,
                        mode, wA, wB);
     plan_set_kara(*P, C->kara);
+    if (C->dsum) plan_set_dsum(*P);
     return MFFTB_OK;
 }
 
@@ -556,6 +561,7 @@ int mfftgpu_create(mfftgpu_ctx** out, int device) {
     if (const char* s = getenv("MFFTGPU_PW_VARIANT")) C->pw_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_WAVE_SYNC")) C->wave_sync = atoi(s);
     if (const char* s = getenv("MFFTGPU_KARA_STAGES")) C->kara_stages = atoi(s);
+    if (const char* s = getenv("MFFTGPU_DSUM")) C->dsum = atoi(s) != 0;
     if (const char* s = getenv("MFFTGPU_HALF_POINTS")) C->half_points = atoi(s) != 0;
     if (const char* s = getenv("MFFTGPU_INV_VARIANT")) C->inv_variant = atoi(s);
     if (const char* s = getenv("MFFTGPU_FWD_VARIANT")) C->fwd_variant = atoi(s) == 1 ? 1 : 0;
@@ -671,6 +677,12 @@ int mfftgpu_set_half_points(mfftgpu_ctx* C, int on) {
     return MFFTB_OK;
 }
 
+int mfftgpu_set_digit_sums(mfftgpu_ctx* C, int on) {
+    if (!C || on < 0 || on > 1) return MFFTB_ERR_ARG;
+    C->dsum = on;
+    return MFFTB_OK;
+}
+
 int mfftgpu_set_karatsuba(mfftgpu_ctx* C, int level) {
     if (!C || level < 0 || level > 3) return MFFTB_ERR_ARG;
     C->kara = level;
@@ -751,7 +763,8 @@ int mfftgpu_plan_info_get(int n, int mode, int wA, int wB, mfftgpu_plan_info* o)
     } else if (plan_search(n, mode, wA, wB, 0, 0, &P)) {
         return MFFTB_ERR_PLAN;
     } else {
-        plan_set_kara(P, kDefaultKara);  // the default context setting
+        plan_set_kara(P, kDefaultKara);  // the default context settings
+        plan_set_dsum(P);
     }
     fill_info(P, o);
     return MFFTB_OK;
@@ -799,6 +812,7 @@ static void fill_info(const Plan& P, mfftgpu_plan_info* o) {
     o->wB = P.wB;
     o->schoolbook7_macs = (double)n * n * (double)n * ((P.wA + 6) / 7) * ((P.wB + 6) / 7);
     o->kara = P.kara;
+    o->dsum = P.dsum;
     o->rblock = 0;
     o->pw_kernel = 0;
     o->kind = P.kind;
@@ -1133,6 +1147,15 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;
+    // variant 7: the t-grouped kernel on a digit-sum job table (dA = dB = 3,
+    // class w pairs digit w with digit w)
+    if (variant == 7) {
+        if (dA != 3 || dB != 3) return MFFTB_ERR_ARG;
+        J.nW = 3;
+        J.njobs = NB * K * 3 * nchunk;
+        J.dsum = 1;
+        variant = 3;
+    }
     if (kara) {
         J.NB = NB;
         J.kara = variant - 3;

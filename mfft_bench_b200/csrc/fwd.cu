@@ -157,18 +157,24 @@ __global__ void __launch_bounds__(256) forward_kernel(const FwdArgs a) {
                 x[2] += sgn * v[2];
                 x[3] += sgn * v[3];
             }
-            // d signed int8 digits: balanced 7-bit low digits, top digit rest
+            // d signed int8 digits: balanced 7-bit low digits, top digit
+            // rest; with digit sums the two digits of the split, then their sum
+            const int nsplit = a.dsum ? 2 : a.d;
+            int dsum4[4] = {0, 0, 0, 0};
             for (int dd = 0; dd < a.d; ++dd) {
                 int dg[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    if (dd < a.d - 1) {
+                    if (dd >= nsplit) {
+                        dg[q] = dsum4[q];
+                    } else if (dd < nsplit - 1) {
                         int lo = ((x[q] + 64) & 127) - 64;
                         dg[q] = lo;
                         x[q] = (x[q] - lo) >> 7;
                     } else {
                         dg[q] = x[q];
                     }
+                    dsum4[q] += dd < nsplit ? dg[q] : 0;
                 }
                 if (!a.f_stack) {
                     long long plane = ((long long)j * a.d + dd) * nplanes_j + c;
@@ -370,7 +376,7 @@ __global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a, int np
     // d signed int8 digits per value (balanced 7-bit low digits, top digit
     // the rest), the same split as forward_kernel
     const long long plane0 = (long long)j * a.d * (a.f_stack ? (2 * K - 1) : K);
-    if (a.d <= 2) {
+    if (a.d <= 2 || a.dsum) {
         // the same split on the packed int16 pairs: lo = ((x + 64) & 127) - 64
         // per halfword (only its low 7 bits matter, so a wrapping add is
         // exact), hi = (x - lo) / 128, whose byte is bits 7..14 of each
@@ -397,8 +403,14 @@ __global__ void __launch_bounds__(256) forward_pt_kernel(const FwdArgs a, int np
             }
             const uint32_t lo01 = __vsub2(__vadd2(p01, 0x00400040u) & 0x007F007Fu, 0x00400040u);
             const uint32_t lo23 = __vsub2(__vadd2(p23, 0x00400040u) & 0x007F007Fu, 0x00400040u);
-            store_planes(0, c, __byte_perm(lo01, lo23, 0x6420));
-            store_planes(1, c, __byte_perm(__vsub2(p01, lo01) >> 7, __vsub2(p23, lo23) >> 7, 0x6420));
+            const uint32_t lo = __byte_perm(lo01, lo23, 0x6420);
+            const uint32_t hi =
+                __byte_perm(__vsub2(p01, lo01) >> 7, __vsub2(p23, lo23) >> 7, 0x6420);
+            store_planes(0, c, lo);
+            store_planes(1, c, hi);
+            // digit sums: lo + hi per byte (in [-128, 127] by the plan, so
+            // the byte-wise wrapping add is exact)
+            if (a.dsum) store_planes(2, c, __vadd4(lo, hi));
         }
         return;
     }
@@ -462,6 +474,7 @@ static int launch_simd(const FwdArgs& a, cudaStream_t stream) {
 
 int forward_launch(const FwdArgs& a, cudaStream_t stream) {
     if (a.nelem % 4 || a.d < 1 || a.d > 4) return MFFTB_ERR_ARG;
+    if (a.dsum && (a.d != 3 || a.f_stack >= 2)) return MFFTB_ERR_ARG;
     // Karatsuba operands: one int8 digit per value, blocks of S = K/2
     if (a.f_stack >= 2 && (a.d != 1 || 2 * a.S != a.K)) return MFFTB_ERR_ARG;
     if (a.f_stack >= 3 && a.S < 2) return MFFTB_ERR_ARG;

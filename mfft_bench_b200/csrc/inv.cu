@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(INV_THREADS) inverse_kernel(const InvArgs a) {
             for (int w = 0; w < a.nW; ++w) {
                 int64_t s = 0;
                 for (int ch = 0; ch < a.nchunk; ++ch, src += a.acc_plane) s += (int64_t)__ldg(src);
-                v += s * ((int64_t)1 << (7 * w));
+                v += s * inv_class_weight(a.dsum, w);
             }
         }
         sm[idx] = v;
@@ -318,7 +318,7 @@ __global__ void __launch_bounds__(128, KARA >= 2 ? 3 : 1) inverse_reg_kernel(con
                     int64_t s = 0;
                     for (int ch = 0; ch < a.nchunk; ++ch, src += a.acc_plane)
                         s += (int64_t)__ldg(src);
-                    v += s * ((int64_t)1 << (7 * w));
+                    v += s * inv_class_weight(a.dsum, w);
                 }
                 x[bitrev(j)][t] = v;
             }
@@ -574,7 +574,7 @@ __global__ void __launch_bounds__(INVL_THREADS, 2) inverse_lane_kernel(const Inv
 #pragma unroll
                     for (int kk = 0; kk < INVL_KB; ++kk) {
                         if (kk >= kn) break;
-                        const int64_t f = (int64_t)1 << (7 * ((k0 + kk) / a.nchunk));
+                        const int64_t f = inv_class_weight(a.dsum, (k0 + kk) / a.nchunk);
                         s0 += (int64_t)r[u][kk].x * f;
                         s1 += (int64_t)r[u][kk].y * f;
                         s2 += (int64_t)r[u][kk].z * f;

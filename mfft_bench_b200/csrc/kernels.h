@@ -56,6 +56,8 @@ struct FwdArgs {
     int* err;
     int b;             // digit width: every digit has |digit| <= 2^b
     int variant;       // 0 auto, 1 the generic kernel only (for comparisons)
+    int dsum;          // digit sums (d = 3): digits lo, hi of the two-digit split, then
+                       // lo + hi (the plan bounds it to int8)
 };
 int forward_launch(const FwdArgs& a, cudaStream_t stream);
 
@@ -100,8 +102,18 @@ struct InvArgs {
     // the Q's of P2 at 18..26.  The register kernel reads every layout, the
     // lane kernel kara = 1 only.
     int kara;
+    // digit sums (nW = 3): class w holds the products of digit w of A with
+    // digit w of B -- lo*lo, hi*hi, (lo+hi)*(lo+hi) -- so Chat = (1 - 2^7) acc0
+    // + (2^14 - 2^7) acc1 + 2^7 acc2 instead of the sum over w of 2^(7w) acc_w
+    int dsum;
 };
 int inverse_launch(const InvArgs& a, cudaStream_t stream);
+
+// weight of digit class w in Chat (see InvArgs::dsum)
+__host__ __device__ inline int64_t inv_class_weight(int dsum, int w) {
+    if (dsum) return w == 0 ? 1 - 128 : (w == 1 ? 16384 - 128 : 128);
+    return (int64_t)1 << (7 * w);
+}
 
 // fp32 exponent scan of src/fpfixed.c:40-54: out[0] = min e2, out[1] = max e2,
 // out[2] = any finite non-zero (e2 = frexp exponent - 24).

@@ -163,6 +163,50 @@ void plan_set_kara(Plan& p, int level) {
     }
 }
 
+// chunks per class of a digit-sum plan (0: none fits); *worst receives the
+// largest accumulator bound
+static int dsum_chunks(const Plan& p, long long* worst) {
+    const long long lim = 2147483647LL;
+    const long long bA[3] = {p.boundA[0], p.boundA[1], (long long)p.boundA[0] + p.boundA[1]};
+    const long long bB[3] = {p.boundB[0], p.boundB[1], (long long)p.boundB[0] + p.boundB[1]};
+    for (int c = 1; c <= p.K; ++c) {
+        long long w = 0;
+        bool ok = true;
+        for (int cls = 0; cls < 3 && ok; ++cls) {
+            const long long bnd = (long long)((p.K + c - 1) / c) * p.n_int * bA[cls] * bB[cls];
+            if (bnd > lim) ok = false;
+            if (bnd > w) w = bnd;
+        }
+        if (ok) {
+            *worst = w;
+            return c;
+        }
+    }
+    return 0;
+}
+
+bool plan_dsum_ok(const Plan& p) {
+    if (p.kind != KIND_MFFT || p.kara || p.dsum || p.dA != 2 || p.dB != 2) return false;
+    if (p.boundA[0] > 64 || p.boundB[0] > 64 || p.boundA[1] > 64 || p.boundB[1] > 64)
+        return false;
+    long long worst = 0;
+    return dsum_chunks(p, &worst) > 0;
+}
+
+void plan_set_dsum(Plan& p) {
+    if (!plan_dsum_ok(p)) return;
+    long long worst = 0;
+    p.nchunk = dsum_chunks(p, &worst);
+    p.acc_bound = worst;
+    p.dsum = 1;
+    p.dA = p.dB = 3;
+    p.nW = 3;
+    p.boundA[2] = p.boundA[0] + p.boundA[1];
+    p.boundB[2] = p.boundB[0] + p.boundB[1];
+    p.njobs = p.NB * p.K * p.nW * p.nchunk;
+    p.macs_per_elem = (double)p.NB * p.K * p.K * 3 * p.n_int;
+}
+
 int plan_search_school(int n, int wA, int wB, int force_b, Plan* out, int balanced_ok) {
     if (n <= 0 || wA <= 0 || wB <= 0 || !out) return 1;
     if (force_b > 8 || (force_b == 8 && !balanced_ok)) return 1;

@@ -62,6 +62,13 @@ struct Plan {
     // plane products per point, 12 at the half points, NB * 25 job planes);
     // kara = 3 splits P2 as well (36 per point, NB * 27 job planes).
     int kara;
+    // Digit sums (two-digit plans): each transformed value x = lo + 2^7 hi
+    // also gets the digit lo + hi, and the product's middle class
+    // lo_A hi_B + hi_A lo_B comes from (lo_A + hi_A)(lo_B + hi_B) - lo_A lo_B -
+    // hi_A hi_B: three digit-pair products per term instead of four.  The
+    // plan then has dA = dB = 3 digits and nW = 3 classes (lo*lo, hi*hi,
+    // sum*sum), one digit pair each.
+    int dsum;
 };
 
 // Returns 0 and fills *p on success.  wA / wB: magnitude bits per entry in
@@ -91,6 +98,13 @@ int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced
 // has at most two per block, |sum| <= 2 boundA <= 127, and its
 // accumulators have at most 2 terms.
 bool plan_kara_ok(const Plan& p);
+// Whether a plan can take digit sums: two int8 digits per value on both
+// sides, lo in [-64, 63] and |hi| <= 64, so lo + hi lies in [-128, 127]; and
+// chunks that keep every class's accumulators below 2^31.
+bool plan_dsum_ok(const Plan& p);
+// Switch a two-digit plan to digit sums (dA = dB = 3, nW = 3, chunks, job
+// planes and issued MACs); a plan that cannot take them is left unchanged.
+void plan_set_dsum(Plan& p);
 // Set a plan's Karatsuba level (0 = negacyclic; 1; 2, P0 and P1 split once
 // more; 3, P2 as well; job planes and issued MACs); a level the plan cannot
 // take falls back to 0.

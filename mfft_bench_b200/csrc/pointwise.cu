@@ -674,7 +674,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PW_THREADS, 1)
             pw3_point_ranges(p.jobs, j, t0, plo, phi);
             const int npr = pw_class_pairs(p.jobs, w);
             for (int pi = 0; pi < npr; ++pi) {
-            const int da = pw_class_first_da(p.jobs, w) + pi, db = w - da;
+            const int da = pw_class_first_da(p.jobs, w) + pi, db = pw_class_db(p.jobs, w, da);
             const int a_base = (j * p.jobs.dA + da) * K;            // Ahat planes (j, da, .)
             const int f_base = (j * p.jobs.dB + db) * (2 * K - 1);  // F planes (j, db, .)
             for (int cp = 0; cp < cps_per_kb; ++cp) {

@@ -89,6 +89,11 @@ struct PwJobs {
     // (a0+a1)[1]+(a0+a1)[3]; 27 job planes: the Q0, Q1, Q2 of P0 (0..8), of
     // P1 (9..17) and of P2 (18..26).
     int kara;
+    // digit sums (dA = dB = 3, nW = 3): the three digits of a transformed
+    // value are lo, hi and lo + hi, and class w multiplies digit w of A by
+    // digit w of B only (one digit pair per class instead of up to two); the
+    // inverse weighs the classes (1 - 2^7, 2^14 - 2^7, 2^7)
+    int dsum;
 };
 
 constexpr int PWK_OPS = 12;    // operand planes per point, kara = 1
@@ -203,13 +208,19 @@ __host__ __device__ inline void pw_job_decode(const PwJobs& J, int q, int& j, in
 }
 
 __host__ __device__ inline int pw_class_first_da(const PwJobs& J, int w) {
+    if (J.dsum) return w;
     int lo = w - (J.dB - 1);
     return lo > 0 ? lo : 0;
 }
 __host__ __device__ inline int pw_class_pairs(const PwJobs& J, int w) {
+    if (J.dsum) return 1;
     int lo = pw_class_first_da(J, w);
     int hi = w < J.dA - 1 ? w : J.dA - 1;
     return hi - lo + 1;
+}
+// B's digit paired with A's digit da in class w
+__host__ __device__ inline int pw_class_db(const PwJobs& J, int w, int da) {
+    return J.dsum ? w : w - da;
 }
 // segments [s0, s1) of job q's class that chunk ch covers; the split is
 // balanced so no chunk is empty while nchunk <= K (checked by the planner)
@@ -222,7 +233,7 @@ __host__ __device__ inline void pw_segment_planes(const PwJobs& J, int j, int t,
                                                   int& planeA, int& planeF) {
     int pair = s / J.K, c1 = s % J.K;
     int da = pw_class_first_da(J, w) + pair;
-    int db = w - da;
+    int db = pw_class_db(J, w, da);
     planeA = (j * J.dA + da) * J.K + c1;
     planeF = (j * J.dB + db) * (2 * J.K - 1) + (J.K - 1 - t + c1);
 }

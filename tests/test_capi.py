@@ -112,13 +112,26 @@ def test_plan_exactness_invariants(n, mode, w):
     else:
         assert pi["LbA"] == w and pi["b"] == 16
     MA = pi["ncA"] * dmax
-    # recompute the split bounds independently
+    # recompute the split bounds independently (digit sums: the two digits of
+    # the split, whose sum lo + hi must also be an int8)
+    nsplit = 2 if pi["dsum"] else pi["dA"]
     T, bounds = MA, []
-    for i in range(pi["dA"] - 1):
+    for i in range(nsplit - 1):
         bounds.append(min(64, T))
         T = (T + 64) // 128
     bounds.append(T)
-    assert T <= 127 and _split_ok(MA, pi["dA"], bounds)
+    assert T <= 127 and _split_ok(MA, nsplit, bounds)
+    if pi["dsum"]:
+        # lo in [-64, 63] and |hi| <= 64 keep lo + hi in [-128, 127]; three
+        # digit-pair classes (lo*lo, hi*hi, sum*sum) of K terms each
+        MB = pi["ncB"] * dmax
+        TB = (MB + 64) // 128
+        assert pi["dA"] == pi["dB"] == 3 and pi["nW"] == 3 and T <= 64 and TB <= 64
+        per = -(-pi["K"] // pi["nchunk"]) * pi["n_int"]
+        assert per * (64 + T) * (64 + TB) < 2 ** 31
+        assert pi["njobs"] == pi["NB"] * pi["K"] * 3 * pi["nchunk"]
+        assert pi["int8_macs"] == pi["NB"] * pi["K"] ** 2 * 3 * float(pi["n_int"]) ** 3
+        return
     if pi["kara"]:
         # Karatsuba pointwise: three full length-S convolutions per ordinary
         # point, one per half point; the sums a0 + a1 fit int8 and P2's

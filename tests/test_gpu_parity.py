@@ -418,6 +418,55 @@ def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
                                   variant=3 + level) == 0
 
 
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,nchunk", [
+    (256, 256, 512, 32, 16, 1),
+    (300, 272, 1000, 8, 16, 2),   # ragged, two contraction chunks per class
+    (128, 64, 256, 4, 64, 1),     # the c1 shape of plan (K = 64)
+])
+def test_digit_sum_pointwise_kernel(ctx, rows, cols, kdim, NB, K, nchunk):
+    """The t-grouped kernel on a digit-sum job table (class w multiplies digit
+    w of A by digit w of B) against a CUDA-core evaluation of the table."""
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 3, 3, nchunk, 256, variant=7) == 0
+
+
+@pytest.mark.parametrize("n,L,signed", [(256, 64, False), (300, 64, True), (64, 512, False),
+                                        (130, 128, False)])
+def test_digit_sums_are_exact(ctx, oracle, n, L, signed):
+    """Two-digit plans with digit sums (the default) and without them give the
+    same bits, and match the oracle's exact entries."""
+    gen = oracle.signed_planes if signed else oracle.bigmat_rand
+    A, B = gen(n, L, 91 + n), gen(n, L, 93 + L)
+    got = ctx.mm_u16(A, B, n, L, signed=signed)
+    p = ctx.last_plan()
+    assert p["dsum"] == 1 and p["dA"] == p["dB"] == 3 and p["nW"] == 3
+    ctx.set_digit_sums(0)
+    try:
+        ref = ctx.mm_u16(A, B, n, L, signed=signed)
+        q = ctx.last_plan()
+    finally:
+        ctx.set_digit_sums(1)
+    assert q["dsum"] == 0 and q["dA"] == q["dB"] == 2
+    assert p["int8_macs"] * 4 == q["int8_macs"] * 3
+    assert np.array_equal(got, ref)
+    RL = 2 * L + 1
+    rows = np.repeat(np.arange(n), n)[:: max(1, n * n // 1500)]
+    cols = np.tile(np.arange(n), n)[:: max(1, n * n // 1500)]
+    want = oracle.entries(A, B, n, L, signed, rows, cols, RL)
+    assert np.array_equal(got.reshape(RL, n, n)[:, rows, cols], want)
+
+
+def test_karatsuba_four_stage_pipeline(monkeypatch):
+    """The opt-in four-stage pipeline of the level-3 kernel (one k-block per
+    48 KB stage) on the same job-table check."""
+    monkeypatch.setenv("MFFTGPU_KARA_STAGES", "4")
+    c = m.Context(0)
+    try:
+        for rows, cols, kdim, NB in ((256, 128, 512, 8), (300, 144, 640, 4)):
+            assert c.selftest_pointwise(rows, cols, kdim, NB, 8, 1, 1, 1, 256, variant=6) == 0
+    finally:
+        c.close()
+
+
 @pytest.mark.parametrize("n,kind", [(256, "i64"), (300, "i64"), (1000, "i64"), (2112, "i64"),
                                     (512, "u16s"), (384, "u16")])
 def test_karatsuba_products_are_exact(ctx, oracle, n, kind):

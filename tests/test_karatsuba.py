@@ -179,6 +179,29 @@ def _merge(a, b):
     return out
 
 
+def test_digit_sum_identity():
+    """Digit sums: with x = lo + 2^7 hi (lo in [-64, 63]) on both sides,
+    xa xb = (1 - 2^7) lo_a lo_b + (2^14 - 2^7) hi_a hi_b
+            + 2^7 (lo_a + hi_a)(lo_b + hi_b),
+    the class weights the inverse kernels apply; |hi| <= 64 keeps lo + hi an
+    int8.  Checked at the extremes of the c1 plan's values (|x| <= 8160)."""
+    rng = random.Random(17)
+
+    def split(x):
+        lo = ((x + 64) & 127) - 64
+        return lo, (x - lo) >> 7
+
+    for _ in range(20000):
+        xa, xb = rng.randint(-8160, 8160), rng.randint(-8160, 8160)
+        (la, ha), (lb, hb) = split(xa), split(xb)
+        assert -128 <= la + ha <= 127 and -128 <= lb + hb <= 127
+        got = (1 - 128) * la * lb + (16384 - 128) * ha * hb + 128 * (la + ha) * (lb + hb)
+        assert got == xa * xb
+    for xa in (-8160, 8160, -8097, 8095):
+        la, ha = split(xa)
+        assert -128 <= la + ha <= 127
+
+
 def test_karatsuba_extremes():
     """All-extreme operands: every job value and the recombined coefficients
     stay within the int32 accumulator and int64 inverse bounds the planner
