@@ -1147,14 +1147,15 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
     if (kara && (K != 8 || dA != 1 || dB != 1 || nchunk != 1 || NB < 2 || NB > 8 || cols < 128))
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;
-    // variant 7: the t-grouped kernel on a digit-sum job table (dA = dB = 3,
-    // class w pairs digit w with digit w)
+    // variant 7: a digit-sum job table (dA = dB = 3, class w pairs digit w
+    // with digit w) on the t-grouped kernel, or with several contraction
+    // chunks on the kernel the product path picks
     if (variant == 7) {
         if (dA != 3 || dB != 3) return MFFTB_ERR_ARG;
         J.nW = 3;
         J.njobs = NB * K * 3 * nchunk;
         J.dsum = 1;
-        variant = 3;
+        variant = nchunk == 1 ? 3 : 0;
     }
     if (kara) {
         J.NB = NB;

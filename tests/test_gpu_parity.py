@@ -424,8 +424,9 @@ def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
     (128, 64, 256, 4, 64, 1),     # the c1 shape of plan (K = 64)
 ])
 def test_digit_sum_pointwise_kernel(ctx, rows, cols, kdim, NB, K, nchunk):
-    """The t-grouped kernel on a digit-sum job table (class w multiplies digit
-    w of A by digit w of B) against a CUDA-core evaluation of the table."""
+    """A digit-sum job table (class w multiplies digit w of A by digit w of B)
+    on the t-grouped kernel (one chunk) or the CTA-pair kernel (two chunks)
+    against a CUDA-core evaluation of the table."""
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 3, 3, nchunk, 256, variant=7) == 0
 
 
