@@ -131,17 +131,27 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
     return 0;
 }
 
-bool plan_kara_ok(const Plan& p) {
+int plan_kara_max_level(const Plan& p) {
     if (p.kind != KIND_MFFT || p.mode != PLAN_VALUE || p.K != 8 || p.S != 4 || p.dA != 1 ||
-        p.dB != 1 || p.nchunk != 1 || p.NB < 2 || p.NB > 8)
-        return false;
-    const long long sa = 2LL * p.boundA[0], sb = 2LL * p.boundB[0];
-    if (sa > 127 || sb > 127) return false;
-    return 4LL * p.n_int * sa * sb <= 2147483647LL;
+        p.dB != 1 || p.nchunk != 1 || p.NB < 2 || p.NB > 8 || p.dsum)
+        return 0;
+    const long long lim = 2147483647LL;
+    const long long A = p.boundA[0], B = p.boundB[0];
+    // level 1: the operands of P2, one digit term per block, are int8 like
+    // the values; P2's accumulators sum up to 4 terms of length n
+    if (A > 127 || B > 127 || 4LL * p.n_int * A * B > lim) return 0;
+    // levels 2 and 3: sums of two terms per block, accumulators of at most
+    // 2 terms of such sums
+    if (2 * A > 127 || 2 * B > 127 || 2LL * p.n_int * (2 * A) * (2 * B) > lim) return 1;
+    return 3;
 }
 
+bool plan_kara_ok(const Plan& p) { return plan_kara_max_level(p) > 0; }
+
 void plan_set_kara(Plan& p, int level) {
-    if (level < 0 || level > 3 || (level && !plan_kara_ok(p))) level = 0;
+    if (level < 0 || level > 3) level = 0;
+    const int top = plan_kara_max_level(p);
+    if (level > top) level = top;
     p.kara = level;
     const double S2 = (double)p.S * p.S;
     const double pts = p.NB <= 2 ? 0.0 : (double)p.NB - 2.0;  // ordinary points

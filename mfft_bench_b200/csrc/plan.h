@@ -86,17 +86,17 @@ int plan_search(int n, int mode, int wA, int wB, int force_b, int force_S, Plan*
 // balanced_ok: the operands are two's complement int64 entries, which may use
 // balanced 8-bit digits (ceil((W+1)/8) of them).
 int plan_search_school(int n, int wA, int wB, int force_b, Plan* p, int balanced_ok = 0);
-// Whether the Karatsuba pointwise keeps the plan exact: one int8 digit per
-// transformed value with room for the sums a0 + a1 (2 |x| <= 127), K = 8,
-// one contraction chunk, and every int32 accumulator of P2 = (a0+a1)(b0+b1)
-// (4 terms of length n) below 2^31.  The further levels need nothing more.
-// A block of the transform holds S coefficients in a ring of K = 2S, so a
-// signed permutation y^e puts each block's digit in exactly one of the
-// positions c and c+S: (a0 + a1)[c] = x[c] + x[c+S] has one digit term per
-// block, as x[c] has, and |a0 + a1| <= boundA.  Every sum the second level
-// forms -- x[c] + x[c+2] (P0, P1) or (a0+a1)[c] + (a0+a1)[c+2] (P2) -- then
-// has at most two per block, |sum| <= 2 boundA <= 127, and its
-// accumulators have at most 2 terms.
+// The deepest Karatsuba level that keeps the plan exact (0: none).  Every
+// level needs K = 8, one int8 digit per transformed value and one
+// contraction chunk.  A block of the transform holds S coefficients in a
+// ring of K = 2S, so a signed permutation y^e puts each block's digit in
+// exactly one of the positions c and c+S: (a0 + a1)[c] = x[c] + x[c+S] has
+// one digit term per block, as x[c] has, and |a0 + a1| <= boundA (level 1;
+// P2's int32 accumulators sum up to 4 terms of length n).  Every sum the
+// second level forms -- x[c] + x[c+2] (P0, P1) or (a0+a1)[c] +
+// (a0+a1)[c+2] (P2) -- has at most two terms per block, so levels 2 and 3
+// need 2 boundA <= 127 (accumulators of at most 2 terms of such sums).
+int plan_kara_max_level(const Plan& p);
 bool plan_kara_ok(const Plan& p);
 // Whether a plan can take digit sums: two int8 digits per value on both
 // sides, lo in [-64, 63] and |hi| <= 64, so lo + hi lies in [-128, 127]; and
@@ -106,8 +106,8 @@ bool plan_dsum_ok(const Plan& p);
 // planes and issued MACs); a plan that cannot take them is left unchanged.
 void plan_set_dsum(Plan& p);
 // Set a plan's Karatsuba level (0 = negacyclic; 1; 2, P0 and P1 split once
-// more; 3, P2 as well; job planes and issued MACs); a level the plan cannot
-// take falls back to 0.
+// more; 3, P2 as well; job planes and issued MACs), capped at the deepest
+// level the plan can take.
 void plan_set_kara(Plan& p, int level);
 // Whether job (t, ch) of a schoolbook plan has any term.
 inline bool school_job_live(const Plan& p, int t, int ch) {

@@ -134,19 +134,24 @@ def test_plan_exactness_invariants(n, mode, w):
         return
     if pi["kara"]:
         # Karatsuba pointwise: three full length-S convolutions per ordinary
-        # point, one per half point; the sums a0 + a1 fit int8 and P2's
-        # accumulators (S terms of length n) fit int32.  The default level 3
-        # takes P0, P1 and P2 as three length-S/2 convolutions each: their
-        # sums have two digit terms per block, with at most S/2 terms per
-        # accumulator.
+        # point, one per half point.  The operands a0 + a1 take one digit per
+        # transform block, so they are bounded like the values (MA), and P2's
+        # accumulators sum S terms of length n.  Level 3 (the default where
+        # it fits) takes P0, P1 and P2 as three length-S/2 convolutions each:
+        # their sums take two digits per block (2 MA <= 127), with at most
+        # S/2 terms per accumulator; otherwise the plan stays at level 1.
         NB, S = pi["NB"], pi["S"]
+        MB = pi["ncB"] * dmax
         assert pi["K"] == 8 and pi["dA"] == pi["dB"] == 1 and pi["nchunk"] == 1 and NB <= 8
-        assert 2 * MA <= 127 and 2 * pi["ncB"] * dmax <= 127
-        assert S * pi["n_int"] * (2 * MA) * (2 * pi["ncB"] * dmax) < 2 ** 31
-        assert pi["kara"] == 3 and pi["njobs"] == NB * 27
-        q = 3 * (S // 2) ** 2
+        assert MA <= 127 and MB <= 127 and S * pi["n_int"] * MA * MB < 2 ** 31
         nh = min(NB, 2)
-        assert pi["int8_macs"] == (3 * q * (NB - nh) + q * nh) * float(pi["n_int"]) ** 3
+        if 2 * MA <= 127 and 2 * MB <= 127 and 2 * pi["n_int"] * (2 * MA) * (2 * MB) < 2 ** 31:
+            assert pi["kara"] == 3 and pi["njobs"] == NB * 27
+            q = 3 * (S // 2) ** 2
+            assert pi["int8_macs"] == (3 * q * (NB - nh) + q * nh) * float(pi["n_int"]) ** 3
+        else:
+            assert pi["kara"] == 1 and pi["njobs"] == NB * 21
+            assert pi["int8_macs"] == (3 * S * S * (NB - nh) + S * S * nh) * float(pi["n_int"]) ** 3
     else:
         assert pi["njobs"] == pi["NB"] * pi["K"] * pi["nW"] * pi["nchunk"]
         assert pi["int8_macs"] == (pi["NB"] * pi["K"] ** 2 * pi["dA"] * pi["dB"]

@@ -225,9 +225,13 @@ def test_planner_uses_karatsuba_on_the_w64_plan():
     # 6 ordinary points x 3 x 12 + 2 half points x 12 = 240 plane products
     # (P2 one level deep: 264; one level: 6 x 48 + 2 x 16 = 320; none: 512)
     assert pi["int8_macs"] == 240 * 16384.0 ** 3
-    # past n ~ 37000 the P2 accumulators (4 * n * 120^2) would pass 2^31
-    assert m.plan_info(40000, 0, 64)["kara"] == 0
-    # plans whose transformed sums do not leave room for a0 + a1 keep the
-    # negacyclic pointwise
-    assert m.plan_info(8192, 0, 68)["kara"] == 0
+    # the level-3 accumulators (2 terms of sums <= 120) fit int32 up to
+    # n ~ 74565; the W = 64 plan changes beyond that
+    assert m.plan_info(40000, 0, 64)["kara"] == 3
+    assert m.plan_info(74560, 0, 64)["kara"] == 3
+    # b = 5 (values <= 124, c4's plan): a0 + a1 still fits int8 (one digit per
+    # block), the second level's sums (<= 248) do not -- one level
+    pi = m.plan_info(8192, 0, 68)
+    assert (pi["b"], pi["kara"], pi["njobs"]) == (5, 1, 8 * 21)
+    # plans with K != 8 or two digits keep the negacyclic pointwise
     assert m.plan_info(4096, 0, 1024)["kara"] == 0
