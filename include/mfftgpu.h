@@ -257,7 +257,7 @@ void mfftgpu_gen_normal_f32(float *A, float *B, size_t count, uint64_t seed);
  * job planes) on its CTA-pair kernel, 5 the same at level 2 (NB * 16 operand
  * planes, NB * 25 job planes), 6 at level 3 (NB * 18, NB * 27), 7 a
  * digit-sum job table (dA = dB = 3: class w multiplies digit w of A by digit
- * w of B) on the t-grouped kernel (one chunk) or the automatic choice.  *mismatches receives the number of
+ * w of B) on the kernel the product path picks for the shape.  *mismatches receives the number of
  * differing elements. */
 int mfftgpu_selftest_pointwise(mfftgpu_ctx *ctx, int rows, int cols, int kdim, int NB, int K,
                                int dA, int dB, int nchunk, int block_n, int variant,

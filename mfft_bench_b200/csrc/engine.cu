@@ -1148,14 +1148,13 @@ int mfftgpu_selftest_pointwise(mfftgpu_ctx* C, int rows, int cols, int kdim, int
         return MFFTB_ERR_ARG;
     const int arows = kara ? std::max(rows, 256) : rows;
     // variant 7: a digit-sum job table (dA = dB = 3, class w pairs digit w
-    // with digit w) on the t-grouped kernel, or with several contraction
-    // chunks on the kernel the product path picks
+    // with digit w) on the kernel the product path picks for the shape
     if (variant == 7) {
         if (dA != 3 || dB != 3) return MFFTB_ERR_ARG;
         J.nW = 3;
         J.njobs = NB * K * 3 * nchunk;
         J.dsum = 1;
-        variant = nchunk == 1 ? 3 : 0;
+        variant = 0;
     }
     if (kara) {
         J.NB = NB;

@@ -425,8 +425,9 @@ def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
 ])
 def test_digit_sum_pointwise_kernel(ctx, rows, cols, kdim, NB, K, nchunk):
     """A digit-sum job table (class w multiplies digit w of A by digit w of B)
-    on the t-grouped kernel (one chunk) or the CTA-pair kernel (two chunks)
-    against a CUDA-core evaluation of the table."""
+    on the kernel the product path picks -- t-grouped (one chunk, 256 rows),
+    CTA pairs (two chunks), one CTA per tile (the small c1 shape) -- against a
+    CUDA-core evaluation of the table."""
     assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 3, 3, nchunk, 256, variant=7) == 0
 
 
