@@ -418,17 +418,17 @@ def test_karatsuba_pointwise_kernel(ctx, rows, cols, kdim, NB, level):
                                   variant=3 + level) == 0
 
 
-@pytest.mark.parametrize("rows,cols,kdim,NB,K,nchunk", [
-    (256, 256, 512, 32, 16, 1),
-    (300, 272, 1000, 8, 16, 2),   # ragged, two contraction chunks per class
-    (128, 64, 256, 4, 64, 1),     # the c1 shape of plan (K = 64)
+@pytest.mark.parametrize("rows,cols,kdim,NB,K,nchunk,bn", [
+    (256, 256, 512, 32, 16, 1, 256),
+    (300, 272, 1000, 8, 16, 2, 256),   # ragged, two contraction chunks per class
+    (128, 64, 256, 4, 64, 1, 64),      # the c1 shape of plan (K = 64)
 ])
-def test_digit_sum_pointwise_kernel(ctx, rows, cols, kdim, NB, K, nchunk):
+def test_digit_sum_pointwise_kernel(ctx, rows, cols, kdim, NB, K, nchunk, bn):
     """A digit-sum job table (class w multiplies digit w of A by digit w of B)
     on the kernel the product path picks -- t-grouped (one chunk, 256 rows),
     CTA pairs (two chunks), one CTA per tile (the small c1 shape) -- against a
     CUDA-core evaluation of the table."""
-    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 3, 3, nchunk, 256, variant=7) == 0
+    assert ctx.selftest_pointwise(rows, cols, kdim, NB, K, 3, 3, nchunk, bn, variant=7) == 0
 
 
 @pytest.mark.parametrize("n,L,signed", [(256, 64, False), (300, 64, True), (64, 512, False),
