@@ -118,6 +118,7 @@ def test_half_points_skip_is_exact(ctx, oracle, n, L, signed):
     (20, 49, True),     # b7 NB32 K16 d2, int8 digits
     (300, 16, True),    # b4 NB16 K16: the byte-SIMD kernel
     (24, 25, True),     # b13: sums too wide for int16 lanes, generic kernel either way
+    (300, 4, True),     # b4 NB8 K8, Karatsuba level 3: the 18 operand planes per point
 ])
 def test_forward_kernels_vs_generic(ctx, oracle, n, L, signed):
     """The one-point-per-warp and byte-SIMD forward kernels against the
