@@ -246,29 +246,14 @@ __global__ void __launch_bounds__(128, STAGED ? 2 : (KARA >= 2 ? 3 : 1))
         constexpr int NQP = KARA == 3 ? 27 : (KARA == 2 ? 25 : 21);
         constexpr int HALFQ = KARA == 1 ? 7 : 9;  // planes written at a half point
         const long long e0 = blockIdx.x * 128LL;
-        // BATCH 16-byte loads of each thread in flight before their stores
-        constexpr int NCOPY = NB * NQP * 32, NIT = (NCOPY + 127) / 128, BATCH = 12;
-#pragma unroll 1
-        for (int b0 = 0; b0 < NIT; b0 += BATCH) {
-            int4 val[BATCH];
-#pragma unroll
-            for (int u = 0; u < BATCH; ++u) {
-                const int idx = threadIdx.x + (b0 + u) * 128;
-                val[u] = make_int4(0, 0, 0, 0);
-                const int q = idx >> 5, v = idx & 31;
-                const int jq = q / NQP;
-                const long long e4 = e0 + 4 * v;  // total is a multiple of 4
-                if (b0 + u < NIT && idx < NCOPY && e4 < total &&
-                    !((jq == 0 || 2 * jq == NB) && q % NQP >= HALFQ))
-                    val[u] = __ldg(
-                        reinterpret_cast<const int4*>(a.acc + (long long)q * a.acc_plane + e4));
-            }
-#pragma unroll
-            for (int u = 0; u < BATCH; ++u) {
-                const int idx = threadIdx.x + (b0 + u) * 128;
-                if (b0 + u < NIT && idx < NCOPY)
-                    *reinterpret_cast<int4*>(stg + (idx >> 5) * 128 + 4 * (idx & 31)) = val[u];
-            }
+        for (int idx = threadIdx.x; idx < NB * NQP * 32; idx += 128) {
+            const int q = idx >> 5, v = idx & 31;
+            const int jq = q / NQP;
+            const long long e4 = e0 + 4 * v;  // total is a multiple of 4
+            int4 val = make_int4(0, 0, 0, 0);
+            if (e4 < total && !((jq == 0 || 2 * jq == NB) && q % NQP >= HALFQ))
+                val = __ldg(reinterpret_cast<const int4*>(a.acc + (long long)q * a.acc_plane + e4));
+            *reinterpret_cast<int4*>(stg + q * 128 + 4 * v) = val;
         }
         __syncthreads();
     }
