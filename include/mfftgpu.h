@@ -120,8 +120,7 @@ int mfftgpu_ipc_free(void *ptr);
  *   3 t-grouped CTA pairs (error at launch if the plan does not fit it);
  * stage 3 (inverse + carry): 0 auto, 1 the generic shared-memory kernel,
  *   2 the lane kernel wherever it covers the plan (also NB*K <= 64 plans,
- *   which auto gives the register kernel), 3 the register kernel without
- *   its shared-memory staging of Karatsuba job planes. */
+ *   which auto gives the register kernel). */
 int mfftgpu_set_kernel_variant(mfftgpu_ctx *ctx, int stage, int variant);
 /* Karatsuba pointwise level (0 to 3; the default 3, or $MFFTGPU_KARA).
  * Plans with K = 8 and one int8 digit whose sums a0 + a1 still fit int8 (the

@@ -695,7 +695,7 @@ int mfftgpu_set_kernel_variant(mfftgpu_ctx* C, int stage, int variant) {
         C->pw_variant = variant;
         return MFFTB_OK;
     }
-    if (stage == 3 && variant >= 0 && variant <= 3) {
+    if (stage == 3 && variant >= 0 && variant <= 2) {
         C->inv_variant = variant;
         return MFFTB_OK;
     }

@@ -204,19 +204,16 @@ __device__ __forceinline__ void ring_mul_pow(const int64_t (&v)[K], int64_t (&o)
 // kara = 2: a length-4 convolution P from the 9 job planes of its three
 // length-2 convolutions Q0, Q1, Q2 (3 coefficients each):
 // P = Q0 + y^2 (Q2 - Q0 - Q1) + y^4 Q1
-// (SMEM: src points into the shared-memory staging buffer)
-template <bool SMEM = false>
 __device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane,
                                              int64_t (&P)[7]) {
-    auto ld = [&](long long i) -> int64_t { return SMEM ? src[i] : __ldg(src + i); };
     int64_t q0[3], q1[3], m[3];
 #pragma unroll
     for (int s = 0; s < 3; ++s) {
-        q0[s] = ld(s * plane);
-        q1[s] = ld((3 + s) * plane);
+        q0[s] = __ldg(src + s * plane);
+        q1[s] = __ldg(src + (3 + s) * plane);
     }
 #pragma unroll
-    for (int s = 0; s < 3; ++s) m[s] = ld((6 + s) * plane) - q0[s] - q1[s];
+    for (int s = 0; s < 3; ++s) m[s] = (int64_t)__ldg(src + (6 + s) * plane) - q0[s] - q1[s];
     P[0] = q0[0];
     P[1] = q0[1];
     P[2] = q0[2] + m[0];
@@ -231,32 +228,11 @@ __device__ __forceinline__ void kara2_expand(const int32_t* src, long long plane
 // Levels 2 and 3 (25 / 27 planes per point) are held to three blocks per SM
 // (168 registers, a small spill): the loads in flight per SM matter more
 // than the spill (c5, level 2: 44.6 ms against 53.8 ms at two blocks per SM).
-// STAGED (Karatsuba levels, K = 8): the CTA first copies the job planes of
-// its 128 elements into shared memory with 16-byte loads ([plane][128]
-// int32, planes the pointwise step does not write skipped), so that a
-// thread's many 4-byte loads become a few wide ones in flight per SM.
-template <int NB, int K, int KARA, bool STAGED = false>
-__global__ void __launch_bounds__(128, STAGED ? 2 : (KARA >= 2 ? 3 : 1))
-    inverse_reg_kernel(const InvArgs a) {
+template <int NB, int K, int KARA>
+__global__ void __launch_bounds__(128, KARA >= 2 ? 3 : 1) inverse_reg_kernel(const InvArgs a) {
     constexpr int S = K / 2, LGNB = NB == 2 ? 1 : (NB == 4 ? 2 : 3);
     const long long e = blockIdx.x * 128LL + threadIdx.x;
     const long long total = (long long)a.rows * a.lda;
-    extern __shared__ int32_t stg[];  // STAGED: [NB * planes per point][128]
-    if constexpr (STAGED) {
-        constexpr int NQP = KARA == 3 ? 27 : (KARA == 2 ? 25 : 21);
-        constexpr int HALFQ = KARA == 1 ? 7 : 9;  // planes written at a half point
-        const long long e0 = blockIdx.x * 128LL;
-        for (int idx = threadIdx.x; idx < NB * NQP * 32; idx += 128) {
-            const int q = idx >> 5, v = idx & 31;
-            const int jq = q / NQP;
-            const long long e4 = e0 + 4 * v;  // total is a multiple of 4
-            int4 val = make_int4(0, 0, 0, 0);
-            if (e4 < total && !((jq == 0 || 2 * jq == NB) && q % NQP >= HALFQ))
-                val = __ldg(reinterpret_cast<const int4*>(a.acc + (long long)q * a.acc_plane + e4));
-            *reinterpret_cast<int4*>(stg + q * 128 + 4 * v) = val;
-        }
-        __syncthreads();
-    }
     if (e >= total) return;
     const int row = (int)(e / a.lda), col = (int)(e % a.lda);
     if (row >= a.rows || col >= a.cols) return;
@@ -277,18 +253,15 @@ __global__ void __launch_bounds__(128, STAGED ? 2 : (KARA >= 2 ? 3 : 1))
             // first forms P0 and P1 from their length-2 convolutions.
             constexpr int NQ = KARA == 3 ? 27 : (KARA == 2 ? 25 : 21);
             constexpr int P2 = KARA == 1 ? 14 : 18;
-            const long long pl = STAGED ? 128 : a.acc_plane;  // plane stride of src
-            auto ld = [&](const int32_t* p) -> int64_t { return STAGED ? *p : __ldg(p); };
 #pragma unroll
             for (int j = 0; j < NB; ++j) {
-                const int32_t* src = STAGED ? stg + j * NQ * 128 + threadIdx.x
-                                            : a.acc + (long long)j * NQ * a.acc_plane + e;
+                const int32_t* src = a.acc + (long long)j * NQ * a.acc_plane + e;
                 int64_t P0[7];
                 if constexpr (KARA >= 2) {
-                    kara2_expand<STAGED>(src, pl, P0);
+                    kara2_expand(src, a.acc_plane, P0);
                 } else {
 #pragma unroll
-                    for (int s = 0; s < 7; ++s) P0[s] = ld(src + s * pl);
+                    for (int s = 0; s < 7; ++s) P0[s] = __ldg(src + (long long)s * a.acc_plane);
                 }
                 if (j == 0 || 2 * j == NB) {  // half point: P0 only
 #pragma unroll
@@ -298,18 +271,21 @@ __global__ void __launch_bounds__(128, STAGED ? 2 : (KARA >= 2 ? 3 : 1))
                 }
                 int64_t P1[7], M[7];
                 if constexpr (KARA >= 2) {
-                    kara2_expand<STAGED>(src + 9 * pl, pl, P1);
+                    kara2_expand(src + 9 * a.acc_plane, a.acc_plane, P1);
                 } else {
 #pragma unroll
-                    for (int s = 0; s < 7; ++s) P1[s] = ld(src + (7 + s) * pl);
+                    for (int s = 0; s < 7; ++s)
+                        P1[s] = __ldg(src + (long long)(7 + s) * a.acc_plane);
                 }
                 if constexpr (KARA == 3) {
-                    kara2_expand<STAGED>(src + 18 * pl, pl, M);
+                    kara2_expand(src + 18 * a.acc_plane, a.acc_plane, M);
 #pragma unroll
                     for (int s = 0; s < 7; ++s) M[s] -= P0[s] + P1[s];
                 } else {
 #pragma unroll
-                    for (int s = 0; s < 7; ++s) M[s] = ld(src + (P2 + s) * pl) - P0[s] - P1[s];
+                    for (int s = 0; s < 7; ++s)
+                        M[s] = (int64_t)__ldg(src + (long long)(P2 + s) * a.acc_plane) - P0[s] -
+                               P1[s];
                 }
                 int64_t(&y)[K] = x[bitrev(j)];
 #pragma unroll
@@ -824,40 +800,16 @@ static int try_lane(const InvArgs& a, cudaStream_t stream) {
     return MFFTB_ERR_UNSUPPORTED;
 }
 
-template <int NB, int K, int KARA = 0, bool STAGED = false>
+template <int NB, int K, int KARA = 0>
 static int launch_reg(const InvArgs& a, cudaStream_t stream) {
     const long long total = (long long)a.rows * a.lda;
     const long long blocks = (total + 127) / 128;
-    size_t smem = 0;
-    if constexpr (STAGED) {
-        smem = (size_t)NB * (KARA == 3 ? 27 : (KARA == 2 ? 25 : 21)) * 128 * sizeof(int32_t);
-        static int attr_dev = -1;
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (attr_dev != dev) {
-            if (cudaFuncSetAttribute(inverse_reg_kernel<NB, K, KARA, true>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem) != cudaSuccess)
-                return MFFTB_ERR_CUDA;
-            attr_dev = dev;
-        }
-    }
-    if (blocks > 0)
-        inverse_reg_kernel<NB, K, KARA, STAGED><<<(unsigned)blocks, 128, smem, stream>>>(a);
+    if (blocks > 0) inverse_reg_kernel<NB, K, KARA><<<(unsigned)blocks, 128, 0, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? MFFTB_OK : MFFTB_ERR_CUDA;
 }
 
-// Karatsuba job planes: staged through shared memory (16-byte loads) unless
-// variant 3 asks for the direct loads or the planes are not 16-byte aligned
 template <int NB>
 static int launch_reg_kara(const InvArgs& a, cudaStream_t stream) {
-    const bool staged = a.variant != 3 && a.acc_plane % 4 == 0 && a.lda % 4 == 0 &&
-                        reinterpret_cast<uintptr_t>(a.acc) % 16 == 0;
-    if (staged) {
-        if (a.kara == 3) return launch_reg<NB, 8, 3, true>(a, stream);
-        if (a.kara == 2) return launch_reg<NB, 8, 2, true>(a, stream);
-        return launch_reg<NB, 8, 1, true>(a, stream);
-    }
     if (a.kara == 3) return launch_reg<NB, 8, 3>(a, stream);
     return a.kara == 2 ? launch_reg<NB, 8, 2>(a, stream) : launch_reg<NB, 8, 1>(a, stream);
 }

@@ -87,8 +87,7 @@ struct InvArgs {
     int elems;            // elements per CTA (power of two, <= 32)
     int* err;
     int variant;          // 0 auto, 1 the generic shared-memory kernel only, 2 the lane
-                          // kernel wherever it covers the plan, 3 the register kernel's
-                          // direct loads on Karatsuba plans (no shared-memory staging)
+                          // kernel wherever it covers the plan
     // schoolbook plans: acc holds job planes q = t * nchunk + ch (t < positions)
     // of C_t = sum_u A_u B_(t-u); planes of jobs without terms are not read
     int school;
